@@ -1,0 +1,464 @@
+"""Benchmark of the Laguna MoE block / q8 decode attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload moe_prefill|moe_decode|q8_decode]
+
+Prints ONE JSON line on rank 0. Default workload: one SparseMoeBlock
+forward (router + routed experts + shared expert + combine) on T = 4096 tokens, 128 experts,
+top-8, hidden 2048, intermediate 1024, 4-bit g64 weights, Zipf-skewed routing; metric
+"MoE-layer tokens/s". ``q8_decode`` is config 4 (40 layers of fused 8-bit KV decode attention
+at 82,671 keys, metric HBM GB/s); ``moe_decode`` is config 1 (T = 16).
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and cuda synchronize, timed with
+CUDA events on the launching stream; the max over ranks is reported. Inputs are resident in
+HBM and larger than L2 (453 MB of expert weights; 3.6 GB of KV for q8_decode). ``e2e`` is the
+same metric through the public module API with the step's input copied from pinned host
+memory and the output copied back inside the timed region.
+
+Multi-GPU (torchrun, N > 1): expert-parallel — every rank holds E/N experts and routes its own
+4096 tokens; dispatch and combine are NCCL all-to-alls (weak scaling: tokens per rank fixed).
+``--impl reference`` times the CPU restatement of the reference's path on the host cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    "moe_prefill": dict(T=4096, E=128, k=8, H=2048, I=1024, I_sh=1024, zipf=True, scale=1.0),
+    "moe_decode": dict(T=16, E=128, k=8, H=2048, I=1024, I_sh=1024, zipf=False, scale=2.5),
+    "q8_decode": dict(L=40, n=82671, B=1, Hq=32, Hkv=4),
+}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ----------------------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------------------
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, ws):
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.idx = gpu_index
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(gpu_index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        self.t0 = self.t1 = None
+
+    def mark(self, start):
+        if start:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def result(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        load = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------------------
+
+def timed(step, K, stream, profile_stage=None):
+    """Run K steps between CUDA events; optionally time one library stage per step."""
+    from lagunalab_b200 import _lib
+    L = _lib.lib()
+    pairs = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = L.lg_launch_count()
+    start.record(stream)
+    for _ in range(K):
+        if profile_stage:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            L.lg_profile_stage(profile_stage.encode(), e0.cuda_event, e1.cuda_event)
+            pairs.append((e0, e1))
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    L.lg_profile_stage(None, None, None)
+    launches = L.lg_launch_count() - n0
+    ms = start.elapsed_time(end) / K
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs) if pairs else None
+    return ms, kernel_ms, launches
+
+
+def run_moe(args, wl, ws, rank):
+    from lagunalab_b200 import ep, synth
+    T, E, k, H, I, I_sh = (wl[n] for n in ("T", "E", "k", "H", "I", "I_sh"))
+    if ws > 1:
+        blk, x, fwd = ep.bench_block(T, E, k, H, I, I_sh, wl["zipf"], wl["scale"], ws, rank)
+    else:
+        blk, x = synth.moe_block(T, E, k, H, I, I_sh, seed=0, zipf=wl["zipf"],
+                                 routed_scaling_factor=wl["scale"])
+        fwd = blk
+    stream = torch.cuda.current_stream()
+    out = fwd(x)
+    # routing statistics of the synthetic workload (reported in config)
+    inds, _ = blk.route(x)
+    counts = torch.bincount(inds.reshape(-1).long(), minlength=E)
+    for _ in range(args.warmup):
+        fwd(x)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(torch.cuda.current_device())
+    time.sleep(0.3)
+    clocks.mark(True)
+    ms, gu_ms, launches = timed(lambda: fwd(x), args.steps, stream, "experts_gateup")
+    barrier(ws)
+    # end to end through the module API with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        o = fwd(x_dev)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    e2e_ms, _, _ = timed(e2e_step, args.steps, stream)
+    clocks.mark(False)
+    barrier(ws)
+    ms = max_over_ranks(ms, ws)
+    e2e_ms = max_over_ranks(e2e_ms, ws)
+    gu_ms = max_over_ranks(gu_ms, ws)
+    tokens = T * ws
+    return dict(ms=ms, e2e_ms=e2e_ms, kernel_ms=gu_ms, launches=launches, clocks=clocks,
+                tokens=tokens, counts=counts, h2d=x.numel() * x.element_size(),
+                d2h=out.numel() * out.element_size())
+
+
+def run_q8(args, wl, ws, rank):
+    from lagunalab_b200 import synth
+    from lagunalab_b200.q8_attn import q8_decode_attention
+    L, n, B, Hq, Hkv = (wl[k] for k in ("L", "n", "B", "Hq", "Hkv"))
+    layers = synth.q8_layers(L, n, B, Hq, Hkv, seed=rank)
+    scale = 128 ** -0.5
+    outs = [torch.empty_like(q) for q, _, _ in layers]
+    from lagunalab_b200 import ops
+
+    def step():
+        for (q, kt, vt), o in zip(layers, outs):
+            ops.q8_decode_attention(q, kt, vt, n, scale, out=o)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(torch.cuda.current_device())
+    time.sleep(0.3)
+    clocks.mark(True)
+    ms, k_ms, launches = timed(step, args.steps, stream, "q8_decode")
+    q_host = [q.cpu().pin_memory() for q, _, _ in layers]
+    o_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+
+    def e2e_step():
+        for (q, kt, vt), qh, oh in zip(layers, q_host, o_host):
+            q.copy_(qh, non_blocking=True)
+            oh.copy_(q8_decode_attention(q, kt, vt, n, scale), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms, _, _ = timed(e2e_step, args.steps, stream)
+    clocks.mark(False)
+    ms = max_over_ranks(ms, ws)
+    e2e_ms = max_over_ranks(e2e_ms, ws)
+    return dict(ms=ms, e2e_ms=e2e_ms, kernel_ms=k_ms, launches=launches, clocks=clocks,
+                bytes=synth.q8_bytes_per_layer(n, B, Hkv) * L * ws,
+                h2d=sum(q.numel() * 2 for q, _, _ in layers),
+                d2h=sum(o.numel() * 2 for o in outs))
+
+
+# ----------------------------------------------------------------------------------------
+# CPU baseline (the oracle restatement timed on the host cores; rank 0 only)
+# ----------------------------------------------------------------------------------------
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_moe(wl, steps, warmup, sample_tokens=256):
+    """The oracle's MoE block (pre-dequantized fp32 weights) on a sample of the workload."""
+    from oracle import moe_ref
+    from lagunalab_b200 import synth
+    T, E, k, H, I, I_sh = (wl[n] for n in ("T", "E", "k", "H", "I", "I_sh"))
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if dev == "cuda":
+        blk, x = synth.moe_block(T, E, k, H, I, I_sh, seed=0, zipf=wl["zipf"],
+                                 routed_scaling_factor=wl["scale"])
+        deq = lambda m: moe_ref.dequantize(*(t.cpu() for t in m.mat), 64, 4)
+        wg, wu, wd = (deq(m) for m in (blk.switch_mlp.gate_proj, blk.switch_mlp.up_proj,
+                                       blk.switch_mlp.down_proj))
+        sh = tuple(deq(m) for m in (blk.shared_expert.gate_proj, blk.shared_expert.up_proj,
+                                    blk.shared_expert.down_proj))
+        router, bias = blk.gate.cpu(), blk.e_score_correction_bias.cpu()
+        xs = x[:sample_tokens].cpu()
+        del blk, x
+        torch.cuda.empty_cache()
+    else:  # a CPU-only host: same shapes, weights drawn here
+        g = torch.Generator().manual_seed(0)
+        r = lambda *s: torch.randn(*s, generator=g) * 0.02
+        wg, wu, wd = r(E, I, H), r(E, I, H), r(E, H, I)
+        sh = (r(I_sh, H), r(I_sh, H), r(H, I_sh))
+        router = r(E, H)
+        bias = synth.zipf_bias(E, 0, device="cpu") if wl["zipf"] else torch.zeros(E)
+        xs = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16)
+    nt = cpu_threads()
+    torch.set_num_threads(nt)
+
+    def step():
+        inds, w, *_ = moe_ref.route(xs, router, bias, k)
+        y = moe_ref.switch_glu_deq(xs, inds, wg, wu, wd)
+        return moe_ref.combine(y, w, wl["scale"], moe_ref.mlp_deq(xs, *sh))
+
+    for _ in range(warmup):
+        step()
+    t = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        t.append(time.perf_counter() - t0)
+    sec = statistics.median(t)
+    return dict(value=sample_tokens / sec, unit="tokens/s", cores=nt, kind="port",
+                sample=f"{sample_tokens} of the {T} tokens per step, same weights and routing "
+                       f"(oracle restatement, weights pre-dequantized to fp32)")
+
+
+def cpu_q8(wl, steps, warmup, sample_layers=1):
+    from oracle import attn_ref
+    from lagunalab_b200 import synth
+    n, B, Hq, Hkv = (wl[k] for k in ("n", "B", "Hq", "Hkv"))
+    if torch.cuda.is_available():
+        layers = synth.q8_layers(sample_layers, n, B, Hq, Hkv, seed=0)
+        layers = [(q.cpu(), tuple(t.cpu() for t in kt), tuple(t.cpu() for t in vt))
+                  for q, kt, vt in layers]
+    else:
+        layers = []
+        for _ in range(sample_layers):
+            g = torch.Generator().manual_seed(0)
+            mk = lambda: tuple(
+                torch.from_numpy(a.view("int32") if a.dtype.kind == "u" and a.itemsize == 4
+                                 else a.view("int16")) for a in
+                attn_ref.quantize_rows(torch.randn(B, Hkv, n, 128, generator=g).numpy(), 64, 8))
+            kt, vt = mk(), mk()
+            kt = (kt[0], kt[1].view(torch.bfloat16), kt[2].view(torch.bfloat16))
+            vt = (vt[0], vt[1].view(torch.bfloat16), vt[2].view(torch.bfloat16))
+            layers.append((torch.randn(B, Hq, 1, 128, generator=g).to(torch.bfloat16), kt, vt))
+    nt = cpu_threads()
+    torch.set_num_threads(nt)
+
+    def step():
+        for q, kt, vt in layers:
+            attn_ref.q8_decode_attention_ref(q, kt, vt, n, 128 ** -0.5)
+
+    for _ in range(warmup):
+        step()
+    t = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        t.append(time.perf_counter() - t0)
+    sec = statistics.median(t)
+    gbs = synth.q8_bytes_per_layer(n, B, Hkv) * sample_layers / sec / 1e9
+    return dict(value=gbs, unit="GB/s", cores=nt, kind="port",
+                sample=f"{sample_layers} of the {wl['L']} layers per step at {n} keys "
+                       f"(oracle restatement: dequantize + fp32 softmax)")
+
+
+# ----------------------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="moe_prefill")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    wl = WORKLOADS[args.workload]
+    ws, rank, local = dist_setup()
+
+    if args.impl == "reference":
+        if rank == 0:
+            ref = (cpu_q8(wl, args.steps, args.warmup) if args.workload == "q8_decode"
+                   else cpu_moe(wl, args.steps, args.warmup))
+            metric, unit = metric_unit(args.workload)
+            print(json.dumps({
+                "impl": "reference", "metric": metric, "value": ref["value"], "unit": unit,
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                "config": config(args, wl, ws),
+                "cpu_baseline": {"value": ref["value"], "unit": unit, "cores": ref["cores"],
+                                 "kind": ref["kind"], "sample": ref["sample"]},
+                "e2e": {"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+            }), flush=True)
+        finish(ws)
+        return
+
+    pk, pk_kind = peaks()
+    if args.workload == "q8_decode":
+        r = run_q8(args, wl, ws, rank)
+        value = r["bytes"] / (r["ms"] * 1e-3) / 1e9
+        e2e = r["bytes"] / (r["e2e_ms"] * 1e-3) / 1e9
+        per_launch = r["bytes"] / wl["L"] / ws
+        achieved = per_launch / (r["kernel_ms"] * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "q8_decode_kernel", "achieved": achieved,
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                "traffic": None, "peak_source": pk_kind,
+                "algorithmic": f"{per_launch:.0f} B per launch (n x Hkv x 272 B)"}
+        dtype = "u8"
+    else:
+        r = run_moe(args, wl, ws, rank)
+        value = r["tokens"] / (r["ms"] * 1e-3)
+        e2e = r["tokens"] / (r["e2e_ms"] * 1e-3)
+        from lagunalab_b200 import synth
+        fl = synth.gateup_flops(wl["T"], wl["k"], wl["H"], wl["I"], wl["I_sh"])
+        if ws > 1:
+            fl = None
+        achieved = fl / (r["kernel_ms"] * 1e-3) / 1e12 if fl else None
+        peak = pk["bf16_tflops"]
+        roof = {"bound": "tensor", "kernel": "experts_gateup", "achieved": achieved,
+                "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if achieved else None, "traffic": None,
+                "peak_source": pk_kind,
+                "algorithmic": "2 * 2I * H FLOP per routed pick and shared row"}
+        c = r["counts"]
+        wl = dict(wl, max_count=int(c.max()), min_count=int(c.min()),
+                  distinct=int((c > 0).sum()))
+        dtype = "bf16"
+    metric, unit = metric_unit(args.workload)
+    line = {
+        "metric": metric, "value": value, "unit": unit, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": config(args, wl, ws),
+        "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": r["h2d"],
+                "d2h_bytes_per_step": r["d2h"], "ms_per_step": r["e2e_ms"]},
+        "roofline": roof,
+        "gpu_launches": r["launches"],
+        "clocks": r["clocks"].result(),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else cpu_moe(wl, 5, 1))
+        line["cpu_baseline"] = cb
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    finish(ws)
+
+
+def metric_unit(workload):
+    if workload == "q8_decode":
+        return "q8 decode attention HBM GB/s (40 layers @82,671 ctx)", "GB/s"
+    if workload == "moe_decode":
+        return "MoE-layer tokens/s (T=16)", "tokens/s"
+    return "MoE-layer tokens/s", "tokens/s"
+
+
+def config(args, wl, ws):
+    c = {"workload": args.workload, **{k: v for k, v in wl.items()}}
+    c["l2"] = "inputs larger than L2 (126 MB): weights/KV streamed from HBM each step"
+    c["parallelism"] = f"ep{ws}" if ws > 1 and args.workload != "q8_decode" else \
+        (f"replicas{ws}" if ws > 1 else "single")
+    return c
+
+
+def finish(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,185 @@
+/*
+ * laguna_b200.h — C ABI of the B200 (sm_100a) kernels for the Laguna MoE decoder hot path.
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer unless stated otherwise. The caller allocates every
+ *    input, output and workspace; the library never allocates on these paths and keeps no
+ *    pointer past the call.
+ *  - bf16 tensors are passed as `const void*` / `void*` (IEEE bfloat16 bit patterns).
+ *  - MLX packed layouts: a quantized matrix [rows, cols] is `uint32 weight[rows, cols*bits/32]`
+ *    (32/bits codes per word, low bits first) plus bf16 `scales`/`biases` [rows, cols/group];
+ *    value = scale * code + bias.  A stacked expert tensor adds a leading [E] axis.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are asynchronous,
+ *    stateless and re-entrant per stream.
+ *  - Return value: LG_OK (0) or an LG_ERR_* code; lg_last_error() then holds a message
+ *    (thread-local).  Argument checks happen on the host before any launch.
+ *
+ * Each entry point names the lagunaLab interface (file:line) whose computation it replaces.
+ */
+#ifndef LAGUNA_B200_H
+#define LAGUNA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LG_OK = 0,
+  LG_ERR_INVALID = 1,     /* bad shape / unsupported configuration (reference ValueError / assert) */
+  LG_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  LG_ERR_CUDA = 3,        /* CUDA runtime error (launch, memset) */
+  LG_ERR_WORKSPACE = 4    /* workspace pointer NULL, misaligned or smaller than required */
+};
+
+enum { LG_SCORE_SIGMOID = 0, LG_SCORE_SOFTMAX = 1 };
+
+enum { LG_PATH_AUTO = 0, LG_PATH_GEMV = 1, LG_PATH_TENSOR = 2 };
+
+/* ABI version of this library (bumped on any signature change). */
+int lg_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* lg_last_error(void);
+
+/* Number of kernels this library has launched so far (all threads). */
+long long lg_launch_count(void);
+
+/*
+ * Measurement hook: on this thread, record cudaEvent_t ev_start / ev_end on the launching
+ * stream immediately before / after every launch of the named stage ("router_logits",
+ * "router_topk", "plan", "experts_gateup", "experts_down", "finalize", "q8_decode").
+ * stage == NULL turns it off.  No effect on results.
+ */
+int lg_profile_stage(const char* stage, void* ev_start, void* ev_end);
+
+/*
+ * Router: laguna_mlx/laguna.py:137-145 (SparseMoeBlock.route).
+ *   logits = x @ Wg^T (fp32), scores = sigmoid(logits), sel = scores + e_bias,
+ *   inds = top-k of sel (larger first; equal sel -> lower expert index first),
+ *   w = scores[inds], w /= sum(w) if norm_topk_prob, w -> bf16.
+ * x bf16 [T, H].  Router weight: gate_bits == 0 -> gate_w fp32 [E, H] (scales/biases NULL);
+ * gate_bits == 8 -> MLX 8-bit group-64 (laguna.py:236-238): gate_w uint32 [E, H/4],
+ * scales/biases bf16 [E, H/64]; the quantized matmul's bf16 output is what the sigmoid sees.
+ * e_bias fp32 [E] or NULL (zeros).  Outputs: inds int32 [T, k], weights bf16 [T, k],
+ * logits fp32 [T, E] (optional, NULL to skip), counts int32 [E] (optional histogram of picks).
+ * Limits: E <= 256, 1 <= k <= min(E, 32), H % 64 == 0.
+ */
+int lg_router_topk(const void* x, int T, int H,
+                   const void* gate_w, const void* gate_scales, const void* gate_biases, int gate_bits,
+                   const float* e_bias, int E, int k, int norm_topk_prob, int score_fn,
+                   int32_t* inds, void* weights, float* logits, int32_t* counts,
+                   void* stream);
+
+/*
+ * Routing plan (the token->expert dispatch order used by SwitchGLU's sorted path,
+ * mlx-lm switch_layers, called at laguna_mlx/laguna.py:149): per-expert pick counts and an
+ * expert-contiguous permutation of the T*k picks.  With with_shared != 0 a last group E
+ * holds the T tokens of the shared expert (laguna.py:150), pick ids T*k + t.
+ * counts int32 [E+1], offsets int32 [E+2] (exclusive prefix sums), perm int32 [T*k + T]
+ * (pick ids ordered by expert, then by pick id).  Deterministic.
+ */
+int lg_moe_plan(const int32_t* inds, int T, int k, int E, int with_shared,
+                int32_t* counts, int32_t* offsets, int32_t* perm, void* stream);
+
+/* Workspace bytes for lg_moe_experts / lg_switch_glu / lg_qmlp at these sizes. */
+size_t lg_moe_workspace_bytes(int T, int H, int I, int E, int k, int I_shared);
+
+/*
+ * Routed experts + combine: laguna_mlx/laguna.py:147-150 after route():
+ *   out = (SwitchGLU(x, inds) * w[..., None]).sum(-2) * routed_scaling_factor + shared_expert(x)
+ * SwitchGLU (mlx-lm 0.31.3 switch_layers, laguna.py:134, :149): per pick
+ *   y = down(silu(gate(x)) * up(x)) on the picked expert's MLX-layout quantized weights,
+ *   gate/up: weight [E, I, H*bits/32], scales/biases [E, I, H/group];
+ *   down:    weight [E, H, I*bits/32], scales/biases [E, H, I/group].
+ * Shared expert (laguna.py:114-122, :135): same layout without the E axis, intermediate
+ * I_shared (0 = no shared expert, all sh_* may then be NULL).
+ * x bf16 [T, H]; inds int32 [T, k]; weights bf16 [T, k]; out bf16 [T, H].
+ * path: LG_PATH_AUTO picks the split-K GEMV kernels for few picks and the tcgen05
+ * grouped GEMM otherwise.  bits == 4, group_size == 64 (the MLX default the reference
+ * converts with, scripts/convert.py:14).  H % 128 == 0, I % 128 == 0.
+ */
+int lg_moe_experts(const void* x, int T, int H, int I, int E, int k,
+                   const int32_t* inds, const void* weights, float routed_scaling_factor,
+                   const uint32_t* gate_q, const void* gate_s, const void* gate_b,
+                   const uint32_t* up_q, const void* up_s, const void* up_b,
+                   const uint32_t* down_q, const void* down_s, const void* down_b,
+                   int I_shared,
+                   const uint32_t* sh_gate_q, const void* sh_gate_s, const void* sh_gate_b,
+                   const uint32_t* sh_up_q, const void* sh_up_s, const void* sh_up_b,
+                   const uint32_t* sh_down_q, const void* sh_down_s, const void* sh_down_b,
+                   int group_size, int bits, int path,
+                   void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * SwitchGLU call surface (mlx-lm switch_layers.SwitchGLU.__call__(x, indices), used at
+ * laguna_mlx/laguna.py:149 and streaming.py:95): per-pick, unweighted outputs
+ * y bf16 [T, k, H].  Same weights and limits as lg_moe_experts.
+ */
+int lg_switch_glu(const void* x, int T, int H, int I, int E, int k, const int32_t* inds,
+                  const uint32_t* gate_q, const void* gate_s, const void* gate_b,
+                  const uint32_t* up_q, const void* up_s, const void* up_b,
+                  const uint32_t* down_q, const void* down_s, const void* down_b,
+                  int group_size, int bits, int path,
+                  void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Dense quantized SwiGLU MLP: laguna_mlx/laguna.py:114-122 (MLP.__call__; the shared
+ * expert and the dense layer-0 MLP).  x bf16 [T, H] -> out bf16 [T, H], intermediate I.
+ */
+int lg_qmlp(const void* x, int T, int H, int I,
+            const uint32_t* gate_q, const void* gate_s, const void* gate_b,
+            const uint32_t* up_q, const void* up_s, const void* up_b,
+            const uint32_t* down_q, const void* down_s, const void* down_b,
+            int group_size, int bits, int path,
+            void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Affine quantize rows (the append side of mlx-lm's QuantizedKVCache, laguna_mlx/cache.py:90,
+ * and MLX-layout weight conversion, scripts/convert.py:14) with this library's rule:
+ *   per group: scale = bf16((max - min) / (2^bits - 1)), bias = bf16(min),
+ *   code = clamp(rint((x - bias) / scale), 0, 2^bits - 1)  (0 where scale == 0).
+ * Source rows: x (bf16 if x_is_f32 == 0, else fp32) [B, H, L, D] with element strides
+ * (sb, sh, sl) and unit stride on D.  Destination: packed uint32 [B, H, cap, D*bits/32],
+ * scales/biases bf16 [B, H, cap, D/group], rows [offset, offset + L) written.
+ * bits in {4, 8}, group_size in {32, 64, 128}, D % group_size == 0.
+ */
+int lg_quantize_rows(const void* x, int x_is_f32, int B, int H, int L, int D,
+                     long long sb, long long sh, long long sl,
+                     int bits, int group_size,
+                     uint32_t* dst_q, void* dst_s, void* dst_b, int cap, int offset,
+                     void* stream);
+
+/*
+ * Dequantize rows [0, n) of a packed [B, H, cap, *] buffer to bf16 [B, H, n, D]
+ * (laguna_mlx/cache.py:99-100, the DequantKVCache path for multi-token steps).
+ */
+int lg_dequantize_rows(const uint32_t* q, const void* s, const void* b, int B, int H, int cap,
+                       int n, int D, int bits, int group_size, void* out, void* stream);
+
+/* Workspace bytes for lg_q8_decode_attention. */
+size_t lg_q8_decode_workspace_bytes(int B, int Hq, int Hkv, int n);
+
+/*
+ * Fused single-token attention over an 8-bit group-64 quantized KV cache:
+ * laguna_mlx/q8_attn.py:102-130 (q8_decode_attention) and the Metal kernel at :17-92.
+ *   out = softmax((q * scale) . K[:n]^T) . V[:n]   per query head, GQA group Hq/Hkv.
+ * q bf16 [B, Hq, D]; K/V: packed uint32 [B, Hkv, cap, D/4], scales/biases bf16
+ * [B, Hkv, cap, D/64] (full-capacity buffers; only rows < n are read).  out bf16 [B, Hq, D].
+ * D == 128, Hq % Hkv == 0, Hq/Hkv <= 16, 1 <= n <= cap.
+ * The workspace's first 256 bytes hold per-(batch, kv head) counters that must be zero
+ * before the first call; every completed call leaves them zero again.
+ */
+int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
+                           const uint32_t* k_q, const void* k_s, const void* k_b,
+                           const uint32_t* v_q, const void* v_s, const void* v_b,
+                           int cap, int n, float scale,
+                           void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAGUNA_B200_H */

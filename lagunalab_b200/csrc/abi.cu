@@ -1,0 +1,60 @@
+// Error reporting and version for the C ABI (include/laguna_b200.h).
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace lg {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static std::atomic<long long> g_launches{0};
+static thread_local char g_stage[32] = "";
+static thread_local cudaEvent_t g_ev0 = nullptr, g_ev1 = nullptr;
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void prof_begin(const char* stage, cudaStream_t s) {
+  if (g_ev0 && std::strcmp(stage, g_stage) == 0) cudaEventRecord(g_ev0, s);
+}
+
+void prof_end(const char* stage, cudaStream_t s) {
+  if (g_ev1 && std::strcmp(stage, g_stage) == 0) cudaEventRecord(g_ev1, s);
+}
+
+}  // namespace lg
+
+extern "C" long long lg_launch_count(void) { return lg::g_launches.load(); }
+
+extern "C" int lg_profile_stage(const char* stage, void* ev_start, void* ev_end) {
+  if (!stage || !ev_start || !ev_end) {
+    lg::g_stage[0] = 0;
+    lg::g_ev0 = lg::g_ev1 = nullptr;
+    return LG_OK;
+  }
+  std::snprintf(lg::g_stage, sizeof(lg::g_stage), "%s", stage);
+  lg::g_ev0 = static_cast<cudaEvent_t>(ev_start);
+  lg::g_ev1 = static_cast<cudaEvent_t>(ev_end);
+  return LG_OK;
+}
+
+extern "C" int lg_abi_version(void) { return 1; }
+
+extern "C" const char* lg_last_error(void) { return lg::g_err; }

@@ -1,0 +1,108 @@
+// Shared helpers for the Laguna B200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/laguna_b200.h"
+
+namespace lg {
+
+// Thread-local last-error message for lg_last_error().
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+
+// Kernel launches issued by this library (all threads), read by lg_launch_count().
+void count_launch();
+// Optional CUDA events recorded around one named stage (lg_profile_stage); no-ops otherwise.
+void prof_begin(const char* stage, cudaStream_t s);
+void prof_end(const char* stage, cudaStream_t s);
+
+#define LG_CHECK_ARG(cond, ...)                                  \
+  do {                                                           \
+    if (!(cond)) return ::lg::fail(LG_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+#define LG_CUDA_TRY(expr)                                                          \
+  do {                                                                             \
+    cudaError_t e_ = (expr);                                                       \
+    if (e_ != cudaSuccess)                                                         \
+      return ::lg::fail(LG_ERR_CUDA, "%s: %s (%s:%d)", #expr,                      \
+                        cudaGetErrorString(e_), __FILE__, __LINE__);               \
+  } while (0)
+
+// Launch-error check after a <<<>>> launch (also counts the launch).
+#define LG_LAUNCH_CHECK(name)                                                      \
+  do {                                                                             \
+    cudaError_t e_ = cudaGetLastError();                                           \
+    if (e_ != cudaSuccess)                                                         \
+      return ::lg::fail(LG_ERR_CUDA, "launch %s: %s", name, cudaGetErrorString(e_)); \
+    ::lg::count_launch();                                                          \
+  } while (0)
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Carves consecutive 256-byte aligned regions out of a caller workspace.
+struct Carver {
+  char* base;
+  size_t used = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    used = align_up(used, 256);
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += count * sizeof(T);
+    return p;
+  }
+};
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float bf16_bits_to_f(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+__device__ __forceinline__ float round_bf16(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Exact small-integer -> float for codes in [0, 2^23): 2^23 + c has c in the mantissa.
+__device__ __forceinline__ float code_to_f(uint32_t c) {
+  return __uint_as_float(0x4B000000u | c) - 8388608.0f;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Read-only 128-bit global load that bypasses L1 allocation (weights are streamed once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+}  // namespace lg

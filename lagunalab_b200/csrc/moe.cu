@@ -1,0 +1,228 @@
+// MoE block orchestration: routing plan -> expert products -> combine, behind the C ABI.
+//
+// lg_moe_experts:  laguna_mlx/laguna.py:147-150 after route(); SwitchGLU + weighted sum +
+//                  routed scale + shared expert, accumulated in fp32, one bf16 rounding.
+// lg_switch_glu:   SwitchGLU(x, indices) per-pick outputs (mlx-lm switch_layers surface).
+// lg_qmlp:         dense quantized SwiGLU MLP (laguna.py:114-122): the shared-expert machinery
+//                  with no routed experts.
+#include "moe.cuh"
+
+namespace lg {
+
+int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cudaStream_t s);
+size_t tc_workspace_bytes(int T, int H, int I, int I_sh, int E, int k);
+
+struct MoeWs {
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* active;
+  int32_t* perm;
+  __nv_bfloat16* h;
+  float* out_acc;
+  void* tc;
+};
+
+static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh, MoeWs* w) {
+  Carver c(base);
+  const int P = T * k;
+  const int Imax = I > I_sh ? I : I_sh;
+  MoeWs t;
+  t.counts = c.take<int32_t>(E + 2);
+  t.offsets = c.take<int32_t>(E + 2);
+  t.active = c.take<int32_t>(E + 3);
+  t.perm = c.take<int32_t>((size_t)P + T);
+  t.h = c.take<__nv_bfloat16>(((size_t)P + T) * Imax);
+  t.out_acc = c.take<float>((size_t)T * H);
+  t.tc = c.take<char>(tc_workspace_bytes(T, H, I, I_sh, E, k));
+  if (w) *w = t;
+  return align_up(c.used, 256);
+}
+
+__global__ void finalize_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
+                                     size_t n4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(acc)[i];
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&lo);
+    o.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(out)[i] = o;
+  }
+}
+
+static int check_qmat(const void* q, const void* s, const void* b, const char* name) {
+  if (!q || !s || !b) return fail(LG_ERR_INVALID, "%s: NULL weight/scales/biases", name);
+  if (!aligned(q, 16) || !aligned(s, 2) || !aligned(b, 2))
+    return fail(LG_ERR_INVALID, "%s: weight must be 16-byte aligned", name);
+  return LG_OK;
+}
+
+// Common driver. mode: 0 = combine into bf16 out, 1 = per-pick SwitchGLU outputs.
+static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32_t* inds,
+                   const void* weights, float routed_scale, const uint32_t* const* q,
+                   const void* const* sc, const void* const* bi, int I_sh,
+                   const uint32_t* const* sq, const void* const* ss, const void* const* sb,
+                   int group_size, int bits, int path, void* out, void* workspace,
+                   size_t workspace_bytes, int mode, cudaStream_t st) {
+  LG_CHECK_ARG(bits == 4 && group_size == 64,
+               "experts: only 4-bit group-64 weights are supported (got bits=%d group=%d)", bits,
+               group_size);
+  LG_CHECK_ARG(T >= 0 && H > 0 && E >= 0 && E <= 256 && k >= 0 && I_sh >= 0,
+               "experts: bad sizes T=%d H=%d E=%d k=%d", T, H, E, k);
+  LG_CHECK_ARG(E == 0 || (k >= 1 && k <= E && I > 0), "experts: k=%d I=%d invalid for E=%d", k,
+               I, E);
+  LG_CHECK_ARG(H % 64 == 0 && (E == 0 || I % 64 == 0) && I_sh % 64 == 0,
+               "experts: hidden %d and intermediate %d/%d must be multiples of 64", H, I, I_sh);
+  LG_CHECK_ARG(path >= LG_PATH_AUTO && path <= LG_PATH_TENSOR, "experts: path %d", path);
+  LG_CHECK_ARG(x && out && aligned(x, 16) && aligned(out, 16),
+               "experts: x/out must be non-NULL and 16-byte aligned");
+  if (E > 0) {
+    LG_CHECK_ARG(inds != nullptr, "experts: NULL inds");
+    LG_CHECK_ARG(mode == 1 || weights != nullptr, "experts: NULL routing weights");
+    for (int j = 0; j < 3; ++j) {
+      int rc = check_qmat(q[j], sc[j], bi[j], "experts");
+      if (rc) return rc;
+    }
+  }
+  if (I_sh > 0)
+    for (int j = 0; j < 3; ++j) {
+      int rc = check_qmat(sq[j], ss[j], sb[j], "shared expert");
+      if (rc) return rc;
+    }
+  const int Ie = E > 0 ? I : 0;
+  const size_t need = carve_moe(nullptr, T, H, Ie, E, k, I_sh, nullptr);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(LG_ERR_WORKSPACE, "experts: workspace %zu bytes at %p, need %zu (256-aligned)",
+                workspace_bytes, workspace, need);
+  if (T == 0) return LG_OK;
+  MoeWs w;
+  carve_moe(workspace, T, H, Ie, E, k, I_sh, &w);
+  const int P = T * (E > 0 ? k : 0);
+  const bool with_sh = I_sh > 0;
+  if (mode == 0) LG_CUDA_TRY(cudaMemsetAsync(w.out_acc, 0, sizeof(float) * (size_t)T * H, st));
+  if (mode == 1) LG_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(uint16_t) * (size_t)P * H, st));
+  int rc = launch_plan(inds, T, E > 0 ? k : 0, E, with_sh ? 1 : 0, w.counts, w.offsets, w.perm,
+                       w.active, st);
+  if (rc) return rc;
+  GemvArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.T = T;
+  a.H = H;
+  a.I = Ie;
+  a.I_sh = I_sh;
+  a.E = E;
+  a.k = E > 0 ? k : 0;
+  a.P = P;
+  a.offsets = w.offsets;
+  a.perm = w.perm;
+  a.active = w.active;
+  a.g_q = q[0];
+  a.u_q = q[1];
+  a.d_q = q[2];
+  a.g_s = static_cast<const __nv_bfloat16*>(sc[0]);
+  a.u_s = static_cast<const __nv_bfloat16*>(sc[1]);
+  a.d_s = static_cast<const __nv_bfloat16*>(sc[2]);
+  a.g_b = static_cast<const __nv_bfloat16*>(bi[0]);
+  a.u_b = static_cast<const __nv_bfloat16*>(bi[1]);
+  a.d_b = static_cast<const __nv_bfloat16*>(bi[2]);
+  a.sg_q = sq[0];
+  a.su_q = sq[1];
+  a.sd_q = sq[2];
+  a.sg_s = static_cast<const __nv_bfloat16*>(ss[0]);
+  a.su_s = static_cast<const __nv_bfloat16*>(ss[1]);
+  a.sd_s = static_cast<const __nv_bfloat16*>(ss[2]);
+  a.sg_b = static_cast<const __nv_bfloat16*>(sb[0]);
+  a.su_b = static_cast<const __nv_bfloat16*>(sb[1]);
+  a.sd_b = static_cast<const __nv_bfloat16*>(sb[2]);
+  a.h = w.h;
+  a.h_stride = Ie > I_sh ? Ie : I_sh;
+  a.w = static_cast<const __nv_bfloat16*>(weights);
+  a.routed_scale = routed_scale;
+  a.out_acc = w.out_acc;
+  a.ypick = static_cast<__nv_bfloat16*>(out);
+  int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
+  bool use_tc = (path == LG_PATH_TENSOR) || (path == LG_PATH_AUTO && P + (with_sh ? T : 0) > 512);
+  if (use_tc)
+    rc = launch_tc(a, max_groups, mode == 0, w.tc, st);
+  else
+    rc = launch_gemv(a, max_groups, mode == 0, st);
+  if (rc) return rc;
+  if (mode == 0) {
+    size_t n4 = (size_t)T * H / 4;
+    int blocks = (int)((n4 + 255) / 256);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    prof_begin("finalize", st);
+    finalize_bf16_kernel<<<blocks, 256, 0, st>>>(w.out_acc, static_cast<__nv_bfloat16*>(out), n4);
+    prof_end("finalize", st);
+    LG_LAUNCH_CHECK("finalize_bf16");
+  }
+  return LG_OK;
+}
+
+}  // namespace lg
+
+using namespace lg;
+
+extern "C" size_t lg_moe_workspace_bytes(int T, int H, int I, int E, int k, int I_shared) {
+  if (T < 0 || H <= 0 || E < 0 || k < 0 || I < 0 || I_shared < 0) return 0;
+  return carve_moe(nullptr, T, H, E > 0 ? I : 0, E, k, I_shared, nullptr);
+}
+
+extern "C" int lg_moe_experts(const void* x, int T, int H, int I, int E, int k,
+                              const int32_t* inds, const void* weights,
+                              float routed_scaling_factor, const uint32_t* gate_q,
+                              const void* gate_s, const void* gate_b, const uint32_t* up_q,
+                              const void* up_s, const void* up_b, const uint32_t* down_q,
+                              const void* down_s, const void* down_b, int I_shared,
+                              const uint32_t* sh_gate_q, const void* sh_gate_s,
+                              const void* sh_gate_b, const uint32_t* sh_up_q,
+                              const void* sh_up_s, const void* sh_up_b,
+                              const uint32_t* sh_down_q, const void* sh_down_s,
+                              const void* sh_down_b, int group_size, int bits, int path,
+                              void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  const uint32_t* q[3] = {gate_q, up_q, down_q};
+  const void* s[3] = {gate_s, up_s, down_s};
+  const void* b[3] = {gate_b, up_b, down_b};
+  const uint32_t* sq[3] = {sh_gate_q, sh_up_q, sh_down_q};
+  const void* ss[3] = {sh_gate_s, sh_up_s, sh_down_s};
+  const void* sb[3] = {sh_gate_b, sh_up_b, sh_down_b};
+  LG_CHECK_ARG(E >= 1, "lg_moe_experts: E=%d must be >= 1 (use lg_qmlp for a dense MLP)", E);
+  return moe_run(x, T, H, I, E, k, inds, weights, routed_scaling_factor, q, s, b, I_shared, sq,
+                 ss, sb, group_size, bits, path, out, workspace, workspace_bytes, 0,
+                 static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lg_switch_glu(const void* x, int T, int H, int I, int E, int k,
+                             const int32_t* inds, const uint32_t* gate_q, const void* gate_s,
+                             const void* gate_b, const uint32_t* up_q, const void* up_s,
+                             const void* up_b, const uint32_t* down_q, const void* down_s,
+                             const void* down_b, int group_size, int bits, int path, void* y,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  const uint32_t* q[3] = {gate_q, up_q, down_q};
+  const void* s[3] = {gate_s, up_s, down_s};
+  const void* b[3] = {gate_b, up_b, down_b};
+  const uint32_t* nq[3] = {nullptr, nullptr, nullptr};
+  const void* nv[3] = {nullptr, nullptr, nullptr};
+  LG_CHECK_ARG(E >= 1, "lg_switch_glu: E=%d must be >= 1", E);
+  return moe_run(x, T, H, I, E, k, inds, nullptr, 1.0f, q, s, b, 0, nq, nv, nv, group_size,
+                 bits, path, y, workspace, workspace_bytes, 1, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lg_qmlp(const void* x, int T, int H, int I, const uint32_t* gate_q,
+                       const void* gate_s, const void* gate_b, const uint32_t* up_q,
+                       const void* up_s, const void* up_b, const uint32_t* down_q,
+                       const void* down_s, const void* down_b, int group_size, int bits,
+                       int path, void* out, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  const uint32_t* sq[3] = {gate_q, up_q, down_q};
+  const void* ss[3] = {gate_s, up_s, down_s};
+  const void* sb[3] = {gate_b, up_b, down_b};
+  const uint32_t* nq[3] = {nullptr, nullptr, nullptr};
+  const void* nv[3] = {nullptr, nullptr, nullptr};
+  LG_CHECK_ARG(I > 0, "lg_qmlp: intermediate %d must be > 0", I);
+  return moe_run(x, T, H, 0, 0, 0, nullptr, nullptr, 1.0f, nq, nv, nv, I, sq, ss, sb,
+                 group_size, bits, path, out, workspace, workspace_bytes, 0,
+                 static_cast<cudaStream_t>(stream));
+}

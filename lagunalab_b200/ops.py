@@ -1,0 +1,254 @@
+"""Torch-facing wrappers of the C-ABI kernels (device tensors in, device tensors out).
+
+Every op runs on the CUDA stream that is current for the input's device and raises if the
+library is missing or an input is not a contiguous CUDA tensor; nothing runs on the CPU.
+Packed MLX words are carried as ``torch.int32`` tensors holding the uint32 bit patterns
+(``torch.uint32`` has too few kernels to be practical); ``torch.uint32`` inputs are viewed
+as int32.
+"""
+import torch
+
+from . import _lib
+
+_WS = {}
+
+
+def _dev(t):
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise ValueError("lagunalab_b200 ops take CUDA tensors (there is no CPU path)")
+    return t.device
+
+
+def _c(t, dtype=None):
+    """Contiguous CUDA tensor (optionally checked dtype); uint32 is viewed as int32."""
+    if t is None:
+        return None
+    _dev(t)
+    if t.dtype == torch.uint32:
+        t = t.view(torch.int32)
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"expected {dtype}, got {t.dtype}")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(device, kind, nbytes, zero=False):
+    """A cached device workspace per (device, kind), grown on demand (256-byte aligned).
+
+    ``zero=True`` workspaces are zero-filled when (re)allocated; the kernels that use them
+    leave their counters at zero. Calls on one device that share a kind must not overlap in
+    time on different streams."""
+    key = (device.index, kind)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        n = max(int(nbytes), 256)
+        buf = torch.zeros(n, dtype=torch.uint8, device=device) if zero else \
+            torch.empty(n, dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def _qm(mat):
+    """(weight, scales, biases) -> contiguous tuple."""
+    q, s, b = mat
+    return _c(q, torch.int32), _c(s, torch.bfloat16), _c(b, torch.bfloat16)
+
+
+# ---------------------------------------------------------------------------------------
+# Router (laguna_mlx/laguna.py:137-145)
+# ---------------------------------------------------------------------------------------
+
+def router_topk(x, gate, e_bias, k, norm_topk_prob=True, score_fn="sigmoid", counts=False):
+    """Fused router. ``gate`` is an fp32 [E, H] weight or an MLX 8-bit tuple
+    (weight, scales, biases). Returns (inds int32 [T, k], w bf16 [T, k], logits fp32 [T, E]
+    [, counts int32 [E]])."""
+    x = _c(x, torch.bfloat16)
+    dev = x.device
+    T, H = x.shape
+    if isinstance(gate, tuple):
+        gw, gs, gb = _qm(gate)
+        bits = 8
+    else:
+        gw, gs, gb = _c(gate, torch.float32), None, None
+        bits = 0
+    E = gw.shape[0]
+    eb = _c(e_bias.to(torch.float32)) if e_bias is not None else None
+    inds = torch.empty(T, k, dtype=torch.int32, device=dev)
+    w = torch.empty(T, k, dtype=torch.bfloat16, device=dev)
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+    cnt = torch.empty(E, dtype=torch.int32, device=dev) if counts else None
+    sf = _lib.LG_SCORE_SOFTMAX if score_fn == "softmax" else _lib.LG_SCORE_SIGMOID
+    _lib.call("lg_router_topk", _p(x), T, H, _p(gw), _p(gs), _p(gb), bits, _p(eb), E, k,
+              int(bool(norm_topk_prob)), sf, _p(inds), _p(w), _p(logits), _p(cnt), _stream(dev))
+    return (inds, w, logits, cnt) if counts else (inds, w, logits)
+
+
+def moe_plan(inds, E, with_shared=True):
+    """Expert histogram and expert-contiguous permutation of the picks (deterministic)."""
+    inds = _c(inds, torch.int32)
+    dev = inds.device
+    T, k = inds.shape
+    counts = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 2, dtype=torch.int32, device=dev)
+    perm = torch.empty(T * k + T, dtype=torch.int32, device=dev)
+    _lib.call("lg_moe_plan", _p(inds), T, k, E, int(with_shared), _p(counts), _p(offsets),
+              _p(perm), _stream(dev))
+    return counts, offsets, perm
+
+
+# ---------------------------------------------------------------------------------------
+# Experts (SwitchGLU + combine, laguna_mlx/laguna.py:147-150; MLP, laguna.py:114-122)
+# ---------------------------------------------------------------------------------------
+
+_PATHS = {"auto": _lib.LG_PATH_AUTO, "gemv": _lib.LG_PATH_GEMV, "tensor": _lib.LG_PATH_TENSOR}
+
+
+def moe_experts(x, inds, w, routed_scaling_factor, experts, shared=None, path="auto",
+                group_size=64, bits=4, out=None):
+    """(SwitchGLU(x, inds) * w).sum(-2) * routed_scaling_factor + shared(x) -> bf16 [T, H]."""
+    x = _c(x, torch.bfloat16)
+    dev = x.device
+    T, H = x.shape
+    inds = _c(inds, torch.int32)
+    w = _c(w, torch.bfloat16)
+    k = inds.shape[-1]
+    g, u, d = (_qm(m) for m in experts)
+    E, I = g[0].shape[0], g[0].shape[1]
+    if shared is not None:
+        sg, su, sd = (_qm(m) for m in shared)
+        Ish = sg[0].shape[0]
+    else:
+        sg = su = sd = (None, None, None)
+        Ish = 0
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    nb = _lib.lib().lg_moe_workspace_bytes(T, H, I, E, k, Ish)
+    ws = workspace(dev, "moe", nb)
+    _lib.call("lg_moe_experts", _p(x), T, H, I, E, k, _p(inds), _p(w),
+              float(routed_scaling_factor),
+              *map(_p, g), *map(_p, u), *map(_p, d),
+              Ish, *map(_p, sg), *map(_p, su), *map(_p, sd),
+              group_size, bits, _PATHS[path], _p(out), _p(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def switch_glu(x, inds, experts, path="auto", group_size=64, bits=4):
+    """SwitchGLU(x, indices): per-pick outputs bf16 [T, k, H] (unweighted)."""
+    x = _c(x, torch.bfloat16)
+    dev = x.device
+    T, H = x.shape
+    inds = _c(inds, torch.int32)
+    k = inds.shape[-1]
+    g, u, d = (_qm(m) for m in experts)
+    E, I = g[0].shape[0], g[0].shape[1]
+    y = torch.empty(T, k, H, dtype=torch.bfloat16, device=dev)
+    nb = _lib.lib().lg_moe_workspace_bytes(T, H, I, E, k, 0)
+    ws = workspace(dev, "moe", nb)
+    _lib.call("lg_switch_glu", _p(x), T, H, I, E, k, _p(inds),
+              *map(_p, g), *map(_p, u), *map(_p, d),
+              group_size, bits, _PATHS[path], _p(y), _p(ws), ws.numel(), _stream(dev))
+    return y
+
+
+def qmlp(x, mats, path="auto", group_size=64, bits=4):
+    """Dense quantized SwiGLU MLP: down(silu(gate x) * up x) -> bf16 [T, H]."""
+    x = _c(x, torch.bfloat16)
+    dev = x.device
+    T, H = x.shape
+    g, u, d = (_qm(m) for m in mats)
+    I = g[0].shape[0]
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    nb = _lib.lib().lg_moe_workspace_bytes(T, H, 0, 0, 0, I)
+    ws = workspace(dev, "moe", nb)
+    _lib.call("lg_qmlp", _p(x), T, H, I, *map(_p, g), *map(_p, u), *map(_p, d),
+              group_size, bits, _PATHS[path], _p(out), _p(ws), ws.numel(), _stream(dev))
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+# Quantization (MLX affine layout) and the q8 decode attention
+# ---------------------------------------------------------------------------------------
+
+def quantize(w, group_size=64, bits=4):
+    """MLX-layout affine quantization of the last axis: (int32 words, bf16 scales, bf16 biases)."""
+    w = _c(w)
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.to(torch.float32)
+    dev = w.device
+    D = w.shape[-1]
+    rows = w.numel() // D
+    q = torch.empty(*w.shape[:-1], D * bits // 32, dtype=torch.int32, device=dev)
+    s = torch.empty(*w.shape[:-1], D // group_size, dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(s)
+    _lib.call("lg_quantize_rows", _p(w), int(w.dtype == torch.float32), 1, 1, rows, D,
+              0, 0, D, bits, group_size, _p(q), _p(s), _p(b), rows, 0, _stream(dev))
+    return q, s, b
+
+
+def quantize_into(x, dst, offset, group_size=64, bits=8):
+    """Quantize x [B, H, L, D] (bf16, any strides with unit last stride) into rows
+    [offset, offset + L) of packed buffers dst = (q [B,H,cap,*], s, b)."""
+    _dev(x)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    B, H, L, D = x.shape
+    q, s, b = dst
+    cap = q.shape[2]
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        x = x.to(torch.bfloat16)
+    _lib.call("lg_quantize_rows", _p(x), int(x.dtype == torch.float32), B, H, L, D,
+              x.stride(0), x.stride(1), x.stride(2), bits, group_size,
+              _p(q), _p(s), _p(b), cap, offset, _stream(x.device))
+
+
+def dequantize_rows(dst, n, group_size=64, bits=8):
+    """Rows [0, n) of packed [B, H, cap, *] buffers -> bf16 [B, H, n, D]."""
+    q, s, b = dst
+    _dev(q)
+    B, H, cap, W = q.shape
+    D = W * 32 // bits
+    out = torch.empty(B, H, n, D, dtype=torch.bfloat16, device=q.device)
+    _lib.call("lg_dequantize_rows", _p(q), _p(s), _p(b), B, H, cap, n, D, bits, group_size,
+              _p(out), _stream(q.device))
+    return out
+
+
+def dequantize(q, s, b, group_size=64, bits=4):
+    """MLX-layout words -> bf16 matrix (for checks and model conversion)."""
+    q = _c(q, torch.int32)
+    rows = q.numel() // q.shape[-1]
+    D = q.shape[-1] * 32 // bits
+    out = dequantize_rows((q.reshape(1, 1, rows, -1), _c(s).reshape(1, 1, rows, -1),
+                           _c(b).reshape(1, 1, rows, -1)), rows, group_size, bits)
+    return out.reshape(*q.shape[:-1], D)
+
+
+def q8_decode_attention(q, keys, values, n, scale, out=None):
+    """Single-token attention over 8-bit group-64 packed K/V (first n rows valid).
+    q [B, Hq, 1, D] bf16; keys/values = (uint32 words [B, Hkv, cap, D/4], bf16 scales,
+    bf16 biases [B, Hkv, cap, D/64]). Returns [B, Hq, 1, D] bf16."""
+    B, Hq, L, D = q.shape
+    if L != 1:
+        raise ValueError("decode only: q must have one token")
+    q = _c(q, torch.bfloat16)
+    kq, ks, kb = (_c(t) for t in keys)
+    vq, vs, vb = (_c(t) for t in values)
+    Hkv, cap = kq.shape[1], kq.shape[2]
+    if kq.shape[-1] != D // 4:
+        raise ValueError("8-bit, group_size 64 only")
+    dev = q.device
+    if out is None:
+        out = torch.empty(B, Hq, 1, D, dtype=torch.bfloat16, device=dev)
+    nb = _lib.lib().lg_q8_decode_workspace_bytes(B, Hq, Hkv, int(n))
+    ws = workspace(dev, "q8", nb, zero=True)
+    _lib.call("lg_q8_decode_attention", _p(q), B, Hq, Hkv, D, _p(kq), _p(ks), _p(kb),
+              _p(vq), _p(vs), _p(vb), cap, int(n), float(scale), _p(out), _p(ws), ws.numel(),
+              _stream(dev))
+    return out
