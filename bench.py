@@ -150,6 +150,8 @@ def timed(step, K, stream, profile_stage=None):
     for _ in range(K):
         if profile_stage:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)  # torch creates the event on first record; the library
+            e1.record(stream)  # then re-records both around the profiled stage
             L.lg_profile_stage(profile_stage.encode(), e0.cuda_event, e1.cuda_event)
             pairs.append((e0, e1))
         step()
@@ -158,7 +160,7 @@ def timed(step, K, stream, profile_stage=None):
     L.lg_profile_stage(None, None, None)
     launches = L.lg_launch_count() - n0
     ms = start.elapsed_time(end) / K
-    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs) if pairs else None
+    kernel_ms = statistics.mean(_lib.event_elapsed_ms(a, b) for a, b in pairs) if pairs else None
     return ms, kernel_ms, launches
 
 

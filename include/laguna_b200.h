@@ -55,6 +55,9 @@ long long lg_launch_count(void);
  */
 int lg_profile_stage(const char* stage, void* ev_start, void* ev_end);
 
+/* Milliseconds between two recorded cudaEvent_t (waits for ev_end). */
+int lg_event_elapsed_ms(void* ev_start, void* ev_end, float* ms);
+
 /*
  * Router: laguna_mlx/laguna.py:137-145 (SparseMoeBlock.route).
  *   logits = x @ Wg^T (fp32), scores = sigmoid(logits), sel = scores + e_bias,

@@ -21,6 +21,7 @@ SIGNATURES = {
     "lg_last_error": (ctypes.c_char_p, []),
     "lg_launch_count": (c_longlong, []),
     "lg_profile_stage": (c_int, [ctypes.c_char_p, P, P]),
+    "lg_event_elapsed_ms": (c_int, [P, P, ctypes.POINTER(c_float)]),
     "lg_router_topk": (c_int, [P, I, I, P, P, P, I, P, I, I, I, I, P, P, P, P, P]),
     "lg_moe_plan": (c_int, [P, I, I, I, I, P, P, P, P]),
     "lg_moe_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
@@ -66,6 +67,13 @@ def lib():
             f.argtypes = args
         _lib = h
     return _lib
+
+
+def event_elapsed_ms(ev_start, ev_end):
+    """Elapsed ms between two torch.cuda.Event objects recorded by the library."""
+    ms = c_float(0.0)
+    call("lg_event_elapsed_ms", ev_start.cuda_event, ev_end.cuda_event, ctypes.byref(ms))
+    return ms.value
 
 
 def call(name, *args):

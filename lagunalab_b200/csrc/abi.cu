@@ -55,6 +55,15 @@ extern "C" int lg_profile_stage(const char* stage, void* ev_start, void* ev_end)
   return LG_OK;
 }
 
+extern "C" int lg_event_elapsed_ms(void* ev_start, void* ev_end, float* ms) {
+  if (!ev_start || !ev_end || !ms) return lg::fail(LG_ERR_INVALID, "event_elapsed: NULL");
+  cudaError_t e = cudaEventSynchronize(static_cast<cudaEvent_t>(ev_end));
+  if (e == cudaSuccess)
+    e = cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(ev_start), static_cast<cudaEvent_t>(ev_end));
+  if (e != cudaSuccess) return lg::fail(LG_ERR_CUDA, "event_elapsed: %s", cudaGetErrorString(e));
+  return LG_OK;
+}
+
 extern "C" int lg_abi_version(void) { return 1; }
 
 extern "C" const char* lg_last_error(void) { return lg::g_err; }

@@ -76,6 +76,7 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   LG_CHECK_ARG(H % 64 == 0 && (E == 0 || I % 64 == 0) && I_sh % 64 == 0,
                "experts: hidden %d and intermediate %d/%d must be multiples of 64", H, I, I_sh);
   LG_CHECK_ARG(path >= LG_PATH_AUTO && path <= LG_PATH_TENSOR, "experts: path %d", path);
+  if (T == 0) return LG_OK;
   LG_CHECK_ARG(x && out && aligned(x, 16) && aligned(out, 16),
                "experts: x/out must be non-NULL and 16-byte aligned");
   if (E > 0) {

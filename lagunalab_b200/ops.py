@@ -129,6 +129,8 @@ def moe_experts(x, inds, w, routed_scaling_factor, experts, shared=None, path="a
         Ish = 0
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if T == 0:
+        return out
     nb = _lib.lib().lg_moe_workspace_bytes(T, H, I, E, k, Ish)
     ws = workspace(dev, "moe", nb)
     _lib.call("lg_moe_experts", _p(x), T, H, I, E, k, _p(inds), _p(w),
