@@ -100,9 +100,10 @@ size_t lg_moe_workspace_bytes(int T, int H, int I, int E, int k, int I_shared);
  * Shared expert (laguna.py:114-122, :135): same layout without the E axis, intermediate
  * I_shared (0 = no shared expert, all sh_* may then be NULL).
  * x bf16 [T, H]; inds int32 [T, k]; weights bf16 [T, k]; out bf16 [T, H].
- * path: LG_PATH_AUTO picks the split-K GEMV kernels for few picks and the tcgen05
- * grouped GEMM otherwise.  bits == 4, group_size == 64 (the MLX default the reference
- * converts with, scripts/convert.py:14).  H % 128 == 0, I % 128 == 0.
+ * path: LG_PATH_AUTO picks the split-K GEMV kernels for few picks (<= 512 rows including the
+ * shared expert's) and the tcgen05 grouped GEMM otherwise; LG_PATH_TENSOR forces the latter
+ * (needs H % 256 == 0, I % 128 == 0, I_shared % 128 == 0).  bits == 4, group_size == 64 (the
+ * MLX default the reference converts with, scripts/convert.py:14); H, I, I_shared % 64 == 0.
  */
 int lg_moe_experts(const void* x, int T, int H, int I, int E, int k,
                    const int32_t* inds, const void* weights, float routed_scaling_factor,
@@ -115,6 +116,14 @@ int lg_moe_experts(const void* x, int T, int H, int I, int E, int k,
                    const uint32_t* sh_down_q, const void* sh_down_s, const void* sh_down_b,
                    int group_size, int bits, int path,
                    void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Status word of the last tensor-core expert launch that used this workspace (same sizes as
+ * that call): 0 = ok, otherwise the code of the pipeline role whose bounded wait expired (the
+ * kernel then stopped instead of hanging).  Synchronous (copies 4 bytes to the host).
+ */
+int lg_moe_status(const void* workspace, int T, int H, int I, int E, int k, int I_shared,
+                  int* status);
 
 /*
  * SwitchGLU call surface (mlx-lm switch_layers.SwitchGLU.__call__(x, indices), used at

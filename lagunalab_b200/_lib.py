@@ -25,6 +25,7 @@ SIGNATURES = {
     "lg_router_topk": (c_int, [P, I, I, P, P, P, I, P, I, I, I, I, P, P, P, P, P]),
     "lg_moe_plan": (c_int, [P, I, I, I, I, P, P, P, P]),
     "lg_moe_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
+    "lg_moe_status": (c_int, [P, I, I, I, I, I, I, ctypes.POINTER(c_int)]),
     "lg_moe_experts": (c_int, [P, I, I, I, I, I, P, P, c_float,
                                P, P, P, P, P, P, P, P, P,
                                I, P, P, P, P, P, P, P, P, P,

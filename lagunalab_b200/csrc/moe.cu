@@ -11,6 +11,8 @@ namespace lg {
 
 int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cudaStream_t s);
 size_t tc_workspace_bytes(int T, int H, int I, int I_sh, int E, int k);
+bool tc_supported(int H, int I, int I_sh, int E);
+int tc_status(const void* tc_ws, int T, int H, int I, int I_sh, int E, int k, int* status);
 
 struct MoeWs {
   int32_t* counts;
@@ -144,7 +146,11 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   a.out_acc = w.out_acc;
   a.ypick = static_cast<__nv_bfloat16*>(out);
   int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
-  bool use_tc = (path == LG_PATH_TENSOR) || (path == LG_PATH_AUTO && P + (with_sh ? T : 0) > 512);
+  // Tensor-core grouped GEMM when there are enough rows per expert to fill 128-row tiles;
+  // the split-K GEMV otherwise (decode), or when the shapes do not tile.
+  const bool tiles_ok = tc_supported(H, Ie, I_sh, E);
+  const bool use_tc = (path == LG_PATH_TENSOR) ||
+                      (path == LG_PATH_AUTO && tiles_ok && P + (with_sh ? T : 0) > 512);
   if (use_tc)
     rc = launch_tc(a, max_groups, mode == 0, w.tc, st);
   else
@@ -165,6 +171,14 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
 }  // namespace lg
 
 using namespace lg;
+
+extern "C" int lg_moe_status(const void* workspace, int T, int H, int I, int E, int k,
+                             int I_shared, int* status) {
+  LG_CHECK_ARG(workspace && status, "moe_status: NULL pointer");
+  MoeWs w;
+  carve_moe(const_cast<void*>(workspace), T, H, E > 0 ? I : 0, E, k, I_shared, &w);
+  return tc_status(w.tc, T, H, E > 0 ? I : 0, I_shared, E, k, status);
+}
 
 extern "C" size_t lg_moe_workspace_bytes(int T, int H, int I, int E, int k, int I_shared) {
   if (T < 0 || H <= 0 || E < 0 || k < 0 || I < 0 || I_shared < 0) return 0;

@@ -141,6 +141,18 @@ def moe_experts(x, inds, w, routed_scaling_factor, experts, shared=None, path="a
     return out
 
 
+def moe_status(device, T, H, I, E, k, I_sh):
+    """Status word of the last tensor-core expert launch on ``device`` with these sizes
+    (0 = ok; nonzero = a bounded pipeline wait expired). Synchronises."""
+    import ctypes
+    ws = _WS.get((torch.device(device).index, "moe"))
+    if ws is None:
+        return 0
+    st = ctypes.c_int(0)
+    _lib.call("lg_moe_status", _p(ws), T, H, I, E, k, I_sh, ctypes.byref(st))
+    return st.value
+
+
 def switch_glu(x, inds, experts, path="auto", group_size=64, bits=4):
     """SwitchGLU(x, indices): per-pick outputs bf16 [T, k, H] (unweighted)."""
     x = _c(x, torch.bfloat16)

@@ -29,6 +29,9 @@ CASES = [
     (10, 8, 2, 128, 64, 64, 2.5, "gemv"),          # tiny
     (77, 16, 4, 256, 128, 128, 1.0, "gemv"),       # ragged token counts per expert
     (200, 16, 4, 256, 128, 192, 1.0, "auto"),      # shared intermediate != routed
+    (300, 16, 4, 256, 128, 128, 1.0, "tensor"),    # tcgen05 grouped GEMM, small
+    (64, 8, 2, 512, 256, 384, 2.5, "tensor"),      # shared I != routed I on the tensor path
+    (1024, 128, 8, 2048, 1024, 1024, 1.0, "tensor"),  # config-2 shapes, 1024 tokens
 ]
 
 
@@ -43,16 +46,20 @@ def test_moe_block_matches_oracle(T, E, k, H, I, Ish, scale, path):
     sh = moe_ref.mlp(x, *(to_cpu(m) for m in shared))
     ref = moe_ref.combine(y, wts.cpu(), scale, sh)
     assert out.dtype == torch.bfloat16 and out.shape == (T, H)
+    if path == "tensor":
+        assert ops.moe_status(x.cuda().device, T, H, I, E, k, Ish) == 0
     assert rel_err(out, ref) <= REL_TOL, rel_err(out, ref)
     assert cos(out, ref) >= COS_TOL
 
 
-@pytest.mark.parametrize("T,E,k,H,I", [(16, 128, 8, 2048, 1024), (9, 8, 2, 128, 64)])
-def test_switch_glu_per_pick_matches_oracle(T, E, k, H, I):
+@pytest.mark.parametrize("T,E,k,H,I,path", [(16, 128, 8, 2048, 1024, "auto"),
+                                            (9, 8, 2, 128, 64, "auto"),
+                                            (200, 16, 4, 256, 128, "tensor")])
+def test_switch_glu_per_pick_matches_oracle(T, E, k, H, I, path):
     from lagunalab_b200 import ops
     w, q, x, inds, _ = _setup(T, E, k, H, I, 0, seed=5)
     experts = (q["gate"], q["up"], q["down"])
-    y = ops.switch_glu(x.cuda(), inds, experts)
+    y = ops.switch_glu(x.cuda(), inds, experts, path=path)
     ref = moe_ref.switch_glu(x, inds.cpu().long(), *(to_cpu(m) for m in experts))
     assert y.shape == (T, k, H)
     # per-pick outputs are bf16 gather_qmm results: compare each pick row
@@ -98,3 +105,16 @@ def test_zero_tokens_is_a_no_op():
     out = ops.moe_experts(x[:0].cuda(), inds[:0], wts[:0], 1.0,
                           (q["gate"], q["up"], q["down"]), (q["sh_gate"], q["sh_up"], q["sh_down"]))
     assert out.shape == (0, 128)
+
+
+def test_tensor_and_gemv_paths_agree_on_skewed_routing():
+    """Zipf-skewed routing (one expert with hundreds of rows, others with few): the tcgen05
+    grouped GEMM and the split-K GEMV give the same block output within bf16 tolerance."""
+    from lagunalab_b200 import ops, synth
+    blk, x = synth.moe_block(T=512, E=64, k=8, H=1024, I=512, I_sh=512, seed=2, zipf=True)
+    inds, w = blk.route(x)
+    sw, sh = blk.switch_mlp, blk.shared_expert
+    a = ops.moe_experts(x, inds, w, 1.0, sw.mats, sh.mats, path="tensor")
+    assert ops.moe_status(x.device, 512, 1024, 512, 64, 8, 512) == 0
+    b = ops.moe_experts(x, inds, w, 1.0, sw.mats, sh.mats, path="gemv")
+    assert rel_err(a, b) <= REL_TOL and cos(a, b) >= COS_TOL
