@@ -190,6 +190,28 @@ int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
                            int cap, int n, float scale,
                            void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * lg_q8_decode_attention_noalloc: no counterpart in the reference.  The same fused q8 decode
+ * attention as lg_q8_decode_attention, for callers that cannot allocate device memory at the
+ * moment they call (a plugin host that only hands over input and output pointers, code running
+ * where CUDA forbids allocation calls such as a host function enqueued on a stream, or a
+ * latency-critical path that cannot afford cudaMalloc's implicit device synchronisation).
+ * It allocates nothing: its scratch (split partials and completion counters) lives in a fixed
+ * 4 MiB array inside this library, which every GPU that loads the library holds until the
+ * process exits (lg_q8_decode_fixed_scratch_bytes() returns the size).  A call whose scratch
+ * (lg_q8_decode_workspace_bytes of the same sizes) exceeds it is rejected with LG_ERR_INVALID.
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress)
+ * for the current device; make that first call before any stream capture.  Every call clears
+ * the counters it needs on `stream`; all calls on a device share the one array, so calls that
+ * overlap on the GPU (different streams, or threads without ordering) race and must not be
+ * issued.  Inputs, outputs and limits are those of lg_q8_decode_attention.
+ */
+size_t lg_q8_decode_fixed_scratch_bytes(void);
+int lg_q8_decode_attention_noalloc(const void* q, int B, int Hq, int Hkv, int D,
+                                   const uint32_t* k_q, const void* k_s, const void* k_b,
+                                   const uint32_t* v_q, const void* v_s, const void* v_b,
+                                   int cap, int n, float scale, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

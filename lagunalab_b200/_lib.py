@@ -40,6 +40,9 @@ SIGNATURES = {
     "lg_q8_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
     "lg_q8_decode_attention": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, c_float, P, P,
                                        c_size_t, P]),
+    "lg_q8_decode_fixed_scratch_bytes": (c_size_t, []),
+    "lg_q8_decode_attention_noalloc": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, c_float,
+                                               P, P]),
 }
 
 _lib = None

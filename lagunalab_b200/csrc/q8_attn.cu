@@ -464,3 +464,81 @@ extern "C" int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int
   a.out = static_cast<__nv_bfloat16*>(out);
   return launch_q8_decode(a, scale, workspace, cb, static_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------------------
+// Fixed-scratch variant: the same kernel with its split partials and completion counters in
+// a file-scope device array instead of a caller workspace, for callers that cannot allocate
+// device memory when they call. The array's device address is looked up once per device
+// with cudaGetSymbolAddress (in host code the symbol name is only a stand-in).
+// ---------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace lg {
+
+constexpr size_t Q8_FIXED_SCRATCH_BYTES = (size_t)4 << 20;  // 4 MiB per device
+static __device__ __align__(256) unsigned char q8_fixed_scratch[Q8_FIXED_SCRATCH_BYTES];
+
+constexpr int Q8_MAX_DEVICES = 64;
+static std::mutex q8_fixed_mu;
+static void* q8_fixed_ptr[Q8_MAX_DEVICES] = {};
+
+static int q8_fixed_base(void** out) {
+  int dev = 0;
+  LG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= Q8_MAX_DEVICES)
+    return fail(LG_ERR_UNSUPPORTED, "q8 decode (fixed scratch): device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(q8_fixed_mu);
+  if (!q8_fixed_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, q8_fixed_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(LG_ERR_CUDA, "q8 decode (fixed scratch): cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    q8_fixed_ptr[dev] = p;
+  }
+  *out = q8_fixed_ptr[dev];
+  return LG_OK;
+}
+
+}  // namespace lg
+
+extern "C" size_t lg_q8_decode_fixed_scratch_bytes(void) { return lg::Q8_FIXED_SCRATCH_BYTES; }
+
+extern "C" int lg_q8_decode_attention_noalloc(const void* q, int B, int Hq, int Hkv, int D,
+                                              const uint32_t* k_q, const void* k_s,
+                                              const void* k_b, const uint32_t* v_q,
+                                              const void* v_s, const void* v_b, int cap, int n,
+                                              float scale, void* out, void* stream) {
+  int rc = check_q8_args(q, B, Hq, Hkv, D, k_q, k_s, k_b, v_q, v_s, v_b, cap, n, out);
+  if (rc) return rc;
+  size_t cb;
+  const size_t need = q8_ws(B, Hq, Hkv, n, &cb);
+  if (need > Q8_FIXED_SCRATCH_BYTES)
+    return fail(LG_ERR_INVALID,
+                "q8 decode (fixed scratch): this call needs %zu bytes of scratch, more than the "
+                "fixed %zu (use lg_q8_decode_attention with a caller workspace)",
+                need, Q8_FIXED_SCRATCH_BYTES);
+  void* base = nullptr;
+  rc = q8_fixed_base(&base);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the completion counters must start at zero; a completed call leaves them at zero, but a
+  // call that was cut short would not, so clear them on every call
+  LG_CUDA_TRY(cudaMemsetAsync(base, 0, cb, st));
+  Q8Args a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.kq = k_q;
+  a.ks = static_cast<const __nv_bfloat16*>(k_s);
+  a.kb = static_cast<const __nv_bfloat16*>(k_b);
+  a.vq = v_q;
+  a.vs = static_cast<const __nv_bfloat16*>(v_s);
+  a.vb = static_cast<const __nv_bfloat16*>(v_b);
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.cap = cap;
+  a.n = n;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  return launch_q8_decode(a, scale, base, cb, st);
+}
