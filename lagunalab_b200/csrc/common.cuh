@@ -105,4 +105,31 @@ __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float
                : "memory");
 }
 
+// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024); returns the exclusive
+// prefix and writes the block total to *total.
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? warp_tot[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
+    }
+    if (lane < nw) warp_tot[lane] = wi - w;  // exclusive warp offsets
+    if (lane == nw - 1) *total = wi;
+  }
+  __syncthreads();
+  return warp_tot[warp] + inc - v;
+}
+
 }  // namespace lg

@@ -6,14 +6,15 @@
 //
 // Grouped GEMM (one persistent CTA per SM, tiles of 128 rows x 256 columns x K, K-step 64 =
 // one quantization group):
-//   warp 0      TMA: activation tile (128 x 64 bf16, 128-byte swizzle) into the operand ring
+//   warp 0      TMA: activation tile (128 x 64 bf16, 128-byte swizzle) into a 3-stage ring
 //   warp 2      TMA: packed 4-bit weight rows (256 rows x 32 bytes) into a staging ring
-//   warps 4-7   dequantize the staged words in registers, value = scale * code + bias in bf16
+//   warps 4-11  dequantize the staged words in registers (one B row per thread),
+//               value = scale * code + bias in bf16
 //               (one LOP3 + SUB + FMA per two values), and store the bf16 B tile in the
 //               128-byte-swizzled K-major layout the tensor core reads
 //   warp 1      one thread issues tcgen05.mma (M 128, N 256, K 16, bf16 -> fp32) into one of
 //               two TMEM accumulators (2 x 256 columns) and commits stage / tile barriers
-//   warps 8-11  epilogue: tcgen05.ld of the accumulator; gate/up: SwiGLU with the MLX bf16
+//   warps 12-15 epilogue: tcgen05.ld of the accumulator; gate/up: SwiGLU with the MLX bf16
 //               rounding points (laguna.py:122) -> h; down: y -> bf16, times the routing weight
 //               and routed scale, red.global.add.v4.f32 into the fp32 [T, H] combine
 //               accumulator (laguna.py:149-150), or per-pick stores (SwitchGLU surface)
@@ -36,15 +37,28 @@ namespace lg {
 using namespace tc;
 
 constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64;
-constexpr int TC_NS = 3;  // bf16 operand stages
+constexpr int TC_NA = 3;  // activation (A) stages
+constexpr int TC_NS = 3;  // dequantized weight (B) stages
 constexpr int TC_NP = 4;  // packed-weight stages
-constexpr int TC_THREADS = 384;
+constexpr int TC_THREADS = 512;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;  // 32 KB
 constexpr int TC_P_BYTES = TC_BN * TC_BK / 2;  // 8 KB
-constexpr int TC_NBAR = 3 * TC_NS + 2 * TC_NP + 5;
-constexpr size_t TC_SMEM =
-    1024 + TC_NS * (TC_A_BYTES + TC_B_BYTES) + TC_NP * TC_P_BYTES + TC_NBAR * 8 + 16;
+constexpr int TC_NBAR = 2 * TC_NA + 2 * TC_NS + 2 * TC_NP + 5;
+constexpr size_t TC_SMEM = 1024 + TC_NA * TC_A_BYTES + TC_NS * TC_B_BYTES + TC_NP * TC_P_BYTES +
+                           TC_NBAR * 8 + 16;
+
+#ifdef LG_TC_PROFILE
+// Diagnostic build only: cycles each role spends waiting, per CTA (16 counters).
+__device__ long long* g_tc_stats = nullptr;
+#define TC_T0() const long long tc_t0_ = clock64()
+#define TC_ACC(slot) \
+  do { if (g_tc_stats) atomicAdd((unsigned long long*)&g_tc_stats[(GATEUP ? 0 : 4096) + blockIdx.x * 16 + (slot)], \
+                                 (unsigned long long)(clock64() - tc_t0_)); } while (0)
+#else
+#define TC_T0() ((void)0)
+#define TC_ACC(slot) ((void)0)
+#endif
 
 struct TcArgs {
   const int4* tiles;  // {group, m0, n-tile, 0}
@@ -108,12 +122,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
-  uint8_t* sB = sA + TC_NS * TC_A_BYTES;
+  uint8_t* sB = sA + TC_NA * TC_A_BYTES;
   uint32_t* sP = reinterpret_cast<uint32_t*>(sB + TC_NS * TC_B_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sP) + TC_NP * TC_P_BYTES);
   uint64_t* a_full = bars;
-  uint64_t* b_full = a_full + TC_NS;
-  uint64_t* s_empty = b_full + TC_NS;
+  uint64_t* a_empty = a_full + TC_NA;
+  uint64_t* b_full = a_empty + TC_NA;
+  uint64_t* s_empty = b_full + TC_NS;  // B stage free
   uint64_t* p_full = s_empty + TC_NS;
   uint64_t* p_empty = p_full + TC_NP;
   uint64_t* t_full = p_empty + TC_NP;
@@ -125,8 +140,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int* err = a.err;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_NS; ++i) {
+    for (int i = 0; i < TC_NA; ++i) {
       mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < TC_NS; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&s_empty[i], 1);
     }
@@ -164,10 +182,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int row = a.offsets[tl.x] + tl.y;
       const int ks = ksteps(tl.x);
       for (int kb = 0; kb < ks && ok; ++kb, ++step) {
-        const int s = step % TC_NS;
-        const uint32_t ph = (step / TC_NS) & 1;
+        const int s = step % TC_NA;
+        const uint32_t ph = (step / TC_NA) & 1;
         if (lane == 0) {
-          ok = mbar_wait(&s_empty[s], ph ^ 1, err, 1);
+          TC_T0();
+          ok = mbar_wait(&a_empty[s], ph ^ 1, err, 1);
+          TC_ACC(6);
           if (ok) {
             mbar_arrive_expect_tx(&a_full[s], TC_A_BYTES);
             tma_load_2d(sA + s * TC_A_BYTES, &tm_a, &a_full[s], kb * TC_BK, row);
@@ -205,7 +225,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int p = step % TC_NP;
         const uint32_t ph = (step / TC_NP) & 1;
         if (lane == 0) {
+          TC_T0();
           ok = mbar_wait(&p_empty[p], ph ^ 1, err, 2);
+          TC_ACC(7);
           if (ok) {
             mbar_arrive_expect_tx(&p_full[p], TC_P_BYTES);
             uint32_t* dst = sP + p * (TC_P_BYTES / 4);
@@ -226,22 +248,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int ks = ksteps(tl.x);
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      if (lane == 0) ok = mbar_wait(&t_empty[acc], aph ^ 1, err, 3);
+      if (lane == 0) {
+        TC_T0();
+        ok = mbar_wait(&t_empty[acc], aph ^ 1, err, 3);
+        TC_ACC(2);
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * TC_BN;
       for (int kb = 0; kb < ks && ok; ++kb, ++step) {
-        const int s = step % TC_NS;
-        const uint32_t ph = (step / TC_NS) & 1;
+        const int sa = step % TC_NA, s = step % TC_NS;
+        const uint32_t pha = (step / TC_NA) & 1, ph = (step / TC_NS) & 1;
         if (lane == 0) {
-          ok = mbar_wait(&a_full[s], ph, err, 4) && mbar_wait(&b_full[s], ph, err, 5);
+          {
+            TC_T0();
+            ok = mbar_wait(&a_full[sa], pha, err, 4);
+            TC_ACC(0);
+          }
+          if (ok) {
+            TC_T0();
+            ok = mbar_wait(&b_full[s], ph, err, 5);
+            TC_ACC(1);
+          }
           if (ok) {
             tc_fence_after();
-            const uint64_t ad = sw128_desc(smem_u32(sA + s * TC_A_BYTES));
+            const uint64_t ad = sw128_desc(smem_u32(sA + sa * TC_A_BYTES));
             const uint64_t bd = sw128_desc(smem_u32(sB + s * TC_B_BYTES));
 #pragma unroll
             for (int k = 0; k < TC_BK / 16; ++k)
               umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_commit(&a_empty[sa]);
             umma_commit(&s_empty[s]);
           }
         }
@@ -251,9 +287,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane == 0 && ok) umma_commit(&t_full[acc]);
       __syncwarp();
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---------------- dequantizer: B rows dt and 128 + dt ----------------
-    const int dt = threadIdx.x - 128;
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------- dequantizer: one B row per thread (256 rows) ----------------
+    const int dt = threadIdx.x - 128;  // B-tile row
     int step = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -262,67 +298,71 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const bool sh = (g == a.E);
       const int ks = ksteps(g);
       const int gpr = ks;  // groups per weight row = K / 64
-      const __nv_bfloat16 *sc0, *bi0, *sc1, *bi1;
-      if (GATEUP) {
+      const __nv_bfloat16 *sc, *bi;
+      if (GATEUP) {  // rows 0-127: gate rows, 128-255: up rows, of n-tile rows nt*128 + (dt % 128)
         const size_t base = sh ? 0 : (size_t)g * a.I * gpr;
-        const size_t row = (size_t)(nt * 128 + dt) * gpr;
-        sc0 = (sh ? a.ss0 : a.s0 + base) + row;
-        bi0 = (sh ? a.sb0 : a.b0 + base) + row;
-        sc1 = (sh ? a.ss1 : a.s1 + base) + row;
-        bi1 = (sh ? a.sb1 : a.b1 + base) + row;
-      } else {
+        const size_t row = (size_t)(nt * 128 + (dt & 127)) * gpr;
+        const bool up = dt >= 128;
+        sc = (up ? (sh ? a.ss1 : a.s1 + base) : (sh ? a.ss0 : a.s0 + base)) + row;
+        bi = (up ? (sh ? a.sb1 : a.b1 + base) : (sh ? a.sb0 : a.b0 + base)) + row;
+      } else {  // down rows nt*256 + dt
         const size_t base = sh ? 0 : (size_t)g * H * gpr;
-        const size_t row0 = (size_t)(nt * 256 + dt) * gpr;
-        const size_t row1 = (size_t)(nt * 256 + 128 + dt) * gpr;
-        sc0 = (sh ? a.ss0 : a.s0 + base) + row0;
-        bi0 = (sh ? a.sb0 : a.b0 + base) + row0;
-        sc1 = (sh ? a.ss0 : a.s0 + base) + row1;
-        bi1 = (sh ? a.sb0 : a.b0 + base) + row1;
+        const size_t row = (size_t)(nt * 256 + dt) * gpr;
+        sc = (sh ? a.ss0 : a.s0 + base) + row;
+        bi = (sh ? a.sb0 : a.b0 + base) + row;
       }
-      __nv_bfloat16 ns0 = sc0[0], nb0 = bi0[0], ns1 = sc1[0], nb1 = bi1[0];
+      __nv_bfloat16 ns = sc[0], nb = bi[0];
       for (int kb = 0; kb < ks && ok; ++kb, ++step) {
-        const uint32_t s02 = bf2_splat(ns0), b02 = bf2_splat(nb0);
-        const uint32_t s12 = bf2_splat(ns1), b12 = bf2_splat(nb1);
+        const uint32_t s2 = bf2_splat(ns), b2 = bf2_splat(nb);
         if (kb + 1 < ks) {  // next group's scale/bias, issued before the waits
-          ns0 = sc0[kb + 1];
-          nb0 = bi0[kb + 1];
-          ns1 = sc1[kb + 1];
-          nb1 = bi1[kb + 1];
+          ns = sc[kb + 1];
+          nb = bi[kb + 1];
         }
         const int p = step % TC_NP, s = step % TC_NS;
         const uint32_t pph = (step / TC_NP) & 1, sph = (step / TC_NS) & 1;
         // wait for the packed words and for the operand stage, then load, dequantize and
         // store; the staging stage is released only after the stores, which depend on the
         // loaded words, so no later TMA into it can race with these loads
-        const bool got = mbar_wait(&p_full[p], pph, err, 6) && mbar_wait(&s_empty[s], sph ^ 1, err, 7);
+        bool got;
+        {
+          TC_T0();
+          got = mbar_wait(&p_full[p], pph, err, 6);
+          if (dt == 0) TC_ACC(3);
+        }
         if (got) {
-          const uint32_t* src = sP + p * (TC_P_BYTES / 4);
-          const uint4 w0a = *reinterpret_cast<const uint4*>(src + dt * 8);
-          const uint4 w0b = *reinterpret_cast<const uint4*>(src + dt * 8 + 4);
-          const uint4 w1a = *reinterpret_cast<const uint4*>(src + (128 + dt) * 8);
-          const uint4 w1b = *reinterpret_cast<const uint4*>(src + (128 + dt) * 8 + 4);
-          uint8_t* dst = sB + s * TC_B_BYTES;
-          const uint32_t wv0[8] = {w0a.x, w0a.y, w0a.z, w0a.w, w0b.x, w0b.y, w0b.z, w0b.w};
-          const uint32_t wv1[8] = {w1a.x, w1a.y, w1a.z, w1a.w, w1b.x, w1b.y, w1b.z, w1b.w};
-          const int r0 = dt, r1 = 128 + dt;
+          TC_T0();
+          got = mbar_wait(&s_empty[s], sph ^ 1, err, 7);
+          if (dt == 0) TC_ACC(4);
+        }
+        if (got) {
+          // staged rows are 32 bytes, written by TMA with the 32-byte swizzle: the 16-byte half
+          // c of row r sits at half c ^ ((r >> 2) & 1)
+          const uint32_t* src = sP + p * (TC_P_BYTES / 4) + dt * 8;
+          const int x0 = ((dt >> 2) & 1) * 4;
+          const uint4 wa = *reinterpret_cast<const uint4*>(src + x0);
+          const uint4 wb = *reinterpret_cast<const uint4*>(src + (4 - x0));
+          uint8_t* dst = sB + s * TC_B_BYTES + dt * 128;
+          const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            *reinterpret_cast<uint4*>(dst + r0 * 128 + ((j ^ (r0 & 7)) << 4)) = deq_word(wv0[j], s02, b02);
-            *reinterpret_cast<uint4*>(dst + r1 * 128 + ((j ^ (r1 & 7)) << 4)) = deq_word(wv1[j], s12, b12);
-          }
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(dst + ((j ^ (dt & 7)) << 4)) = deq_word(wv[j], s2, b2);
           // order this thread's generic-proxy stores before the tensor core's async-proxy reads
           fence_proxy_async_smem();
         }
-        // all 128 threads have stored and fenced: one thread releases the staging stage and
+        // all 256 threads have stored and fenced: one thread releases the staging stage and
         // publishes the operand stage
-        ok = bar_and_128<1>(got);
+        {
+          TC_T0();
+          ok = bar_and_n<1, 256>(got);
+          if (dt == 0) TC_ACC(5);
+        }
         if (!ok) break;
         if (dt == 0) mbar_arrive(&p_empty[p]);
         if (dt == 0) mbar_arrive(&b_full[s]);
       }
     }
-  } else if (warp >= 8) {
-    // ---------------- epilogue ----------------
+  } else if (warp >= 12) {
+    // ---------------- epilogue (warps 12-15: TMEM lane quarters 0-3) ----------------
     const int q = warp & 3;
     const int er = 32 * q + lane;  // tile row = TMEM lane
     int it = 0;
@@ -332,7 +372,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int g = tl.x, m0 = tl.y, nt = tl.z;
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      ok = bar_and_128<2>(mbar_wait(&t_full[acc], aph, err, 8));
+      {
+        TC_T0();
+        ok = bar_and_n<2, 128>(mbar_wait(&t_full[acc], aph, err, 8));
+        if (er == 0) TC_ACC(8);
+      }
       if (!ok) break;  // uniform over the epilogue warps: tcgen05.ld is a warp-collective
       tc_fence_after();
       const int row0 = a.offsets[g], cnt = a.offsets[g + 1] - row0;
@@ -399,13 +443,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // every epilogue thread has waited for its TMEM loads; one arrive hands the accumulator
       // back to the MMA issuer after all 128 have passed the barrier
       tc_fence_before();
-      bar_and_128<2>(true);
+      bar_and_n<2, 128>(true);
       if (er == 0) mbar_arrive(&t_empty[acc]);
     }
   }
 
   // ---------------- teardown: every MMA retired before TMEM is released ----------------
   __syncthreads();
+#ifdef LG_TC_PROFILE
+  if (threadIdx.x == 0 && g_tc_stats) g_tc_stats[(GATEUP ? 0 : 4096) + blockIdx.x * 16 + 9] = clock64();
+#endif
   if (warp == 1) {
     if (lane == 0) {
       umma_commit(teardown);
@@ -444,14 +491,16 @@ __global__ void __launch_bounds__(256) dispatch_gather_kernel(const __nv_bfloat1
 }
 
 // Tile lists for both products, ordered by group, then n-tile, then m-tile (a group's tiles
-// run side by side, so its weights and activations stay in L2). One thread per group after
-// a block-wide prefix sum of the per-group tile counts.
+// run side by side, so its weights and activations stay in L2). Per-group tile counts are
+// scanned across the block, then every thread writes tiles, finding each tile's group by a
+// binary search over the scanned counts.
 __global__ void __launch_bounds__(512) tc_schedule_kernel(const int32_t* __restrict__ offsets,
                                                           int G, int E, int I, int I_sh, int H,
                                                           int4* __restrict__ tiles_gu,
                                                           int4* __restrict__ tiles_dn,
                                                           int* __restrict__ counts) {
-  __shared__ int pre_gu[513], pre_dn[513];
+  __shared__ int pre_gu[513], pre_dn[513], mts[512];
+  __shared__ int warp_tot[32], tot_gu, tot_dn;
   const int g = threadIdx.x;
   int ngu = 0, ndn = 0, mt = 0;
   if (g < G) {
@@ -461,27 +510,35 @@ __global__ void __launch_bounds__(512) tc_schedule_kernel(const int32_t* __restr
     ngu = mt * (Ig / 128);
     ndn = mt * (H / 256);
   }
-  pre_gu[g + 1] = ngu;
-  pre_dn[g + 1] = ndn;
-  if (g == 0) pre_gu[0] = pre_dn[0] = 0;
+  mts[g] = mt;
+  pre_gu[g] = block_excl_scan(ngu, warp_tot, &tot_gu);
+  pre_dn[g] = block_excl_scan(ndn, warp_tot, &tot_dn);
   __syncthreads();
+  const int ngu_all = tot_gu, ndn_all = tot_dn;
   if (g == 0) {
-    for (int i = 1; i <= (int)blockDim.x; ++i) {
-      pre_gu[i] += pre_gu[i - 1];
-      pre_dn[i] += pre_dn[i - 1];
-    }
-    counts[0] = pre_gu[blockDim.x];
-    counts[1] = pre_dn[blockDim.x];
+    counts[0] = ngu_all;
+    counts[1] = ndn_all;
   }
-  __syncthreads();
-  if (g < G && mt > 0) {
-    const int Ig = (g == E) ? I_sh : I;
-    int o = pre_gu[g];
-    for (int nt = 0; nt < Ig / 128; ++nt)
-      for (int m = 0; m < mt; ++m) tiles_gu[o++] = make_int4(g, m * TC_BM, nt, 0);
-    o = pre_dn[g];
-    for (int nt = 0; nt < H / 256; ++nt)
-      for (int m = 0; m < mt; ++m) tiles_dn[o++] = make_int4(g, m * TC_BM, nt, 0);
+  auto group_of = [&](const int* pre, int i) {
+    int lo = 0, hi = G - 1;  // last group with pre[group] <= i
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (pre[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo;
+  };
+  for (int i = threadIdx.x; i < ngu_all; i += blockDim.x) {
+    int gg = group_of(pre_gu, i);
+    while (mts[gg] == 0) --gg;  // skip empty groups sharing the same prefix
+    const int local = i - pre_gu[gg];
+    tiles_gu[i] = make_int4(gg, (local % mts[gg]) * TC_BM, local / mts[gg], 0);
+  }
+  for (int i = threadIdx.x; i < ndn_all; i += blockDim.x) {
+    int gg = group_of(pre_dn, i);
+    while (mts[gg] == 0) --gg;
+    const int local = i - pre_dn[gg];
+    tiles_dn[i] = make_int4(gg, (local % mts[gg]) * TC_BM, local / mts[gg], 0);
   }
 }
 
@@ -502,8 +559,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// swz: 128 = 128-byte swizzle (bf16 operand tiles), 32 = 32-byte swizzle (packed weight rows)
 static int make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64_t rows,
-                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, int swz) {
   auto fn = encode_fn();
   if (!fn) return fail(LG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {inner, rows};
@@ -512,7 +570,8 @@ static int make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t inner,
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  swz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : (swz == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(LG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return LG_OK;
@@ -606,21 +665,21 @@ int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cuda
   CUtensorMap ma, mg, mu, msg, msu, mh, md, msd;
   const int H = a.H;
   int rc;
-  if ((rc = make_map(&ma, w.xp, true, H, rows, (uint64_t)H * 2, 64, 128, true))) return rc;
-  if ((rc = make_map(&mh, a.h, true, Imax, rows, (uint64_t)a.h_stride * 2, 64, 128, true))) return rc;
+  if ((rc = make_map(&ma, w.xp, true, H, rows, (uint64_t)H * 2, 64, 128, 128))) return rc;
+  if ((rc = make_map(&mh, a.h, true, Imax, rows, (uint64_t)a.h_stride * 2, 64, 128, 128))) return rc;
   const void* dummy = w.xp;  // any valid map for absent matrices (never read)
   if (a.E > 0) {
-    if ((rc = make_map(&mg, a.g_q, false, H / 8, (uint64_t)a.E * a.I, H / 2, 8, 128, false))) return rc;
-    if ((rc = make_map(&mu, a.u_q, false, H / 8, (uint64_t)a.E * a.I, H / 2, 8, 128, false))) return rc;
-    if ((rc = make_map(&md, a.d_q, false, a.I / 8, (uint64_t)a.E * H, a.I / 2, 8, 128, false))) return rc;
+    if ((rc = make_map(&mg, a.g_q, false, H / 8, (uint64_t)a.E * a.I, H / 2, 8, 128, 32))) return rc;
+    if ((rc = make_map(&mu, a.u_q, false, H / 8, (uint64_t)a.E * a.I, H / 2, 8, 128, 32))) return rc;
+    if ((rc = make_map(&md, a.d_q, false, a.I / 8, (uint64_t)a.E * H, a.I / 2, 8, 128, 32))) return rc;
   } else {
-    if ((rc = make_map(&mg, dummy, false, 8, 128, 32, 8, 128, false))) return rc;
+    if ((rc = make_map(&mg, dummy, false, 8, 128, 32, 8, 128, 32))) return rc;
     mu = md = mg;
   }
   if (a.I_sh > 0) {
-    if ((rc = make_map(&msg, a.sg_q, false, H / 8, a.I_sh, H / 2, 8, 128, false))) return rc;
-    if ((rc = make_map(&msu, a.su_q, false, H / 8, a.I_sh, H / 2, 8, 128, false))) return rc;
-    if ((rc = make_map(&msd, a.sd_q, false, a.I_sh / 8, H, a.I_sh / 2, 8, 128, false))) return rc;
+    if ((rc = make_map(&msg, a.sg_q, false, H / 8, a.I_sh, H / 2, 8, 128, 32))) return rc;
+    if ((rc = make_map(&msu, a.su_q, false, H / 8, a.I_sh, H / 2, 8, 128, 32))) return rc;
+    if ((rc = make_map(&msd, a.sd_q, false, a.I_sh / 8, H, a.I_sh / 2, 8, 128, 32))) return rc;
   } else {
     msg = msu = msd = mg;
   }
@@ -685,5 +744,11 @@ int tc_status(const void* tc_ws, int T, int H, int I, int I_sh, int E, int k, in
   LG_CUDA_TRY(cudaMemcpy(status, w.counts + 2, sizeof(int), cudaMemcpyDeviceToHost));
   return LG_OK;
 }
+
+#ifdef LG_TC_PROFILE
+extern "C" int lg_tc_set_stats(void* p) {
+  return cudaMemcpyToSymbol(g_tc_stats, &p, sizeof(p)) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 }  // namespace lg

@@ -1,7 +1,9 @@
 // Router (laguna_mlx/laguna.py:137-145) and routing plan kernels.
 //
-// router_logits_kernel: logits[T, E] = x[T, H] . W[E, H]^T in fp32 (W fp32, or MLX 8-bit
-//   group-64 dequantized while staging, whose bf16 matmul output is rounded to bf16).
+// router logits: logits[T, E] = x[T, H] . W[E, H]^T in fp32 (W fp32, or MLX 8-bit group-64
+//   dequantized, whose bf16 matmul output is rounded to bf16). Three kernels: a warp per expert
+//   for T <= 32 (decode), a tensor-core kernel for fp32 W at larger T (W split into three bf16
+//   parts, so the result keeps fp32 accuracy), and a CUDA-core tiled kernel otherwise.
 // router_topk_kernel:   one warp per token: sigmoid (or softmax), + selection bias, top-k by
 //   repeated warp arg-max (larger first, equal keys -> lower index), unbiased weights,
 //   renormalisation, bf16 weights; a per-CTA histogram in shared memory (the warp's winning
@@ -83,6 +85,147 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
         logits[(size_t)t * E + e] = v;
       }
     }
+  }
+}
+
+// ---- tensor-core router logits (fp32 weight, T > 32) -----------------------------------
+// x (bf16, exact) times W (fp32) with W split into three bf16 parts, hi + mid + lo = W to
+// within 2^-24 relative, each product exact in the fp32 accumulator: fp32-accurate logits
+// on mma.sync m16n8k16. CTA tile 64 tokens x 32 experts, 4 warps of 16 tokens, K chunk 64;
+// the next chunk's global loads are issued into registers before the current chunk's MMAs.
+constexpr int RM_TT = 64, RM_EB = 32, RM_KC = 64, RM_LD = RM_KC + 8;  // padded smem rows
+
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                int T, int H,
+                                                                const float* __restrict__ W,
+                                                                int E, float* __restrict__ logits) {
+  __shared__ __align__(16) __nv_bfloat16 xs[RM_TT][RM_LD];
+  __shared__ __align__(16) __nv_bfloat16 ws[3][RM_EB][RM_LD];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = blockIdx.y * RM_TT, e0 = blockIdx.x * RM_EB;
+  // per thread: 4 uint4 of x (rows tid/8 + 16j, 8-element column block tid%8) and
+  // 4 float4 of W (rows tid/16 + 8j, 4-element column block tid%16)
+  uint4 xv[4];
+  float4 wv[4];
+  auto load = [&](int h0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = (tid >> 3) + 16 * j, c = (tid & 7) * 8;
+      xv[j] = (t0 + r < T) ? *reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * H + h0 + c)
+                           : make_uint4(0, 0, 0, 0);
+      const int er = (tid >> 4) + 8 * j, ec = (tid & 15) * 4;
+      wv[j] = (e0 + er < E) ? *reinterpret_cast<const float4*>(W + (size_t)(e0 + er) * H + h0 + ec)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  load(0);
+  for (int h0 = 0; h0 < H; h0 += RM_KC) {
+    // registers -> shared (W split into three bf16 parts)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      *reinterpret_cast<uint4*>(&xs[(tid >> 3) + 16 * j][(tid & 7) * 8]) = xv[j];
+      const int er = (tid >> 4) + 8 * j, ec = (tid & 15) * 4;
+      const float f[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat16 hi = __float2bfloat16_rn(f[q]);
+        const float r1 = f[q] - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        ws[0][er][ec + q] = hi;
+        ws[1][er][ec + q] = mid;
+        ws[2][er][ec + q] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      }
+    }
+    __syncthreads();
+    if (h0 + RM_KC < H) load(h0 + RM_KC);  // next chunk in flight during the MMAs
+#pragma unroll
+    for (int k16 = 0; k16 < RM_KC; k16 += 16) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(&xs[warp * 16 + (lane & 15)][k16 + ((lane >> 4) << 3)], a0, a1, a2, a3);
+#pragma unroll
+      for (int part = 0; part < 3; ++part) {
+#pragma unroll
+        for (int nt = 0; nt < 4; nt += 2) {
+          const int m = lane >> 3;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(&ws[part][(nt + (m >> 1)) * 8 + (lane & 7)][k16 + ((m & 1) << 3)], b0, b1, b2, b3);
+          mma16816(acc[nt], a0, a1, a2, a3, b0, b1);
+          mma16816(acc[nt + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int r = lane >> 2, c4 = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = t0 + warp * 16 + r + 8 * h;
+      const int e = e0 + nt * 8 + 2 * c4;
+      if (t < T) {
+        if (e < E) logits[(size_t)t * E + e] = acc[nt][2 * h];
+        if (e + 1 < E) logits[(size_t)t * E + e + 1] = acc[nt][2 * h + 1];
+      }
+    }
+  }
+}
+
+// ---- small-T router logits (decode): one warp per expert -------------------------------
+// Lanes stride over the hidden dimension two elements at a time (coalesced bf16x2 / float2
+// loads; the weight row stays in L1 across the T <= 32 tokens) and reduce across the warp.
+template <int GBITS>
+__global__ void __launch_bounds__(256) router_logits_gemv_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int H, const void* __restrict__ gw,
+    const __nv_bfloat16* __restrict__ gs, const __nv_bfloat16* __restrict__ gb, int E,
+    float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (e >= E) return;
+  for (int t = 0; t < T; ++t) {
+    const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (size_t)t * H);
+    float acc = 0.f;
+    for (int k2 = lane; k2 < H / 2; k2 += 32) {
+      const float2 xv = __bfloat1622float2(xr[k2]);
+      float w0, w1;
+      if (GBITS == 0) {
+        const float2 wv = reinterpret_cast<const float2*>(static_cast<const float*>(gw) +
+                                                          (size_t)e * H)[k2];
+        w0 = wv.x;
+        w1 = wv.y;
+      } else {
+        const int k = 2 * k2;
+        const uint32_t word = static_cast<const uint32_t*>(gw)[(size_t)e * (H / 4) + (k >> 2)];
+        const float sc = bf2f(gs[(size_t)e * (H / 64) + k / 64]);
+        const float bi = bf2f(gb[(size_t)e * (H / 64) + k / 64]);
+        w0 = fmaf(sc, code_to_f((word >> (8 * (k & 3))) & 0xffu), bi);
+        w1 = fmaf(sc, code_to_f((word >> (8 * ((k + 1) & 3))) & 0xffu), bi);
+      }
+      acc = fmaf(xv.x, w0, acc);
+      acc = fmaf(xv.y, w1, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(size_t)t * E + e] = (GBITS == 8) ? round_bf16(acc) : acc;
   }
 }
 
@@ -188,80 +331,66 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
 }
 
 // One CTA per group g in [0, G); G = E (+1 with the shared group). Expert ids outside
-// [0, E) belong to no group: such picks produce no output.
+// [0, E) belong to no group: such picks produce no output. Each thread owns a contiguous run
+// of picks, so one counting pass, one block scan and one writing pass give the group's picks
+// in pick order. Every CTA writes its own offset (= valid picks of lower experts); groups with
+// rows append themselves to the active list (order irrelevant; active[0] must start at 0).
 __global__ void __launch_bounds__(512) moe_plan_kernel(const int32_t* __restrict__ inds, int T,
                                                        int k, int E, int with_shared,
                                                        int32_t* __restrict__ counts,
                                                        int32_t* __restrict__ offsets,
                                                        int32_t* __restrict__ perm,
                                                        int32_t* __restrict__ active) {
-  __shared__ int warp_tot[16];
-  __shared__ int s_base;
-  __shared__ int cnt[257];
+  __shared__ int warp_tot[32];
+  __shared__ int s_total, s_before;
   const int g = blockIdx.x;
-  const int G = E + (with_shared ? 1 : 0);
   const int P = T * k;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  if (g == E) {
-    // shared expert: identity rows T*k + t, after every routed group
-    for (int t = threadIdx.x; t < T; t += blockDim.x) perm[P + t] = P + t;
-    if (threadIdx.x == 0) counts[E] = T;
-  } else {
-    if (threadIdx.x == 0) s_base = 0;
-    __syncthreads();
-    // offset of group g = number of valid picks with expert < g
-    int before = 0;
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-      int e = inds[p];
-      before += (e >= 0 && e < g) ? 1 : 0;
-    }
+  const int nth = blockDim.x;
+  const int per = (P + nth - 1) / nth;
+  const int p0 = min(P, threadIdx.x * per), p1 = min(P, p0 + per);
+  if (threadIdx.x == 0) s_before = 0;
+  __syncthreads();
+  int eq = 0, lt = 0;
+  if ((per & 3) == 0 && (reinterpret_cast<uintptr_t>(inds) & 15) == 0) {
+    for (int p = p0; p < p1; p += 4) {
+      const int4 v = *reinterpret_cast<const int4*>(inds + p);
+      const int e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
-    if (lane == 0) atomicAdd(&s_base, before);
-    __syncthreads();
-    const int base = s_base;
-    int running = 0;
-    for (int p0 = 0; p0 < P; p0 += blockDim.x) {
-      int p = p0 + threadIdx.x;
-      bool f = (p < P) && (inds[p] == g);
-      unsigned m = __ballot_sync(0xffffffffu, f);
-      if (lane == 0) warp_tot[warp] = __popc(m);
-      __syncthreads();
-      int wpre = 0, tot = 0;
-      for (int w = 0; w < nwarps; ++w) {
-        int c = warp_tot[w];
-        if (w < warp) wpre += c;
-        tot += c;
+      for (int j = 0; j < 4; ++j) {
+        eq += (e[j] == g);
+        lt += (e[j] >= 0 && e[j] < g);
       }
-      if (f) perm[base + running + wpre + __popc(m & ((1u << lane) - 1u))] = p;
-      running += tot;
-      __syncthreads();
     }
-    if (threadIdx.x == 0) counts[g] = running;
+  } else {
+    for (int p = p0; p < p1; ++p) {
+      const int e = inds[p];
+      eq += (e == g);
+      lt += (e >= 0 && e < g);
+    }
   }
-  if (g == 0) {
-    // CTA 0 also writes the offsets (and the active-group list); it recounts every group
-    // itself so that it does not depend on the other CTAs.
-    for (int i = threadIdx.x; i < 257; i += blockDim.x) cnt[i] = 0;
-    __syncthreads();
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-      int e = inds[p];
-      if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-    }
-    __syncthreads();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
+  if ((threadIdx.x & 31) == 0 && lt) atomicAdd(&s_before, lt);
+  const int off = block_excl_scan(eq, warp_tot, &s_total);  // its barriers also publish s_before
+  const int before = s_before;
+  if (g == E) {  // shared expert: identity rows after all valid routed picks
+    for (int t = threadIdx.x; t < T; t += nth) perm[before + t] = P + t;
     if (threadIdx.x == 0) {
-      if (with_shared) cnt[E] = T;
-      int acc = 0, na = 0;
-      for (int i = 0; i < G; ++i) {
-        offsets[i] = acc;
-        acc += cnt[i];
-        if (active && cnt[i] > 0) active[1 + na++] = i;
-      }
-      offsets[G] = acc;
-      if (!with_shared) offsets[E + 1] = acc;
-      if (active) active[0] = na;
+      counts[E] = T;
+      offsets[E] = before;
+      offsets[E + 1] = before + T;
+      if (active && T > 0) active[1 + atomicAdd(active, 1)] = E;
     }
+    return;
+  }
+  int j = 0;
+  for (int p = p0; p < p1 && j < eq; ++p)
+    if (inds[p] == g) perm[before + off + j++] = p;
+  if (threadIdx.x == 0) {
+    counts[g] = s_total;
+    offsets[g] = before;
+    if (g == E - 1 && !with_shared) offsets[E] = offsets[E + 1] = before + s_total;
+    if (active && s_total > 0) active[1 + atomicAdd(active, 1)] = g;
   }
 }
 
@@ -288,16 +417,30 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (counts) LG_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, s));
   if (T == 0) return LG_OK;
-  dim3 g1((E + RL_EB - 1) / RL_EB, (T + RL_TT - 1) / RL_TT);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  const __nv_bfloat16* gsb = static_cast<const __nv_bfloat16*>(gate_scales);
+  const __nv_bfloat16* gbb = static_cast<const __nv_bfloat16*>(gate_biases);
+  const bool xa = aligned(x, 16) && aligned(gate_w, 16);
   prof_begin("router_logits", s);
-  if (gate_bits == 0)
-    router_logits_kernel<0><<<g1, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T, H,
-                                               gate_w, nullptr, nullptr, E, logits);
-  else
-    router_logits_kernel<8><<<g1, 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), T, H, gate_w,
-        static_cast<const __nv_bfloat16*>(gate_scales),
-        static_cast<const __nv_bfloat16*>(gate_biases), E, logits);
+  if (T <= 32) {
+    // decode: one warp per expert, weight row in registers
+    if (gate_bits == 0)
+      router_logits_gemv_kernel<0><<<(E + 7) / 8, 256, 0, s>>>(xb, T, H, gate_w, nullptr, nullptr,
+                                                               E, logits);
+    else
+      router_logits_gemv_kernel<8><<<(E + 7) / 8, 256, 0, s>>>(xb, T, H, gate_w, gsb, gbb, E,
+                                                               logits);
+  } else if (gate_bits == 0 && xa) {
+    dim3 g((E + RM_EB - 1) / RM_EB, (T + RM_TT - 1) / RM_TT);
+    router_logits_mma_kernel<<<g, 128, 0, s>>>(xb, T, H, static_cast<const float*>(gate_w), E,
+                                               logits);
+  } else {
+    dim3 g1((E + RL_EB - 1) / RL_EB, (T + RL_TT - 1) / RL_TT);
+    if (gate_bits == 0)
+      router_logits_kernel<0><<<g1, 256, 0, s>>>(xb, T, H, gate_w, nullptr, nullptr, E, logits);
+    else
+      router_logits_kernel<8><<<g1, 256, 0, s>>>(xb, T, H, gate_w, gsb, gbb, E, logits);
+  }
   prof_end("router_logits", s);
   LG_LAUNCH_CHECK("router_logits");
   int blocks = (T + TK_WARPS - 1) / TK_WARPS;
@@ -317,6 +460,7 @@ int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32
                 int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s) {
   int G = E + (with_shared ? 1 : 0);
   if (G == 0) return LG_OK;
+  if (active) LG_CUDA_TRY(cudaMemsetAsync(active, 0, sizeof(int32_t), s));
   prof_begin("plan", s);
   moe_plan_kernel<<<G, 512, 0, s>>>(inds, T, k, E, with_shared, counts, offsets, perm, active);
   prof_end("plan", s);

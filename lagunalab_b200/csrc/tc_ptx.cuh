@@ -63,12 +63,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
                                           long long limit_cycles = 4000000000LL) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) != 0) return false;  // another role gave up
-    if (clock64() - t0 > limit_cycles) {
-      atomicCAS(err, 0, code);
-      return false;
+    if ((n & 63) == 0) {  // check the error word and the clock only now and then
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;  // another role gave up
+      if (clock64() - t0 > limit_cycles) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
     }
   }
 }
@@ -87,20 +89,20 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Barrier over 128 threads (four whole warps) on named barrier `ID` (1 = dequantizer warps
-// 4-7, 2 = epilogue warps 8-11) that also returns the AND of every participant's `ok`, so all
+// Barrier over N threads (whole warps) on named barrier ID (1 = dequantizer warps,
+// 2 = epilogue warps) that also returns the AND of every participant's `ok`, so all
 // participants leave a loop together when any wait expired. Every participant must reach it
 // on every iteration.
-template <int ID>
-__device__ __forceinline__ bool bar_and_128(bool ok) {
+template <int ID, int N>
+__device__ __forceinline__ bool bar_and_n(bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred pi, po;\n\t"
       "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.and.pred po, %2, 128, pi;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
       "selp.u32 %0, 1, 0, po;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)ok), "n"(ID)
+      : "r"((uint32_t)ok), "n"(ID), "n"(N)
       : "memory");
   return r != 0;
 }
