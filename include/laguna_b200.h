@@ -51,7 +51,8 @@ long long lg_launch_count(void);
  * Measurement hook: on this thread, record cudaEvent_t ev_start / ev_end on the launching
  * stream immediately before / after every launch of the named stage ("router_logits",
  * "router_topk", "plan", "experts_gateup", "experts_down", "finalize", "q8_decode").
- * stage == NULL turns it off.  No effect on results.
+ * stage == NULL turns it off.  No effect on results.  Inside a stream capture the records
+ * become external event-record nodes, so each graph replay re-times the stage.
  */
 int lg_profile_stage(const char* stage, void* ev_start, void* ev_end);
 
@@ -181,8 +182,9 @@ size_t lg_q8_decode_workspace_bytes(int B, int Hq, int Hkv, int n);
  * q bf16 [B, Hq, D]; K/V: packed uint32 [B, Hkv, cap, D/4], scales/biases bf16
  * [B, Hkv, cap, D/64] (full-capacity buffers; only rows < n are read).  out bf16 [B, Hq, D].
  * D == 128, Hq % Hkv == 0, Hq/Hkv <= 16, 1 <= n <= cap.
- * The workspace's first 256 bytes hold per-(batch, kv head) counters that must be zero
- * before the first call; every completed call leaves them zero again.
+ * The workspace's first 16 KiB hold completion counters that must be zero before the first
+ * call; every completed call leaves them zero again, whatever its sizes, so one zeroed
+ * workspace of the largest size needed serves calls of any shapes.
  */
 int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
                            const uint32_t* k_q, const void* k_s, const void* k_b,
@@ -197,7 +199,7 @@ int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
  * where CUDA forbids allocation calls such as a host function enqueued on a stream, or a
  * latency-critical path that cannot afford cudaMalloc's implicit device synchronisation).
  * It allocates nothing: its scratch (split partials and completion counters) lives in a fixed
- * 4 MiB array inside this library, which every GPU that loads the library holds until the
+ * 1 MiB array inside this library, which every GPU that loads the library holds until the
  * process exits (lg_q8_decode_fixed_scratch_bytes() returns the size).  A call whose scratch
  * (lg_q8_decode_workspace_bytes of the same sizes) exceeds it is rejected with LG_ERR_INVALID.
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress)

@@ -31,12 +31,22 @@ static thread_local cudaEvent_t g_ev0 = nullptr, g_ev1 = nullptr;
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// Inside a stream capture the record becomes a graph node that timestamps on every replay
+// (an "external" event record); outside it is an ordinary record.
+static void prof_record(cudaEvent_t ev, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, s);
+}
+
 void prof_begin(const char* stage, cudaStream_t s) {
-  if (g_ev0 && std::strcmp(stage, g_stage) == 0) cudaEventRecord(g_ev0, s);
+  if (g_ev0 && std::strcmp(stage, g_stage) == 0) prof_record(g_ev0, s);
 }
 
 void prof_end(const char* stage, cudaStream_t s) {
-  if (g_ev1 && std::strcmp(stage, g_stage) == 0) cudaEventRecord(g_ev1, s);
+  if (g_ev1 && std::strcmp(stage, g_stage) == 0) prof_record(g_ev1, s);
 }
 
 }  // namespace lg

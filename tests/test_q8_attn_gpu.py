@@ -3,6 +3,8 @@
 Mirrors lagunaLab tests/test_q8_attn.py:19-31: lengths 1, 7, BLOCK, BLOCK+1, 3*BLOCK+100 on
 48 query / 8 KV heads with buffers longer than n, max abs error < 2e-2; plus BASELINE
 config 4's 32/4 heads (G = 8, which the reference Metal kernel refuses) at 82,671 keys."""
+import ctypes
+
 import pytest
 import torch
 
@@ -97,3 +99,26 @@ def test_fused_cache_decode_matches_dequant_path():
         want = attn_ref.sdpa_decode_ref(q.cpu(), kd.cpu(), vd.cpu(), kd.shape[2], 128 ** -0.5)
         assert (got.cpu().float() - want.float()).abs().max() < 2e-2
     assert fused.offset == 303 and fused.q.keys[0].shape[2] == 512
+
+
+def test_one_workspace_serves_mixed_shapes():
+    """One zeroed workspace, calls of different (batch, kv head) counts in turn: each call
+    must find its completion counters at zero wherever the previous call put its partials."""
+    from lagunalab_b200 import _lib
+    shapes = [(1, 4, 32, 20000), (4, 8, 64, 3000), (1, 2, 16, 9000), (4, 8, 64, 3000),
+              (1, 4, 32, 20000)]
+    need = max(_lib.lib().lg_q8_decode_workspace_bytes(B, Hq, hkv, n) for B, hkv, Hq, n in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for i, (B, hkv, Hq, n) in enumerate(shapes):
+        cap = (n + 255) // 256 * 256
+        kt, vt = _cache(B, hkv, n, cap, seed=100 + i)
+        q = torch.randn(B, Hq, 1, 128, generator=torch.Generator().manual_seed(i)).to(torch.bfloat16).cuda()
+        out = torch.empty_like(q)
+        _lib.call("lg_q8_decode_attention", q.data_ptr(), B, Hq, hkv, 128,
+                  *(t.data_ptr() for t in kt), *(t.data_ptr() for t in vt), cap, n,
+                  ctypes.c_float(128 ** -0.5), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                  torch.cuda.current_stream().cuda_stream)
+        want = attn_ref.q8_decode_attention_ref(q.float().cpu(), tuple(t.cpu() for t in kt),
+                                                tuple(t.cpu() for t in vt), n, 128 ** -0.5)
+        assert (out.cpu().float() - want.float()).abs().max() < 2e-2, (B, hkv, Hq, n)
+    assert int(ws[:16384].count_nonzero()) == 0  # counters left at zero
