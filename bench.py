@@ -42,6 +42,17 @@ WORKLOADS = {
 }
 
 
+def profile_traffic(name):
+    """DRAM bytes per launch from the committed ncu summary profiles/<name>.md (the
+    ``traffic_bytes_per_launch:`` line), or None."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1])
+    return None
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -268,7 +279,6 @@ def run_q8(args, wl, ws, rank):
     a CUDA graph and replayed per step (the per-call host cost of a Python ctypes call would
     otherwise exceed the kernel's ~15 us)."""
     from lagunalab_b200 import ops, synth
-    from lagunalab_b200.q8_attn import q8_decode_attention
     L, n, B, Hq, Hkv = (wl[k] for k in ("L", "n", "B", "Hq", "Hkv"))
     layers = synth.q8_layers(L, n, B, Hq, Hkv, seed=rank)
     scale = 128 ** -0.5
@@ -279,7 +289,7 @@ def run_q8(args, wl, ws, rank):
             ops.q8_decode_attention(q, kt, vt, n, scale, out=o)
 
     stream = torch.cuda.current_stream()
-    g, per_replay, ev = capture(step, "q8_decode")
+    g, per_replay, _ = capture(step)
     for _ in range(args.warmup):
         g.replay()
     torch.cuda.synchronize()
@@ -287,14 +297,22 @@ def run_q8(args, wl, ws, rank):
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.3)
     clocks.mark(True)
-    ms, k_ms = timed_graph(g, args.steps, stream, ev)
-    q_host = [q.cpu().pin_memory() for q, _, _ in layers]
-    o_host = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    ms, _ = timed_graph(g, args.steps, stream)
+    # the step is L launches of the one kernel back to back: its average launch duration is
+    # the step time / L (gaps between launches included, so this understates the kernel)
+    k_ms = ms / L
+    # end to end: every step uploads all layers' q from pinned host memory in one copy, runs
+    # the 40 public-API calls and reads every output back in one copy
+    q_host = torch.stack([q for q, _, _ in layers]).cpu().pin_memory()
+    q_dev = torch.empty_like(q_host, device="cuda")
+    o_dev = torch.empty_like(q_dev)
+    o_host = torch.empty_like(q_host).pin_memory()
 
     def e2e_step():
-        for (q, kt, vt), qh, oh in zip(layers, q_host, o_host):
-            q.copy_(qh, non_blocking=True)
-            oh.copy_(q8_decode_attention(q, kt, vt, n, scale), non_blocking=True)
+        q_dev.copy_(q_host, non_blocking=True)
+        for i, (_, kt, vt) in enumerate(layers):
+            ops.q8_decode_attention(q_dev[i], kt, vt, n, scale, out=o_dev[i])
+        o_host.copy_(o_dev, non_blocking=True)
 
     ge, _, _ = capture(e2e_step)
     for _ in range(max(1, args.warmup)):
@@ -307,8 +325,8 @@ def run_q8(args, wl, ws, rank):
     del g, ge
     return dict(ms=ms, e2e_ms=e2e_ms, kernel_ms=k_ms, launches=per_replay * args.steps,
                 clocks=clocks, bytes=synth.q8_bytes_per_layer(n, B, Hkv) * L * ws,
-                h2d=sum(q.numel() * 2 for q, _, _ in layers),
-                d2h=sum(o.numel() * 2 for o in outs), graph=True)
+                h2d=q_host.numel() * q_host.element_size(),
+                d2h=o_host.numel() * o_host.element_size(), graph=True)
 
 
 # ----------------------------------------------------------------------------------------
@@ -420,9 +438,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="moe_prefill")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="q8_decode only: layers per step (default: the config's 40; fewer "
+                         "for small profiling runs)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.layers and args.workload == "q8_decode":
+        wl["L"] = args.layers
     ws, rank, local = dist_setup()
 
     if args.impl == "reference":
@@ -452,8 +475,10 @@ def main():
         achieved = per_launch / (r["kernel_ms"] * 1e-3) / 1e9
         roof = {"bound": "hbm", "kernel": "q8_decode_kernel", "achieved": achieved,
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                "traffic": None, "peak_source": pk_kind,
-                "algorithmic": f"{per_launch:.0f} B per launch (n x Hkv x 272 B)"}
+                "traffic": profile_traffic("q8_decode_kernel_config4"), "peak_source": pk_kind,
+                "algorithmic": f"{per_launch:.0f} B per launch (n x Hkv x 272 B)",
+                "duration": "graph step time / launches per step (inter-launch gaps included)",
+                "traffic_source": "profiles/q8_decode_kernel_config4.md (ncu, one launch)"}
         dtype = "u8"
     else:
         r = run_moe(args, wl, ws, rank)
@@ -467,9 +492,11 @@ def main():
         peak = pk["bf16_tflops"]
         roof = {"bound": "tensor", "kernel": "experts_gateup", "achieved": achieved,
                 "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak if achieved else None, "traffic": None,
+                "frac": achieved / peak if achieved else None,
+                "traffic": profile_traffic("moe_tc_gateup_config2"),
                 "peak_source": pk_kind,
-                "algorithmic": "2 * 2I * H FLOP per routed pick and shared row"}
+                "algorithmic": "2 * 2I * H FLOP per routed pick and shared row",
+                "traffic_source": "profiles/moe_tc_gateup_config2.md (ncu, one launch)"}
         c = r["counts"]
         wl = dict(wl, max_count=int(c.max()), min_count=int(c.min()),
                   distinct=int((c > 0).sum()))

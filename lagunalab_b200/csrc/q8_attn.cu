@@ -670,11 +670,29 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
 }
 
 // CTAs per (batch, kv head): one CTA per SM is resident (the rings take ~207 KB), so fill the
-// 148 SMs once, each CTA a contiguous range of whole 32-key tiles, with at least one tile per
+// SMs once, each CTA a contiguous range of whole 32-key tiles, with at least one tile per
 // warp. B * Hkv > 74 leaves one CTA per (batch, kv head) (no split merge).
+static int q8_sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return 148;  // no device (host-side size queries): a B200
+  }
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 static void q8_split(int B, int Hkv, int n, int* tpc, int* nsplit) {
   const int BH = B * Hkv;
-  const int SMS = 148;
+  const int SMS = q8_sm_count();
   const int nt = (n + QA_TK - 1) / QA_TK;
   int ns = SMS / BH;
   ns = min(ns, (nt + QA_WARPS - 1) / QA_WARPS);
