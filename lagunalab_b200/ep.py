@@ -66,8 +66,10 @@ class ExpertParallelMoE:
         inds = inds.reshape(-1, self.k)
         w = w.reshape(-1, self.k)
         recv_rows, recv_lid, order, sc, rc = self.dispatch(x2, inds)
+        # expert outputs travel in the input's dtype on every rank (a rank that received no
+        # rows must post a combine exchange of the same element size as the others)
         if recv_rows.shape[0]:
-            y_recv = self.expert_fn(recv_rows, recv_lid)
+            y_recv = self.expert_fn(recv_rows, recv_lid).to(x2.dtype)
         else:
             y_recv = recv_rows.new_empty((0, H))
         y = self.combine(y_recv, order, sc, rc, (x2.shape[0], self.k, H))
