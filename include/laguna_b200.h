@@ -214,6 +214,82 @@ int lg_q8_decode_attention_noalloc(const void* q, int B, int Hq, int Hkv, int D,
                                    const uint32_t* v_q, const void* v_s, const void* v_b,
                                    int cap, int n, float scale, void* out, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Full decoder (laguna_mlx/laguna.py:75-206) around the MoE block and the decode attention.
+ * Rounding follows the MLX graph: each op's output is materialised in bf16.
+ * ------------------------------------------------------------------------------------- */
+
+/*
+ * RMSNorm, nn.RMSNorm / mx.fast.rms_norm (laguna.py:158-160, :189):
+ *   y = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w), statistics in fp32.
+ * With residual != NULL, h = bf16(x + residual) is the decoder's residual stream
+ * (laguna.py:163-164) and is also written to sum_out (may be NULL); else h = x.
+ * x, residual, sum_out, out bf16 [T, H]; w bf16 [H]; H % 8 == 0; 16-byte aligned.
+ */
+int lg_rmsnorm(const void* x, const void* residual, const void* w, int T, int H, float eps,
+               void* sum_out, void* out, void* stream);
+
+/*
+ * 4-bit group-64 dense linear at decode sizes, nn.QuantizedLinear (laguna.py:84-92, :197):
+ *   out = bf16(x . W^T) [+ residual, in bf16], W = scale * code + bias per 64-group.
+ * x bf16 [T, K] (T <= 16), W uint32 [N, K/8] with bf16 scales/biases [N, K/64], residual
+ * and out bf16 [T, N].  K % 64 == 0.  Larger T: dequantize (lg_dequantize_rows) and use a
+ * dense GEMM.
+ */
+int lg_qlinear(const void* x, int T, int K, int N, const uint32_t* w_q, const void* w_s,
+               const void* w_b, int group_size, int bits, const void* residual, void* out,
+               void* stream);
+
+/*
+ * Token embedding, nn.QuantizedEmbedding (laguna.py:174, :183): out[t] = bf16(scale * code
+ * + bias) of row ids[t] (device int32 [T]) of a 4-bit group-64 table [V, H].  An id outside
+ * [0, V) yields a NaN row.
+ */
+int lg_embed(const int32_t* ids, int T, const uint32_t* w_q, const void* w_s, const void* w_b,
+             int V, int H, int group_size, int bits, void* out, void* stream);
+
+/*
+ * Attention prologue, Attention.__call__ (laguna.py:94-106) for one sequence:
+ * from qkvg bf16 [T, Hq*D + 2*Hkv*D + (gate_per_head ? Hq : Hq*D)] (the q, k, v and g
+ * projections of T tokens at positions p = pos + t, pos = *pos_dev if pos_dev else pos_host):
+ *   q_out  bf16 [Hq, T, D]    = rope(bf16(rmsnorm(q_h, qn_w)), p)
+ *   k_cache bf16 [Hkv, cap, D] row p = rope(bf16(rmsnorm(k_h, kn_w)), p)
+ *   v_cache bf16 [Hkv, cap, D] row p = v_h
+ *   gate_out bf16 [T, Hq or Hq*D]     = bf16(softplus(float(g)))
+ * RoPE: non-interleaved pairs (i, i + D/2), inv_freq_i = theta^(-2i/D) (the default rope of
+ * laguna.py:69-72).  D % 64 == 0, D <= 256.  Rows p >= cap are not written (size the cache).
+ */
+int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                 const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                 int pos_host, int gate_per_head, void* q_out, void* k_cache, void* v_cache,
+                 int cap, void* gate_out, void* stream);
+
+/* Workspace bytes for lg_bf16_decode_attention planned for n_plan keys. */
+size_t lg_bf16_decode_workspace_bytes(int B, int Hq, int Hkv, int n_plan);
+
+/*
+ * Single-token attention over a bf16 KV cache: the SDPA branch of Attention.__call__
+ * (laguna.py:102-107) with mlx-lm's KVCache, followed by the output gate (laguna.py:105-106):
+ *   out = bf16(bf16(softmax(q . K[:n]^T * scale) . V[:n]) * gate)   per query head.
+ * q bf16 [B, Hq, 128]; k, v bf16 [B, Hkv, cap, 128]; gate bf16 [B, Hq] (per-head) or NULL;
+ * out bf16 [B, Hq, 128].  n = *n_dev + n_add when n_dev != NULL (a device-side length, for
+ * decode steps that run without the host), else n.  The work split is planned for n_plan
+ * (1 <= n_plan <= cap; an upper bound of n).  Hq % Hkv == 0, Hq / Hkv <= 16.  The workspace's
+ * first 16 KiB hold completion counters that must start zeroed; completed calls leave them so.
+ */
+int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, int D, const void* k,
+                             const void* v, int cap, int n, const int32_t* n_dev, int n_add,
+                             int n_plan, float scale, const void* gate, void* out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Greedy token: ids[t] = argmax of bf16 logits row t of [T, V] (first index among equal
+ * maxima, mx.argmax); if pos != NULL, *pos += inc afterwards (advances a device-side cache
+ * position so consecutive decode steps need no host round trip).
+ */
+int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,
+              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

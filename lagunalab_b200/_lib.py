@@ -43,6 +43,14 @@ SIGNATURES = {
     "lg_q8_decode_fixed_scratch_bytes": (c_size_t, []),
     "lg_q8_decode_attention_noalloc": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, c_float,
                                                P, P]),
+    "lg_rmsnorm": (c_int, [P, P, P, I, I, c_float, P, P, P]),
+    "lg_qlinear": (c_int, [P, I, I, I, P, P, P, I, I, P, P, P]),
+    "lg_embed": (c_int, [P, I, P, P, P, I, I, I, I, P, P]),
+    "lg_attn_prep": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, I, P, P]),
+    "lg_bf16_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
+    "lg_bf16_decode_attention": (c_int, [P, I, I, I, I, P, P, I, I, P, I, I, c_float, P, P, P,
+                                         c_size_t, P]),
+    "lg_argmax": (c_int, [P, I, I, P, P, I, P]),
 }
 
 _lib = None

@@ -1,0 +1,468 @@
+// Decoder-layer kernels around the MoE block and the decode attention, for the full Laguna
+// decoder (laguna_mlx/laguna.py:75-206): RMSNorm with an optional fused residual add, the
+// 4-bit dense linear as a decode-size tensor-core GEMV, the quantized token embedding, the
+// attention prologue (per-head q/k RMSNorm, RoPE, bf16 KV-cache append, softplus output gate)
+// and the greedy argmax. Rounding follows the MLX graph: every op output is materialised in
+// bf16 and the kernels round at the same points.
+#include <math.h>
+
+#include "common.cuh"
+#include "gemv_core.cuh"
+
+namespace lg {
+
+__device__ __forceinline__ uint2 ldg_stream_u2(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
+// ---------------------------------------------------------------------------------------
+// RMSNorm (laguna.py:158-160, :189; mx.fast.rms_norm): y = bf16(bf16(h * rsqrt(mean(h^2) +
+// eps)) * w), fp32 statistics. With a residual, h = bf16(x + residual) is the decoder's
+// residual stream (laguna.py:163-164) and is written out too.
+// ---------------------------------------------------------------------------------------
+constexpr int RN_THREADS = 256;
+
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16* x,
+                                                             const __nv_bfloat16* res,
+                                                             const __nv_bfloat16* w, int H,
+                                                             float eps, __nv_bfloat16* sum_out,
+                                                             __nv_bfloat16* out) {
+  __shared__ float red[RN_THREADS / 32];
+  const int t = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H);
+  const uint4* rr = res ? reinterpret_cast<const uint4*>(res + (size_t)t * H) : nullptr;
+  const int nv = H / 8;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < nv; i += RN_THREADS) {
+    uint4 v = xr[i];
+    if (rr) {
+      const uint4 b = rr[i];
+      uint32_t* pv = &v.x;
+      const uint32_t* pb = &b.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 s = __floats2bfloat162_rn(
+            __uint_as_float(pv[j] << 16) + __uint_as_float(pb[j] << 16),
+            __uint_as_float(pv[j] & 0xffff0000u) + __uint_as_float(pb[j] & 0xffff0000u));
+        pv[j] = *reinterpret_cast<const uint32_t*>(&s);
+      }
+      if (sum_out) reinterpret_cast<uint4*>(sum_out + (size_t)t * H)[i] = v;
+    }
+    const uint32_t* pv = &v.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = __uint_as_float(pv[j] << 16), b = __uint_as_float(pv[j] & 0xffff0000u);
+      ss += a * a + b * b;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < RN_THREADS / 32; ++i) tot += red[i];
+  const float r = 1.0f / sqrtf(tot / (float)H + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  const uint4* src = (rr && sum_out) ? reinterpret_cast<const uint4*>(sum_out + (size_t)t * H)
+                                     : nullptr;
+  for (int i = threadIdx.x; i < nv; i += RN_THREADS) {
+    uint4 v;
+    if (src) {
+      v = src[i];  // this thread wrote it above
+    } else {
+      v = xr[i];
+      if (rr) {
+        const uint4 b = rr[i];
+        uint32_t* pv = &v.x;
+        const uint32_t* pb = &b.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 s = __floats2bfloat162_rn(
+              __uint_as_float(pv[j] << 16) + __uint_as_float(pb[j] << 16),
+              __uint_as_float(pv[j] & 0xffff0000u) + __uint_as_float(pb[j] & 0xffff0000u));
+          pv[j] = *reinterpret_cast<const uint32_t*>(&s);
+        }
+      }
+    }
+    const uint4 wv = wr[i];
+    const uint32_t* pv = &v.x;
+    const uint32_t* pw = &wv.x;
+    uint4 o;
+    uint32_t* po = &o.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = round_bf16(__uint_as_float(pv[j] << 16) * r) * __uint_as_float(pw[j] << 16);
+      const float b = round_bf16(__uint_as_float(pv[j] & 0xffff0000u) * r) *
+                      __uint_as_float(pw[j] & 0xffff0000u);
+      const __nv_bfloat162 s = __floats2bfloat162_rn(a, b);
+      po[j] = *reinterpret_cast<const uint32_t*>(&s);
+    }
+    reinterpret_cast<uint4*>(out + (size_t)t * H)[i] = o;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// 4-bit dense linear at decode sizes (nn.QuantizedLinear, laguna.py:84-92, :197):
+// y[t, n] = sum_k x[t, k] * (scale[n, k/64] * code[n, k] + bias[n, k/64]), fp32 accumulation,
+// one bf16 rounding (quantized_matmul's output), then optionally + residual in bf16.
+// One CTA per 16-row tile of W, 16 warps split the K groups, each warp runs the tensor-core
+// group product of gemv_core.cuh against one or two 8-token tiles.
+// ---------------------------------------------------------------------------------------
+constexpr int QL_WARPS = 16;
+
+struct QlArgs {
+  const __nv_bfloat16* x;  // [T, K]
+  const uint32_t* wq;      // [N, K / 8]
+  const __nv_bfloat16* ws; // [N, K / 64]
+  const __nv_bfloat16* wb;
+  const __nv_bfloat16* res;  // [T, N] or null
+  __nv_bfloat16* out;        // [T, N]
+  int T, K, N;
+};
+
+template <int NTT>
+__global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
+  __shared__ float red[QL_WARPS][32][4 * NTT];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = lane >> 2, c4 = lane & 3;
+  const int m0 = blockIdx.x * 16;
+  const int ra = min(m0 + r, a.N - 1), rb = min(m0 + r + 8, a.N - 1);
+  const int K = a.K, wpr = K / 8, gpr = K / 64;
+  float acc[NTT][4];
+#pragma unroll
+  for (int tt = 0; tt < NTT; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
+#pragma unroll 4
+  for (int gg = warp; gg < gpr; gg += QL_WARPS) {
+    const size_t wo = (size_t)gg * 8 + 2 * c4;
+    const uint2 w0 = ldg_stream_u2(a.wq + (size_t)ra * wpr + wo);
+    const uint2 w8 = ldg_stream_u2(a.wq + (size_t)rb * wpr + wo);
+    const float s0 = bf2f(a.ws[(size_t)ra * gpr + gg]), s8 = bf2f(a.ws[(size_t)rb * gpr + gg]);
+    const float b0 = bf2f(a.wb[(size_t)ra * gpr + gg]), b8 = bf2f(a.wb[(size_t)rb * gpr + gg]);
+#pragma unroll
+    for (int tt = 0; tt < NTT; ++tt) {
+      const int tok = 8 * tt + r;
+      uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
+      if (tok < a.T) {
+        const __nv_bfloat16* xr = a.x + (size_t)tok * K + gg * 64 + 16 * c4;
+        xa0 = *reinterpret_cast<const uint4*>(xr);
+        xa1 = *reinterpret_cast<const uint4*>(xr + 8);
+      }
+      float xs = xsum16(xa0, xa1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+      const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
+      const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      group_mma(d, w0, w8, xa0, xa1);
+      acc[tt][0] += s0 * d[0] + b0 * xs0;
+      acc[tt][1] += s0 * d[1] + b0 * xs1;
+      acc[tt][2] += s8 * d[2] + b8 * xs0;
+      acc[tt][3] += s8 * d[3] + b8 * xs1;
+    }
+  }
+#pragma unroll
+  for (int tt = 0; tt < NTT; ++tt)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[warp][lane][4 * tt + j] = acc[tt][j];
+  __syncthreads();
+  // 32 lanes x 4 NTT values: spread the cross-warp sums over the CTA's threads
+  for (int i = threadIdx.x; i < 32 * 4 * NTT; i += QL_WARPS * 32) {
+    const int l = i / (4 * NTT), q = i % (4 * NTT);
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < QL_WARPS; ++w) v += red[w][l][q];
+    const int lr = l >> 2, lc = l & 3, tt = q / 4, j = q % 4;
+    const int tok = 8 * tt + 2 * lc + (j & 1);
+    const int n = m0 + lr + (j < 2 ? 0 : 8);
+    if (tok < a.T && n < a.N) {
+      float y = round_bf16(v);
+      if (a.res) y += bf2f(a.res[(size_t)tok * a.N + n]);
+      a.out[(size_t)tok * a.N + n] = __float2bfloat16_rn(y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Quantized embedding lookup (nn.QuantizedEmbedding): out[t] = bf16(scale * code + bias) of
+// row ids[t]. An id outside [0, V) gives a NaN row, so a bad id shows in the logits.
+// ---------------------------------------------------------------------------------------
+__global__ void embed_kernel(const int32_t* ids, const uint32_t* wq, const __nv_bfloat16* ws,
+                             const __nv_bfloat16* wb, int V, int H, __nv_bfloat16* out) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  const int wpr = H / 8, gpr = H / 64;
+  for (int i = threadIdx.x; i < wpr; i += blockDim.x) {
+    __align__(16) __nv_bfloat16 o[8];
+    if (ok) {
+      const uint32_t w = wq[(size_t)id * wpr + i];
+      const int g = (8 * i) / 64;
+      const float s = bf2f(ws[(size_t)id * gpr + g]), b = bf2f(wb[(size_t)id * gpr + g]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(s * (float)((w >> (4 * j)) & 15u) + b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + 8 * i) = *reinterpret_cast<uint4*>(o);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Attention prologue (laguna.py:94-104): from the fused projection row
+// [q (Hq*D) | k (Hkv*D) | v (Hkv*D) | g (Hq or Hq*D)] of token t at position p = pos + t:
+//   q = rope(bf16(rmsnorm(q_h, qn_w)), p)  -> q_out [Hq, T, D]
+//   k = rope(bf16(rmsnorm(k_h, kn_w)), p)  -> k_cache [Hkv, cap, D] row p
+//   v                                       -> v_cache row p
+//   gate = bf16(softplus(float(g)))         -> gate_out [T, Hq or Hq*D]
+// RoPE is the default non-interleaved form (pairs i, i + D/2; mx.fast.rope traditional=False)
+// with inv_freq_i = theta^(-2i/D), computed in fp32 with one bf16 rounding.
+// ---------------------------------------------------------------------------------------
+struct PrepArgs {
+  const __nv_bfloat16* qkvg;
+  const __nv_bfloat16* qn_w;
+  const __nv_bfloat16* kn_w;
+  const int* pos_dev;
+  int pos_host, T, Hq, Hkv, D, cap, gate_per_head;
+  float eps, log2_theta;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* gate_out;
+};
+
+// one CTA (D/2 threads) per (token, head slot): slots [0, Hq) q heads, [Hq, Hq+Hkv) k heads,
+// [Hq+Hkv, Hq+2Hkv) v heads
+__global__ void attn_prep_kernel(PrepArgs a) {
+  __shared__ float red[8];
+  const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
+  const int D = a.D, half = D / 2;
+  const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
+  const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
+  const __nv_bfloat16* row = a.qkvg + (size_t)t * row_stride;
+  if (slot >= a.Hq + a.Hkv) {  // v: copy into the cache
+    const int h = slot - a.Hq - a.Hkv;
+    const __nv_bfloat16* src = row + (a.Hq + a.Hkv + h) * D;
+    if (pos < a.cap) {
+      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + pos) * D;
+      dst[i] = src[i];
+      dst[i + half] = src[i + half];
+    }
+    return;
+  }
+  const bool is_q = slot < a.Hq;
+  const int h = is_q ? slot : slot - a.Hq;
+  const __nv_bfloat16* src = row + (is_q ? h : a.Hq + h) * D;
+  const float x0 = bf2f(src[i]), x1 = bf2f(src[i + half]);
+  float ss = x0 * x0 + x1 * x1;
+  ss = warp_sum(ss);
+  if ((i & 31) == 0) red[i >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < (half + 31) / 32; ++w) tot += red[w];
+  const float rn = 1.0f / sqrtf(tot / (float)D + a.eps);
+  const __nv_bfloat16* nw = is_q ? a.qn_w : a.kn_w;
+  const float n0 = round_bf16(round_bf16(x0 * rn) * bf2f(nw[i]));
+  const float n1 = round_bf16(round_bf16(x1 * rn) * bf2f(nw[i + half]));
+  const float inv_freq = exp2f(-(float)(2 * i) / (float)D * a.log2_theta);
+  float sn, cs;
+  sincosf((float)pos * inv_freq, &sn, &cs);
+  const float o0 = n0 * cs - n1 * sn;
+  const float o1 = n0 * sn + n1 * cs;
+  if (is_q) {
+    __nv_bfloat16* dst = a.q_out + ((size_t)h * a.T + t) * D;
+    dst[i] = __float2bfloat16_rn(o0);
+    dst[i + half] = __float2bfloat16_rn(o1);
+    // the output gate of this head (softplus = logaddexp(g, 0), in fp32)
+    const __nv_bfloat16* g = row + (a.Hq + 2 * a.Hkv) * D;
+    auto softplus = [](float v) { return fmaxf(v, 0.f) + log1pf(expf(-fabsf(v))); };
+    if (a.gate_per_head) {
+      if (i == 0)
+        a.gate_out[(size_t)t * a.Hq + h] = __float2bfloat16_rn(softplus(bf2f(g[h])));
+    } else {
+      __nv_bfloat16* go = a.gate_out + (size_t)t * a.Hq * D + (size_t)h * D;
+      go[i] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i])));
+      go[i + half] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i + half])));
+    }
+  } else if (pos < a.cap) {
+    __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + pos) * D;
+    dst[i] = __float2bfloat16_rn(o0);
+    dst[i + half] = __float2bfloat16_rn(o1);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Greedy argmax over bf16 logits (first index among equal maxima); optionally advances a
+// device-side position counter, so a whole decode step can run without the host.
+// ---------------------------------------------------------------------------------------
+constexpr int AM_THREADS = 1024;
+
+__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const __nv_bfloat16* logits, int V,
+                                                            int32_t* ids, int32_t* pos, int inc) {
+  __shared__ float sv[AM_THREADS / 32];
+  __shared__ int si[AM_THREADS / 32];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* row = logits + (size_t)t * V;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += AM_THREADS) {
+    const float v = bf2f(row[i]);
+    if (v > best) {  // NaN never wins
+      best = v;
+      bi = i;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = sv[lane];
+    bi = si[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      ids[t] = bi == 0x7fffffff ? 0 : bi;
+      if (pos && t == 0) pos[0] += inc;
+    }
+  }
+}
+
+}  // namespace lg
+
+using namespace lg;
+
+extern "C" int lg_rmsnorm(const void* x, const void* residual, const void* w, int T, int H,
+                          float eps, void* sum_out, void* out, void* stream) {
+  LG_CHECK_ARG(T >= 0 && H > 0 && H % 8 == 0, "rmsnorm: need H %% 8 == 0 (H=%d, T=%d)", H, T);
+  if (T == 0) return LG_OK;
+  LG_CHECK_ARG(x && w && out, "rmsnorm: NULL pointer");
+  LG_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(out, 16) &&
+                   (!residual || aligned(residual, 16)) && (!sum_out || aligned(sum_out, 16)),
+               "rmsnorm: tensors must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rmsnorm_kernel<<<T, RN_THREADS, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(w), H, eps,
+      residual ? static_cast<__nv_bfloat16*>(sum_out) : nullptr,
+      static_cast<__nv_bfloat16*>(out));
+  LG_LAUNCH_CHECK("rmsnorm");
+  return LG_OK;
+}
+
+extern "C" int lg_qlinear(const void* x, int T, int K, int N, const uint32_t* w_q,
+                          const void* w_s, const void* w_b, int group_size, int bits,
+                          const void* residual, void* out, void* stream) {
+  LG_CHECK_ARG(bits == 4 && group_size == 64, "qlinear: 4-bit group-64 weights only");
+  LG_CHECK_ARG(T >= 0 && T <= 16, "qlinear: decode sizes only (T=%d > 16: dequantize instead)", T);
+  LG_CHECK_ARG(K > 0 && K % 64 == 0 && N > 0, "qlinear: need K %% 64 == 0 (K=%d, N=%d)", K, N);
+  if (T == 0) return LG_OK;
+  LG_CHECK_ARG(x && w_q && w_s && w_b && out, "qlinear: NULL pointer");
+  LG_CHECK_ARG(aligned(x, 16) && aligned(w_q, 8), "qlinear: x 16-byte, weights 8-byte aligned");
+  QlArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.wq = w_q;
+  a.ws = static_cast<const __nv_bfloat16*>(w_s);
+  a.wb = static_cast<const __nv_bfloat16*>(w_b);
+  a.res = static_cast<const __nv_bfloat16*>(residual);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.T = T;
+  a.K = K;
+  a.N = N;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int tiles = (N + 15) / 16;
+  prof_begin("qlinear", st);
+  if (T <= 8)
+    qlinear_kernel<1><<<tiles, QL_WARPS * 32, 0, st>>>(a);
+  else
+    qlinear_kernel<2><<<tiles, QL_WARPS * 32, 0, st>>>(a);
+  prof_end("qlinear", st);
+  LG_LAUNCH_CHECK("qlinear");
+  return LG_OK;
+}
+
+extern "C" int lg_embed(const int32_t* ids, int T, const uint32_t* w_q, const void* w_s,
+                        const void* w_b, int V, int H, int group_size, int bits, void* out,
+                        void* stream) {
+  LG_CHECK_ARG(bits == 4 && group_size == 64, "embed: 4-bit group-64 table only");
+  LG_CHECK_ARG(T >= 0 && V > 0 && H > 0 && H % 64 == 0, "embed: need H %% 64 == 0 (H=%d)", H);
+  if (T == 0) return LG_OK;
+  LG_CHECK_ARG(ids && w_q && w_s && w_b && out && aligned(out, 16), "embed: NULL or misaligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  embed_kernel<<<T, 128, 0, st>>>(ids, w_q, static_cast<const __nv_bfloat16*>(w_s),
+                                  static_cast<const __nv_bfloat16*>(w_b), V, H,
+                                  static_cast<__nv_bfloat16*>(out));
+  LG_LAUNCH_CHECK("embed");
+  return LG_OK;
+}
+
+extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                            const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                            int pos_host, int gate_per_head, void* q_out, void* k_cache,
+                            void* v_cache, int cap, void* gate_out, void* stream) {
+  LG_CHECK_ARG(D % 64 == 0 && D <= 256 && Hq > 0 && Hkv > 0 && T >= 0,
+               "attn_prep: head_dim %d (need a multiple of 64, <= 256)", D);
+  if (T == 0) return LG_OK;
+  LG_CHECK_ARG(qkvg && qn_w && kn_w && q_out && k_cache && v_cache && gate_out,
+               "attn_prep: NULL pointer");
+  LG_CHECK_ARG(pos_dev || (pos_host >= 0 && pos_host + T <= cap),
+               "attn_prep: positions %d..%d beyond the cache capacity %d", pos_host,
+               pos_host + T - 1, cap);
+  PrepArgs a;
+  a.qkvg = static_cast<const __nv_bfloat16*>(qkvg);
+  a.qn_w = static_cast<const __nv_bfloat16*>(qn_w);
+  a.kn_w = static_cast<const __nv_bfloat16*>(kn_w);
+  a.pos_dev = pos_dev;
+  a.pos_host = pos_host;
+  a.T = T;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.cap = cap;
+  a.gate_per_head = gate_per_head;
+  a.eps = eps;
+  a.log2_theta = log2f(rope_theta);
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.gate_out = static_cast<__nv_bfloat16*>(gate_out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid(Hq + 2 * Hkv, T);
+  attn_prep_kernel<<<grid, D / 2, 0, st>>>(a);
+  LG_LAUNCH_CHECK("attn_prep");
+  return LG_OK;
+}
+
+extern "C" int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,
+                         void* stream) {
+  LG_CHECK_ARG(T >= 0 && V > 0, "argmax: bad sizes T=%d V=%d", T, V);
+  if (T == 0) return LG_OK;
+  LG_CHECK_ARG(logits && ids, "argmax: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  argmax_kernel<<<T, AM_THREADS, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), V, ids, pos,
+                                          inc);
+  LG_LAUNCH_CHECK("argmax");
+  return LG_OK;
+}

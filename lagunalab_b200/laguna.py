@@ -1,13 +1,17 @@
-"""Laguna MoE block on B200, with the module surface of laguna_mlx/laguna.py.
+"""Laguna decoder on B200, with the module surface of laguna_mlx/laguna.py.
 
-Same names and call semantics as the reference (laguna.py:18-150): ``ModelArgs`` with its
+Same names and call semantics as the reference (laguna.py:18-241): ``ModelArgs`` with its
 validation, ``MLP(dim, hidden)``, ``SwitchGLU(input_dims, hidden_dims, num_experts)`` called
-as ``switch_mlp(x, indices) -> [..., k, hidden]``, and ``SparseMoeBlock`` with a separate,
-patchable ``route(x) -> (inds, w)`` (hooks and pruning wrap it). Tensors are torch CUDA
-tensors; weights use the MLX packed layout (uint32 words as int32, bf16 scales/biases).
-All arithmetic runs in the sm_100a kernels of ``liblaguna_b200.so``.
+as ``switch_mlp(x, indices) -> [..., k, hidden]``, ``SparseMoeBlock`` with a separate,
+patchable ``route(x) -> (inds, w)`` (hooks and pruning wrap it), ``Attention``,
+``DecoderLayer``, ``LagunaModel`` and ``Model`` (``layers``, ``make_cache``, ``sanitize``,
+``quant_predicate``). Tensors are torch CUDA tensors; weights use the MLX packed layout
+(uint32 words as int32, bf16 scales/biases). All arithmetic runs in the sm_100a kernels of
+``liblaguna_b200.so`` (prefill-sized dense linears dequantize to bf16 for a dense GEMM, and
+prefill attention uses torch's fused SDPA).
 """
 import inspect
+import math
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional
 
@@ -92,6 +96,12 @@ class QuantizedLinear:
 
     def dequantize(self):
         return ops.dequantize(self.weight, self.scales, self.biases, self.group_size, self.bits)
+
+    def __call__(self, x, residual=None):
+        """nn.QuantizedLinear: x @ W^T (bf16 out), optionally + residual (bf16)."""
+        if self.bits != 4:
+            raise ValueError("only 4-bit linears are callable (the 8-bit router has its own kernel)")
+        return ops.qlinear(x, self.mat, residual, self.group_size, self.bits)
 
 
 class MLP:
@@ -213,3 +223,275 @@ def _fused_experts(sw):
         return sw
     resident = getattr(sw, "resident_glu", None)
     return resident() if callable(resident) else None
+
+
+# ----------------------------------------------------------------------------------------
+# The rest of the decoder (laguna.py:75-113, :153-241)
+# ----------------------------------------------------------------------------------------
+
+class RMSNorm:
+    """nn.RMSNorm (laguna.py:92-93, :160-161, :178): bf16 weight [dims]."""
+
+    def __init__(self, dims, eps=1e-5, weight=None, device="cuda"):
+        self.eps = eps
+        self.weight = weight if weight is not None else torch.ones(dims, dtype=torch.bfloat16,
+                                                                    device=device)
+
+    def __call__(self, x):
+        return ops.rmsnorm(x, self.weight, self.eps)
+
+
+class QuantizedEmbedding(QuantizedLinear):
+    """nn.QuantizedEmbedding (laguna.py:174 after nn.quantize): 4-bit table [V, H]."""
+
+    def __call__(self, ids):
+        return ops.embed(ids, self.mat, self.group_size, self.bits)
+
+    def as_linear(self, x):
+        return ops.qlinear(x, self.mat, None, self.group_size, self.bits)
+
+
+class KVCache:
+    """mlx-lm KVCache surface with bf16 keys/values [B, Hkv, cap, D]: ``offset`` rows are
+    valid; capacity grows in 256-row steps (``capacity`` preallocates)."""
+    step = 256
+
+    def __init__(self, capacity=0):
+        self.keys = self.values = None
+        self.offset = 0
+        self.capacity_hint = capacity
+
+    def reserve(self, B, Hkv, D, T, device):
+        need = self.offset + T
+        if self.keys is None or self.keys.shape[2] < need:
+            cap = max(self.capacity_hint, (need + self.step - 1) // self.step * self.step)
+            k = torch.zeros(B, Hkv, cap, D, dtype=torch.bfloat16, device=device)
+            v = torch.zeros_like(k)
+            if self.keys is not None and self.offset:
+                k[:, :, :self.offset] = self.keys[:, :, :self.offset]
+                v[:, :, :self.offset] = self.values[:, :, :self.offset]
+            self.keys, self.values = k, v
+
+    def update_and_fetch(self, keys, values):
+        B, Hkv, T, D = keys.shape
+        self.reserve(B, Hkv, D, T, keys.device)
+        self.keys[:, :, self.offset:self.offset + T] = keys
+        self.values[:, :, self.offset:self.offset + T] = values
+        self.offset += T
+        return self.keys[:, :, :self.offset], self.values[:, :, :self.offset]
+
+    @property
+    def state(self):
+        if self.keys is None:
+            return None, None
+        return self.keys[:, :, :self.offset], self.values[:, :, :self.offset]
+
+    def is_trimmable(self):
+        return True
+
+    def trim(self, n):
+        n = min(self.offset, n)
+        self.offset -= n
+        return n
+
+    def empty(self):
+        return self.keys is None
+
+    @property
+    def nbytes(self):
+        return 0 if self.keys is None else 2 * self.keys.numel() * self.keys.element_size()
+
+
+def _concat_rows(mats):
+    """Row-concatenate MLX-layout matrices (words, scales, biases) with the same K."""
+    return tuple(torch.cat([m[i] for m in mats], dim=0).contiguous() for i in range(3))
+
+
+class Attention:
+    """laguna.py:75-107: q/k/v/o/g projections (4-bit), per-head q/k RMSNorm, default RoPE,
+    softplus output gate (per head or per element), GQA. The four input projections are
+    stored as one row-concatenated matrix (one GEMV per token); ``q_proj``..``g_proj`` are
+    row views of it."""
+
+    def __init__(self, args, layer_idx, q_proj, k_proj, v_proj, o_proj, g_proj, q_norm=None,
+                 k_norm=None):
+        self.n_heads = args.num_attention_heads_per_layer[layer_idx]
+        self.n_kv_heads = args.num_key_value_heads
+        self.head_dim = hd = args.head_dim
+        self.scale = hd ** -0.5
+        self.per_head_gate = args.gating == "per-head"
+        lt = args.layer_types[layer_idx]
+        if lt != "full_attention":
+            raise NotImplementedError("sliding-window layers are not supported on this path")
+        rp = args.rope_for(lt)
+        if rp.get("rope_type", "default") != "default" or rp.get("partial_rotary_factor", 1.0) != 1.0:
+            raise NotImplementedError("only the default full-rotary RoPE is supported")
+        self.rope_theta = float(rp["rope_theta"])
+        self.eps = args.rms_norm_eps
+        dev = q_proj.weight.device
+        self.q_norm = q_norm or RMSNorm(hd, args.rms_norm_eps, device=dev)
+        self.k_norm = k_norm or RMSNorm(hd, args.rms_norm_eps, device=dev)
+        mats = [q_proj.mat, k_proj.mat, v_proj.mat, g_proj.mat]
+        fused = QuantizedLinear(*_concat_rows(mats), q_proj.group_size, q_proj.bits)
+        self._qkvg = fused
+        rows, r0 = [m[0].shape[0] for m in mats], 0
+        views = []
+        for n in rows:
+            views.append(QuantizedLinear(fused.weight[r0:r0 + n], fused.scales[r0:r0 + n],
+                                         fused.biases[r0:r0 + n], q_proj.group_size, q_proj.bits))
+            r0 += n
+        self.q_proj, self.k_proj, self.v_proj, self.g_proj = views
+        self.o_proj = o_proj
+
+    def __call__(self, x, mask=None, cache=None, residual=None):
+        B, L, H = x.shape
+        if B != 1:
+            raise NotImplementedError("batch size 1 only on this path")
+        Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
+        qkvg = self._qkvg(x.reshape(L, H))
+        if cache is None:
+            cache = KVCache()
+        cache.reserve(1, Hkv, D, L, x.device)
+        pos = cache.offset
+        q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                self.eps, self.rope_theta, cache.keys[0], cache.values[0],
+                                pos=pos, gate_per_head=self.per_head_gate)
+        cache.offset += L
+        if L == 1:
+            o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, pos + 1,
+                                          self.scale,
+                                          gate=gate if self.per_head_gate else None)
+            o = o.view(1, Hq * D)
+            if not self.per_head_gate:
+                o = o * gate.view(1, Hq * D)
+        else:
+            k = cache.keys[:, :, :pos + L]
+            v = cache.values[:, :, :pos + L]
+            mask_ = None
+            if pos:
+                qp = torch.arange(L, device=x.device)[:, None] + pos
+                mask_ = torch.arange(pos + L, device=x.device)[None, :] <= qp
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q.unsqueeze(0), k, v, attn_mask=mask_, is_causal=mask_ is None, scale=self.scale,
+                enable_gqa=True)[0].transpose(0, 1)  # [L, Hq, D]
+            g = gate[..., None] if self.per_head_gate else gate.view(L, Hq, D)
+            o = (o * g).reshape(L, Hq * D)
+        out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
+        return out.reshape(B, L, H)
+
+
+class DecoderLayer:
+    """laguna.py:153-166: pre-norm attention and MLP (dense in ``mlp_only_layers``, MoE
+    otherwise) with residual adds."""
+
+    def __init__(self, args, layer_idx, self_attn, mlp, input_layernorm=None,
+                 post_attention_layernorm=None):
+        self.self_attn = self_attn
+        self.mlp = mlp
+        dev = self_attn.o_proj.weight.device
+        self.input_layernorm = input_layernorm or RMSNorm(args.hidden_size, args.rms_norm_eps,
+                                                          device=dev)
+        self.post_attention_layernorm = post_attention_layernorm or RMSNorm(
+            args.hidden_size, args.rms_norm_eps, device=dev)
+
+    def __call__(self, x, mask=None, cache=None):
+        h = self.self_attn(self.input_layernorm(x), mask, cache, residual=x)
+        return h + self.mlp(self.post_attention_layernorm(h))  # bf16 add, one rounding
+
+
+class LagunaModel:
+    """laguna.py:169-193. The layer loop fuses each residual add into the next RMSNorm (and
+    the attention residual into the o_proj GEMV epilogue)."""
+
+    def __init__(self, args, embed_tokens, layers, norm=None):
+        self.args = args
+        self.embed_tokens = embed_tokens
+        self.layers = layers
+        self.norm = norm or RMSNorm(args.hidden_size, args.rms_norm_eps,
+                                    device=embed_tokens.weight.device)
+        self.layer_types = args.layer_types
+
+    def __call__(self, inputs, cache=None):
+        if inputs.dim() == 1:
+            inputs = inputs[None]
+        x = self.embed_tokens(inputs)
+        if cache is None:
+            cache = [None] * len(self.layers)
+        xn = self.layers[0].input_layernorm(x)
+        for i, (layer, c) in enumerate(zip(self.layers, cache)):
+            h = layer.self_attn(xn, None, c, residual=x)
+            m = layer.mlp(layer.post_attention_layernorm(h))
+            nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else self.norm
+            x, xn = ops.rmsnorm(m, nxt.weight, nxt.eps, residual=h)
+        return xn
+
+
+class Model:
+    """laguna.py:196-241: ``model`` (LagunaModel) + untied ``lm_head``."""
+
+    def __init__(self, args, model, lm_head):
+        self.args = args
+        self.model_type = args.model_type
+        self.model = model
+        self.lm_head = lm_head
+
+    def __call__(self, inputs, cache=None):
+        return self.lm_head(self.model(inputs, cache))
+
+    def last_logits(self, inputs, cache=None):
+        """Logits of the last position only (what generation needs after a prefill)."""
+        h = self.model(inputs, cache)
+        return self.lm_head(h[:, -1:])
+
+    @property
+    def layers(self):
+        return self.model.layers
+
+    def make_cache(self, capacity=0):
+        for lt in self.args.layer_types:
+            if lt == "sliding_attention":
+                raise NotImplementedError("sliding-window layers are not supported on this path")
+        return [KVCache(capacity) for _ in self.args.layer_types]
+
+    def sanitize(self, weights):
+        """laguna.py:216-228 on a dict of tensors: per-expert weights stacked into
+        ``switch_mlp``, the router bias moved to ``mlp.e_score_correction_bias``."""
+        E = self.args.num_experts
+        for l in range(self.args.num_hidden_layers):
+            p = f"model.layers.{l}.mlp"
+            if f"{p}.experts.0.gate_proj.weight" in weights:
+                for n in ("gate_proj", "up_proj", "down_proj"):
+                    weights[f"{p}.switch_mlp.{n}.weight"] = torch.stack(
+                        [weights.pop(f"{p}.experts.{e}.{n}.weight") for e in range(E)])
+            bias = weights.pop(f"{p}.experts.e_score_correction_bias", None)
+            if bias is not None:
+                weights[f"{p}.e_score_correction_bias"] = bias
+        return weights
+
+    def cast_predicate(self, key):
+        return "e_score_correction_bias" not in key
+
+    @property
+    def quant_predicate(self):
+        def predicate(path, _):
+            if path.endswith("mlp.gate"):
+                return {"group_size": 64, "bits": 8}
+            return True
+
+        return predicate
+
+
+def generate(model, prompt, max_tokens, cache=None):
+    """Greedy decoding: prefill ``prompt`` (device int tensor [L]), then ``max_tokens`` steps;
+    returns the generated ids (list of int)."""
+    if cache is None:
+        cache = model.make_cache()
+    ids = prompt.to(torch.int32).reshape(1, -1)
+    logits = model.last_logits(ids, cache)
+    out = []
+    tok = ops.argmax(logits.reshape(1, -1))
+    for _ in range(max_tokens):
+        out.append(tok)
+        logits = model.last_logits(tok.view(1, 1), cache)
+        tok = ops.argmax(logits.reshape(1, -1))
+    return [int(t) for t in torch.cat(out).tolist()]

@@ -266,3 +266,109 @@ def q8_decode_attention(q, keys, values, n, scale, out=None):
               _p(vq), _p(vs), _p(vb), cap, int(n), float(scale), _p(out), _p(ws), ws.numel(),
               _stream(dev))
     return out
+
+
+# ----------------------------------------------------------------------------------------
+# Full-decoder ops (laguna.py:75-206)
+# ----------------------------------------------------------------------------------------
+
+def rmsnorm(x, w, eps, residual=None, sum_out=None):
+    """RMSNorm over the last dim (bf16). With ``residual``, normalises h = x + residual and
+    returns (h, norm(h)); else returns norm(x)."""
+    H = x.shape[-1]
+    x2 = _c(x, torch.bfloat16).reshape(-1, H)
+    w = _c(w, torch.bfloat16)
+    out = torch.empty_like(x2)
+    h = None
+    if residual is not None:
+        residual = _c(residual, torch.bfloat16).reshape(-1, H)
+        h = sum_out if sum_out is not None else torch.empty_like(x2)
+    _lib.call("lg_rmsnorm", _p(x2), _p(residual), _p(w), x2.shape[0], H, float(eps), _p(h),
+              _p(out), _stream(x2.device))
+    if residual is not None:
+        return h.reshape(x.shape), out.reshape(x.shape)
+    return out.reshape(x.shape)
+
+
+def qlinear(x, mat, residual=None, group_size=64, bits=4, out=None):
+    """x [..., K] bf16 @ W^T for an MLX 4-bit [N, K] matrix -> [..., N] bf16 (+ residual).
+    Decode sizes (<= 16 rows) run the tensor-core GEMV; larger inputs dequantize W to bf16
+    and use a dense GEMM (fp32 accumulate, one bf16 rounding)."""
+    q, s, b = _qm(mat)
+    K = x.shape[-1]
+    N = q.shape[0]
+    x2 = _c(x, torch.bfloat16).reshape(-1, K)
+    T = x2.shape[0]
+    if T > 16:
+        w = dequantize(q, s, b, group_size, bits)
+        y = x2 @ w.t()
+        if residual is not None:
+            y = y + _c(residual, torch.bfloat16).reshape(-1, N)
+        if out is not None:
+            out.reshape(-1, N).copy_(y)
+            return out
+        return y.reshape(*x.shape[:-1], N)
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    res = None if residual is None else _c(residual, torch.bfloat16)
+    _lib.call("lg_qlinear", _p(x2), T, K, N, _p(q), _p(s), _p(b), group_size, bits, _p(res),
+              _p(out), _stream(x2.device))
+    return out
+
+
+def embed(ids, mat, group_size=64, bits=4):
+    """Quantized embedding rows for device int32 ids [...] -> [..., H] bf16."""
+    q, s, b = _qm(mat)
+    ids = _c(ids.to(torch.int32) if ids.dtype != torch.int32 else ids)
+    V, H = q.shape[0], q.shape[1] * 32 // bits
+    out = torch.empty(*ids.shape, H, dtype=torch.bfloat16, device=ids.device)
+    _lib.call("lg_embed", _p(ids), ids.numel(), _p(q), _p(s), _p(b), V, H, group_size, bits,
+              _p(out), _stream(ids.device))
+    return out
+
+
+def attn_prep(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos=0, pos_dev=None,
+              gate_per_head=True):
+    """From fused q|k|v|g projections [T, .] write k, v rows into the caches [Hkv, cap, D] at
+    positions pos + t and return (q [Hq, T, D] normed + roped, gate [T, Hq or Hq*D])."""
+    qkvg = _c(qkvg, torch.bfloat16)
+    T = qkvg.shape[0]
+    cap = k_cache.shape[-2]
+    q = torch.empty(Hq, T, D, dtype=torch.bfloat16, device=qkvg.device)
+    gate = torch.empty(T, Hq if gate_per_head else Hq * D, dtype=torch.bfloat16, device=qkvg.device)
+    _lib.call("lg_attn_prep", _p(qkvg), T, Hq, Hkv, D, _p(_c(qn_w)), _p(_c(kn_w)), float(eps),
+              float(theta), _p(pos_dev), int(pos), int(bool(gate_per_head)), _p(q), _p(k_cache),
+              _p(v_cache), cap, _p(gate), _stream(qkvg.device))
+    return q, gate
+
+
+def bf16_decode_attention(q, k_cache, v_cache, n, scale, gate=None, n_dev=None, n_add=0,
+                          n_plan=None, out=None):
+    """Single-token attention over a bf16 cache. q [B, Hq, D]; caches [B, Hkv, cap, D];
+    n valid keys (or n_dev[0] + n_add on the device); gate [B, Hq] per-head or None.
+    Returns out [B, Hq, D] bf16 (gated)."""
+    q = _c(q, torch.bfloat16)
+    B, Hq, D = q.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    n_plan = cap if n_plan is None else int(n_plan)
+    nb = _lib.lib().lg_bf16_decode_workspace_bytes(B, Hq, Hkv, n_plan)
+    ws = workspace(q.device, "bf16_attn", nb, zero=True)
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.call("lg_bf16_decode_attention", _p(q), B, Hq, Hkv, D, _p(k_cache), _p(v_cache), cap,
+              int(n), _p(n_dev), int(n_add), n_plan, float(scale), _p(_c(gate)), _p(out),
+              _p(ws), ws.numel(), _stream(q.device))
+    return out
+
+
+def argmax(logits, ids=None, pos=None, inc=1):
+    """Greedy token per row of bf16 logits [T, V] into int32 ids [T]; optionally advances the
+    device position counter ``pos`` by ``inc``."""
+    logits = _c(logits, torch.bfloat16)
+    V = logits.shape[-1]
+    l2 = logits.reshape(-1, V)
+    if ids is None:
+        ids = torch.empty(l2.shape[0], dtype=torch.int32, device=logits.device)
+    _lib.call("lg_argmax", _p(l2), l2.shape[0], V, _p(ids), _p(pos), int(inc),
+              _stream(logits.device))
+    return ids

@@ -17,6 +17,10 @@ Cases:
                   intermediate 32, shared 32, routed scale 2.5), 10 tokens.
 * ``moe_mid``     Laguna-proportioned: hidden 128, 32 experts, top-8,
                   intermediate 32, shared 32, routed scale 1.0, 16 tokens.
+* ``model_tiny``  the whole ``LagunaForCausalLM`` (3 layers: layer 0 dense, 1-2 MoE; hidden
+                  64, 4 query / 2 kv heads of 32, per-head gate, RoPE theta 1e4, 8 experts
+                  top-2, vocab 96), fp32, 12 tokens; stores the state dict under its own
+                  parameter names and the logits of every position.
 """
 import copy
 import sys
@@ -74,7 +78,40 @@ def main(ref_root):
         print(name, "written", out.shape)
 
 
+def model_tiny(ref_root):
+    sys.path.insert(0, str(ref_root))
+    from tests.reference.configuration_laguna import LagunaConfig
+    from tests.reference.modeling_laguna import LagunaForCausalLM
+
+    torch.manual_seed(2)
+    cfg = LagunaConfig(vocab_size=96, hidden_size=64, intermediate_size=128, num_hidden_layers=3,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+                       gating="per-head", num_experts=8, num_experts_per_tok=2,
+                       moe_intermediate_size=32, shared_expert_intermediate_size=32,
+                       mlp_only_layers=[0], moe_routed_scaling_factor=2.5, norm_topk_prob=True,
+                       rope_parameters={"rope_type": "default", "rope_theta": 10000.0},
+                       rms_norm_eps=1e-6, tie_word_embeddings=False, max_position_embeddings=128)
+    cfg._attn_implementation = "eager"
+    model = LagunaForCausalLM(cfg).float().eval()
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("norm.weight"):
+                p.copy_(1.0 + 0.1 * torch.randn_like(p))
+            else:
+                p.copy_(0.08 * torch.randn_like(p))
+        for name, b in model.named_buffers():
+            if name.endswith("e_score_correction_bias"):
+                b.copy_(0.3 * torch.randn_like(b))
+        ids = torch.randint(0, 96, (1, 12))
+        logits = model(input_ids=ids, use_cache=False).logits[0]
+    state = {k: v.detach().float().numpy() for k, v in model.state_dict().items()}
+    np.savez_compressed(OUT / "model_tiny.npz", ids=ids[0].numpy(), ref_logits=logits.numpy(),
+                        **{"w." + k: v for k, v in state.items()})
+    print("model_tiny written", logits.shape)
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: make_golden.py <lagunaLab source root>")
     main(sys.argv[1])
+    model_tiny(sys.argv[1])
