@@ -1,13 +1,15 @@
 """Benchmark of the Laguna MoE block / q8 decode attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_prefill|moe_decode|q8_decode]
+                    [--workload moe_prefill|moe_decode|q8_decode|decode]
 
 Prints ONE JSON line on rank 0. Default workload: one SparseMoeBlock
 forward (router + routed experts + shared expert + combine) on T = 4096 tokens, 128 experts,
 top-8, hidden 2048, intermediate 1024, 4-bit g64 weights, Zipf-skewed routing; metric
 "MoE-layer tokens/s". ``q8_decode`` is config 4 (40 layers of fused 8-bit KV decode attention
-at 82,671 keys, metric HBM GB/s); ``moe_decode`` is config 1 (T = 16).
+at 82,671 keys, metric HBM GB/s); ``moe_decode`` is config 1 (T = 16); ``decode`` is config 3
+(the whole 40-layer decoder, bs1 greedy decode after an 8,192-token prefill, tokens/s; each
+step one CUDA-graph replay of the model).
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and cuda synchronize, timed with
 CUDA events on the launching stream; the max over ranks is reported. Inputs are resident in
@@ -39,6 +41,10 @@ WORKLOADS = {
     "moe_prefill": dict(T=4096, E=128, k=8, H=2048, I=1024, I_sh=1024, zipf=True, scale=1.0),
     "moe_decode": dict(T=16, E=128, k=8, H=2048, I=1024, I_sh=1024, zipf=False, scale=2.5),
     "q8_decode": dict(L=40, n=82671, B=1, Hq=32, Hkv=4),
+    # the 50%-pruned decoder, bs1 greedy decode after an 8,192-token prefill
+    "decode": dict(prefill=8192, new=256, seed=1, vocab=100352, hidden=2048, layers=40, heads=32,
+                   kv_heads=4, head_dim=128, experts=64, top_k=8, moe_inter=1024,
+                   shared_inter=1024, dense_inter=8192, rope_theta=1e6, kv="bf16"),
 }
 
 
@@ -329,6 +335,115 @@ def run_q8(args, wl, ws, rank):
                 d2h=o_host.numel() * o_host.element_size(), graph=True)
 
 
+def decode_model(wl):
+    from lagunalab_b200 import synth
+    a = synth.decoder_args(vocab=wl["vocab"], hidden=wl["hidden"], layers=wl["layers"],
+                           heads=wl["heads"], kv_heads=wl["kv_heads"], head_dim=wl["head_dim"],
+                           experts=wl["experts"], top_k=wl["top_k"], moe_inter=wl["moe_inter"],
+                           shared_inter=wl["shared_inter"], dense_inter=wl["dense_inter"],
+                           rope_theta=wl["rope_theta"])
+    return a, synth.decoder(a, seed=wl["seed"])
+
+
+def decode_bytes_per_token(model, ctx):
+    """HBM bytes one decode step must read: every dense weight of the step (attention,
+    router, shared expert, dense layer 0, lm_head), the top-k routed experts of each MoE
+    layer, one embedding row, and the bf16 K/V rows of ctx keys per layer."""
+    from lagunalab_b200 import laguna
+    nb = lambda m: sum(t.numel() * t.element_size() for t in m.mat)
+    a = model.args
+    total = sum(nb(x) for x in (model.lm_head,)) + nb(model.model.embed_tokens) // a.vocab_size
+    for L in model.layers:
+        at = L.self_attn
+        total += nb(at._qkvg) + nb(at.o_proj)
+        total += 2 * a.num_key_value_heads * ctx * a.head_dim * 2
+        m = L.mlp
+        if isinstance(m, laguna.MLP):
+            total += sum(nb(p) for p in (m.gate_proj, m.up_proj, m.down_proj))
+        else:
+            total += nb(m.gate) + sum(nb(p) for p in (m.shared_expert.gate_proj,
+                                                       m.shared_expert.up_proj,
+                                                       m.shared_expert.down_proj))
+            per_expert = sum(nb(p) for p in (m.switch_mlp.gate_proj, m.switch_mlp.up_proj,
+                                             m.switch_mlp.down_proj)) // a.num_experts
+            total += a.num_experts_per_tok * per_expert
+    return total
+
+
+def run_decode(args, wl, ws, rank):
+    """prefill wl["prefill"] uniform-random ids (seed 1), then greedy decode
+    one token per step, each step one replay of a CUDA graph of the whole model (token id and
+    cache position stay on the device)."""
+    from lagunalab_b200 import laguna, ops
+    margs, model = decode_model(wl)
+    V = margs.vocab_size
+    g = torch.Generator().manual_seed(wl["seed"])
+    prompt = torch.randint(0, V, (wl["prefill"],), generator=g).to(torch.int32).cuda()
+    n_steps = 1 + args.warmup + args.steps + 1 + max(1, args.warmup) + args.steps
+    cap = (wl["prefill"] + n_steps + 255) // 256 * 256
+    cache = model.make_cache(capacity=cap)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    logits = model.last_logits(prompt.view(1, -1), cache)
+    e1.record(stream)
+    tok = ops.argmax(logits.view(1, -1))
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    n0 = _lib_launches()
+    dg = laguna.DecodeGraph(model, cache, tok)  # one eager step, then the capture
+    per_replay = _lib_launches() - n0
+    per_replay //= 2  # the eager step and the capture each issue the step's launches once
+    for _ in range(args.warmup):
+        dg.step()
+    torch.cuda.synchronize()
+    ctx0 = dg.position()
+    clocks = ClockSampler(torch.cuda.current_device())
+    time.sleep(0.3)
+    clocks.mark(True)
+    ms, _ = timed_graph(dg.graph, args.steps, stream)
+    dg.steps += args.steps
+    ctx1 = dg.position()
+    # end to end: every step uploads the input token from pinned host memory, runs the step
+    # and reads the generated token back to the host, which feeds it to the next step
+    tok_in = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    tok_out.copy_(dg.tok.cpu())
+    ge = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ge):
+        dg.tok.copy_(tok_in, non_blocking=True)
+        dg._body()
+        tok_out.copy_(dg.tok, non_blocking=True)
+
+    def e2e_step():
+        tok_in[0] = tok_out[0]
+        ge.replay()
+        torch.cuda.synchronize()
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    t0 = time.perf_counter()
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = s0.elapsed_time(s1) / args.steps
+    clocks.mark(False)
+    ctx = (ctx0 + ctx1) / 2
+    del ge
+    return dict(ms=ms, e2e_ms=e2e_ms, launches=per_replay * args.steps, clocks=clocks,
+                bytes=decode_bytes_per_token(model, ctx), ctx=(ctx0, ctx1), prefill_ms=prefill_ms,
+                h2d=4, d2h=4)
+
+
+def _lib_launches():
+    from lagunalab_b200 import _lib
+    return _lib.lib().lg_launch_count()
+
+
 # ----------------------------------------------------------------------------------------
 # CPU baseline (the oracle restatement timed on the host cores; rank 0 only)
 # ----------------------------------------------------------------------------------------
@@ -428,6 +543,68 @@ def cpu_q8(wl, steps, warmup, sample_layers=1):
                        f"(oracle restatement: dequantize + fp32 softmax)")
 
 
+def cpu_decode(wl, steps, warmup):
+    """The oracle's decode step on a bounded sample: one MoE layer (attention over the
+    prefill's context + MoE block) and the lm_head, on the config-3 weights, scaled to the
+    whole model: seconds/token = layers x t(layer) + t(lm_head)."""
+    from oracle import model_ref, moe_ref
+    from lagunalab_b200 import synth
+    nt = cpu_threads()
+    torch.set_num_threads(nt)
+    a = synth.decoder_args(vocab=wl["vocab"], hidden=wl["hidden"], layers=2, heads=wl["heads"],
+                           kv_heads=wl["kv_heads"], head_dim=wl["head_dim"],
+                           experts=wl["experts"], top_k=wl["top_k"], moe_inter=wl["moe_inter"],
+                           shared_inter=wl["shared_inter"], dense_inter=wl["dense_inter"],
+                           rope_theta=wl["rope_theta"])
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    model = synth.decoder(a, seed=wl["seed"], device=dev)
+    W = synth.oracle_weights(model)
+    oa = synth.oracle_args(a)
+    L = W["layers"][1]  # a MoE layer
+    ctx = wl["prefill"]
+    g = torch.Generator().manual_seed(0)
+    kc = torch.randn(a.num_key_value_heads, ctx, a.head_dim, generator=g).to(torch.bfloat16).float()
+    vc = torch.randn(a.num_key_value_heads, ctx, a.head_dim, generator=g).to(torch.bfloat16).float()
+    x = torch.randn(1, a.hidden_size, generator=g).to(torch.bfloat16).float()
+    del model
+
+    class _C:  # a cache already holding ctx rows
+        offset = ctx
+        k = [None, kc]
+        v = [None, vc]
+
+        def update(self, i, k, v):
+            return torch.cat([self.k[i], k], 1), torch.cat([self.v[i], v], 1)
+
+    def layer():
+        hn = model_ref.rmsnorm(x, L["in_norm"], oa["eps"])
+        a_ = model_ref._attention(L, hn, _C(), 1, oa, ctx, model_ref._qlin)
+        h = (x + a_).to(torch.bfloat16).float()
+        m = L["mlp"][1]
+        y, _, _ = moe_ref.moe_block(model_ref.rmsnorm(h, L["post_norm"], oa["eps"]), m["gate"],
+                                    m["bias"], m["experts"], m["shared"], oa["k"],
+                                    oa["routed_scale"], oa["norm_topk_prob"])
+        return y
+
+    def head():
+        return moe_ref.qlinear(model_ref.rmsnorm(x, W["norm"], oa["eps"]), W["lm_head"])
+
+    for _ in range(warmup):
+        layer()
+    tl = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        layer()
+        tl.append(time.perf_counter() - t0)
+    t0 = time.perf_counter()
+    head()
+    th = time.perf_counter() - t0
+    sec = wl["layers"] * statistics.median(tl) + th
+    return dict(value=1.0 / sec, unit="tokens/s", cores=nt, kind="port",
+                sample=f"1 MoE layer at {ctx} keys ({steps} timed) + the lm_head once, "
+                       f"scaled to {wl['layers']} layers (oracle restatement)")
+
+
 # ----------------------------------------------------------------------------------------
 
 def main():
@@ -450,8 +627,12 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            ref = (cpu_q8(wl, args.steps, args.warmup) if args.workload == "q8_decode"
-                   else cpu_moe(wl, args.steps, args.warmup))
+            if args.workload == "q8_decode":
+                ref = cpu_q8(wl, args.steps, args.warmup)
+            elif args.workload == "decode":
+                ref = cpu_decode(wl, min(args.steps, 5), 1)
+            else:
+                ref = cpu_moe(wl, args.steps, args.warmup)
             metric, unit = metric_unit(args.workload)
             print(json.dumps({
                 "impl": "reference", "metric": metric, "value": ref["value"], "unit": unit,
@@ -467,7 +648,20 @@ def main():
         return
 
     pk, pk_kind = peaks()
-    if args.workload == "q8_decode":
+    if args.workload == "decode":
+        r = run_decode(args, wl, ws, rank)
+        value = 1000.0 / r["ms"]
+        e2e = 1000.0 / r["e2e_ms"]
+        achieved = r["bytes"] / (r["ms"] * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "whole decode step (every kernel of one token)",
+                "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk_kind,
+                "algorithmic": f"{r['bytes']:.0f} B per token (weights read by one step, top-k "
+                               f"experts, bf16 K/V at mean context {sum(r['ctx']) / 2:.0f})",
+                "duration": "graph step time (one replay per token)"}
+        wl = dict(wl, prefill_ms=r["prefill_ms"], context=list(r["ctx"]))
+        dtype = "bf16"
+    elif args.workload == "q8_decode":
         r = run_q8(args, wl, ws, rank)
         value = r["bytes"] / (r["ms"] * 1e-3) / 1e9
         e2e = r["bytes"] / (r["e2e_ms"] * 1e-3) / 1e9
@@ -514,7 +708,8 @@ def main():
         "clocks": r["clocks"].result(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else cpu_moe(wl, 5, 1))
+        cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else
+              cpu_decode(wl, 3, 1) if args.workload == "decode" else cpu_moe(wl, 5, 1))
         line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -522,6 +717,8 @@ def main():
 
 
 def metric_unit(workload):
+    if workload == "decode":
+        return "bs1 decode tok/s @8k ctx (config 3, bf16 KV)", "tokens/s"
     if workload == "q8_decode":
         return "q8 decode attention HBM GB/s (40 layers @82,671 ctx)", "GB/s"
     if workload == "moe_decode":
@@ -532,11 +729,16 @@ def metric_unit(workload):
 def config(args, wl, ws):
     c = {"workload": args.workload, **{k: v for k, v in wl.items()}}
     c["l2"] = "inputs larger than L2 (126 MB): weights/KV streamed from HBM each step"
+    if args.workload == "decode":
+        c["launch"] = ("prefill through the module API, then one CUDA-graph replay per decoded "
+                       "token (token id and cache position kept on the device); e2e feeds each "
+                       "token through pinned host memory and synchronises every step")
+        c["weights"] = "random-init, 4-bit g64 linears and embedding, 8-bit router"
     if args.workload == "q8_decode":
         c["launch"] = ("the step's 40 public-API calls captured once in a CUDA graph and "
                        "replayed per step; the e2e graph also holds each layer's q upload from "
                        "pinned host memory and the output read-back")
-    c["parallelism"] = f"ep{ws}" if ws > 1 and args.workload != "q8_decode" else \
+    c["parallelism"] = f"ep{ws}" if ws > 1 and args.workload not in ("q8_decode", "decode") else \
         (f"replicas{ws}" if ws > 1 else "single")
     return c
 

@@ -343,7 +343,10 @@ class Attention:
         self.q_proj, self.k_proj, self.v_proj, self.g_proj = views
         self.o_proj = o_proj
 
-    def __call__(self, x, mask=None, cache=None, residual=None):
+    def __call__(self, x, mask=None, cache=None, residual=None, pos_dev=None):
+        """``pos_dev`` (device int32 [1]): the cache position lives on the device (one-token
+        steps replayed from a CUDA graph); the cache must already hold the capacity and its
+        host ``offset`` is left alone."""
         B, L, H = x.shape
         if B != 1:
             raise NotImplementedError("batch size 1 only on this path")
@@ -351,6 +354,20 @@ class Attention:
         qkvg = self._qkvg(x.reshape(L, H))
         if cache is None:
             cache = KVCache()
+        if pos_dev is not None:
+            if L != 1 or cache.keys is None:
+                raise ValueError("device-position steps are single-token steps on a sized cache")
+            q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                    self.eps, self.rope_theta, cache.keys[0], cache.values[0],
+                                    pos_dev=pos_dev, gate_per_head=self.per_head_gate)
+            o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, 0,
+                                          self.scale, gate=gate if self.per_head_gate else None,
+                                          n_dev=pos_dev, n_add=1)
+            o = o.view(1, Hq * D)
+            if not self.per_head_gate:
+                o = o * gate.view(1, Hq * D)
+            out = self.o_proj(o, residual=None if residual is None else residual.reshape(1, H))
+            return out.reshape(B, L, H)
         cache.reserve(1, Hkv, D, L, x.device)
         pos = cache.offset
         q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
@@ -411,7 +428,7 @@ class LagunaModel:
                                     device=embed_tokens.weight.device)
         self.layer_types = args.layer_types
 
-    def __call__(self, inputs, cache=None):
+    def __call__(self, inputs, cache=None, pos_dev=None):
         if inputs.dim() == 1:
             inputs = inputs[None]
         x = self.embed_tokens(inputs)
@@ -419,7 +436,7 @@ class LagunaModel:
             cache = [None] * len(self.layers)
         xn = self.layers[0].input_layernorm(x)
         for i, (layer, c) in enumerate(zip(self.layers, cache)):
-            h = layer.self_attn(xn, None, c, residual=x)
+            h = layer.self_attn(xn, None, c, residual=x, pos_dev=pos_dev)
             m = layer.mlp(layer.post_attention_layernorm(h))
             nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else self.norm
             x, xn = ops.rmsnorm(m, nxt.weight, nxt.eps, residual=h)
@@ -479,6 +496,46 @@ class Model:
             return True
 
         return predicate
+
+
+class DecodeGraph:
+    """Greedy bs1 decoding one CUDA-graph replay per token. The token id and the cache
+    position live on the device: each step embeds ``tok``, runs every layer at position
+    ``pos`` (all kernels read it there), and the argmax kernel writes the next id into
+    ``tok`` and advances ``pos`` — so consecutive steps need no host work but the replay.
+
+    ``cache`` is a prefilled ``make_cache(capacity)`` list with room for the tokens to come;
+    ``tok`` (device int32 [1]) is the next input token. The first step runs eagerly (it also
+    sizes every workspace) before the graph is captured."""
+
+    def __init__(self, model, cache, tok):
+        self.model, self.cache = model, cache
+        self.tok = tok.reshape(1).to(torch.int32).clone()
+        self.pos = torch.tensor([cache[0].offset], dtype=torch.int32, device=self.tok.device)
+        self.cap = cache[0].keys.shape[2]
+        self.steps = 0
+        self._body()  # one real step, eagerly
+        self.steps = 1
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+
+    def _body(self):
+        h = self.model.model(self.tok.view(1, 1), self.cache, pos_dev=self.pos)
+        logits = self.model.lm_head(h)
+        ops.argmax(logits.view(1, -1), ids=self.tok, pos=self.pos, inc=1)
+
+    def step(self):
+        """One token (asynchronous); ``tok`` holds it afterwards."""
+        if self.cache[0].offset + self.steps + 1 > self.cap:
+            raise ValueError(f"the cache holds {self.cap} rows")
+        self.graph.replay()
+        self.steps += 1
+
+    def position(self):
+        """Tokens in the cache now (host copy of the device counter)."""
+        return int(self.pos.item())
 
 
 def generate(model, prompt, max_tokens, cache=None):

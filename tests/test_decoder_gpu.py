@@ -173,3 +173,22 @@ def test_model_greedy_decode_matches_oracle():
         if a != b:
             assert gaps[i] < 0.02, f"step {i}: {a} != {b} (oracle margin {gaps[i]:.4f})"
             break  # after a near-tie the continuations legitimately diverge
+
+
+def test_graph_replayed_decode_equals_eager_decode():
+    """DecodeGraph (token id and position on the device, one replay per token) produces the
+    same greedy tokens as eager decoding."""
+    from lagunalab_b200 import laguna, ops
+    args, model, _, _ = _tiny(4)
+    prompt = torch.randint(0, 512, (9,), generator=torch.Generator().manual_seed(5)).cuda()
+    eager = laguna.generate(model, prompt, 8)
+    cache = model.make_cache(capacity=256)
+    logits = model.last_logits(prompt.to(torch.int32).view(1, -1), cache)
+    tok = ops.argmax(logits.view(1, -1))
+    dg = laguna.DecodeGraph(model, cache, tok)
+    toks = [int(tok), int(dg.tok)]
+    for _ in range(6):
+        dg.step()
+        toks.append(int(dg.tok))
+    assert toks == eager
+    assert dg.position() == 9 + 7
