@@ -56,6 +56,19 @@ long long lg_launch_count(void);
  */
 int lg_profile_stage(const char* stage, void* ev_start, void* ev_end);
 
+/*
+ * Programmatic dependent launch for the decode-chain kernels (RMSNorm, GEMVs, embedding,
+ * attention prologue, bf16 decode attention, router, plan, MoE GEMVs, finalize, argmax):
+ * with on != 0 they are launched so that each may start while the previous kernel in the
+ * stream is still running; it waits for that kernel's completion before reading any input
+ * the previous kernel could write, and streams only static data (weights, and K/V rows and
+ * device-side lengths written by earlier kernels) before.  Contract while on: the kernel
+ * launched immediately before one of these must not write its weights, the K/V rows it reads
+ * other than the newest, or its device-side length.  Process-wide; returns the previous
+ * setting.  Off by default.
+ */
+int lg_set_pdl(int on);
+
 /* Milliseconds between two recorded cudaEvent_t (waits for ev_end). */
 int lg_event_elapsed_ms(void* ev_start, void* ev_end, float* ms);
 

@@ -20,6 +20,7 @@ SIGNATURES = {
     "lg_abi_version": (c_int, []),
     "lg_last_error": (ctypes.c_char_p, []),
     "lg_launch_count": (c_longlong, []),
+    "lg_set_pdl": (c_int, [c_int]),
     "lg_profile_stage": (c_int, [ctypes.c_char_p, P, P]),
     "lg_event_elapsed_ms": (c_int, [P, P, ctypes.POINTER(c_float)]),
     "lg_router_topk": (c_int, [P, I, I, P, P, P, I, P, I, I, I, I, P, P, P, P, P]),

@@ -31,6 +31,9 @@ static thread_local cudaEvent_t g_ev0 = nullptr, g_ev1 = nullptr;
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+static std::atomic<int> g_pdl{0};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
 // Inside a stream capture the record becomes a graph node that timestamps on every replay
 // (an "external" event record); outside it is an ordinary record.
 static void prof_record(cudaEvent_t ev, cudaStream_t s) {
@@ -52,6 +55,11 @@ void prof_end(const char* stage, cudaStream_t s) {
 }  // namespace lg
 
 extern "C" long long lg_launch_count(void) { return lg::g_launches.load(); }
+
+extern "C" int lg_set_pdl(int on) {
+  const int prev = lg::g_pdl.exchange(on ? 1 : 0);
+  return prev;
+}
 
 extern "C" int lg_profile_stage(const char* stage, void* ev_start, void* ev_end) {
   if (!stage || !ev_start || !ev_end) {

@@ -30,6 +30,8 @@ constexpr int AB_THREADS = AB_WARPS * 32;
 constexpr int AB_TK = 16;  // keys per tile
 constexpr size_t AB_CTRL_BYTES = 16384;  // completion counters, one 128-byte slot per (b, kv head)
 constexpr int AB_CTRL_SLOTS = (int)(AB_CTRL_BYTES / 128);
+constexpr int AB_MERGE_MAX = AB_WARPS * 16 * (AB_D + 1);  // split x head weights in the slab
+constexpr int AB_MIN_WARP_TILES = 4;  // plan at least this many 16-key tiles per warp
 
 __device__ __forceinline__ void mma_bf16_ab(float (&d)[4], uint32_t a0, uint32_t a1,
                                             uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -102,25 +104,6 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
   const __nv_bfloat16* kbase = a.k + (size_t)bh * a.cap * AB_D;
   const __nv_bfloat16* vbase = a.v + (size_t)bh * a.cap * AB_D;
 
-  // Q^T fragments: k-block kb = 2j + e, b0 = dims 32j + 8c4 + 4e + {0,1}, b1 = + {2,3}
-  uint32_t qb[NT][8][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int h = r + 8 * nt;
-    const bool hv = h < G;
-    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-        a.q + ((size_t)b * a.Hq + hk * G + (hv ? h : 0)) * AB_D);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 w = hv ? *reinterpret_cast<const uint4*>(qrow + 16 * j + 4 * c4)
-                         : make_uint4(0, 0, 0, 0);
-      qb[nt][2 * j][0] = w.x;
-      qb[nt][2 * j][1] = w.y;
-      qb[nt][2 * j + 1][0] = w.z;
-      qb[nt][2 * j + 1][1] = w.w;
-    }
-  }
-
   float m[NT][2], l[NT][2], acc[NT][8][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -144,9 +127,36 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
     }
   };
 
+  // Before the PDL wait: the length comes from a counter the previous kernel does not write,
+  // and the first tile is loaded unless it holds the newest row (the previous kernel appends
+  // it); everything else (q, the newest row, the gate) is read after the wait.
   uint4 kw[2][4], vw[2][4], kn[2][4], vn[2][4];
   int tile = tile_lo + warp;
-  if (tile < tile_hi) load_tile(tile, kw, vw);
+  const bool early = tile < tile_hi && tile * AB_TK + AB_TK <= n - 1;
+  if (early) load_tile(tile, kw, vw);
+  pdl_wait();
+  pdl_trigger();
+  if (tile < tile_hi && !early) load_tile(tile, kw, vw);
+  // Q^T fragments: k-block kb = 2j + e, b0 = dims 32j + 8c4 + 4e + {0,1}, b1 = + {2,3}
+  uint32_t qb[NT][8][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = r + 8 * nt;
+    const bool hv = h < G;
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        a.q + ((size_t)b * a.Hq + hk * G + (hv ? h : 0)) * AB_D);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = hv ? *reinterpret_cast<const uint4*>(qrow + 16 * j + 4 * c4)
+                         : make_uint4(0, 0, 0, 0);
+      qb[nt][2 * j][0] = w.x;
+      qb[nt][2 * j][1] = w.y;
+      qb[nt][2 * j + 1][0] = w.z;
+      qb[nt][2 * j + 1][1] = w.w;
+    }
+  }
+
+
   for (; tile < tile_hi; tile += AB_WARPS) {
     const int next = tile + AB_WARPS;
     if (next < tile_hi) load_tile(next, kn, vn);
@@ -293,40 +303,57 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // ---- the last CTA of this (batch, kv head) merges the splits ----
+  // ---- the last CTA of this (batch, kv head) merges the splits: split weights staged in
+  // shared memory (reusing the slab), then each thread sums its float4 items over the
+  // splits with 16 loads in flight ----
   const size_t hbase = (size_t)bh * ns * G;
-  if (threadIdx.x < G) {
-    const int h = threadIdx.x;
+  float* t_w = &slab[0][0][0];  // [split][G] normalised weights (ns * G <= AB_MERGE_MAX)
+  for (int i = threadIdx.x; i < ns * G; i += AB_THREADS) t_w[i] = __ldcg(&a.part_ml[hbase + i].x);
+  __syncthreads();
+  for (int h = warp; h < G; h += AB_WARPS) {  // one warp per head
     float M = -INFINITY;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(&a.part_ml[hbase + (size_t)s * G + h].x));
+    for (int s = lane; s < ns; s += 32) M = fmaxf(M, t_w[s * G + h]);
+    M = warp_max(M);
     float L = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float2 v = __ldcg(a.part_ml + hbase + (size_t)s * G + h);
-      if (v.x != -INFINITY) L += v.y * ex2_ab(v.x - M);
+    for (int s = lane; s < ns; s += 32) {
+      const float mx = t_w[s * G + h];
+      const float w = (mx == -INFINITY) ? 0.f : ex2_ab(mx - M);
+      L += w * __ldcg(&a.part_ml[hbase + (size_t)s * G + h].y);
+      t_w[s * G + h] = w;
     }
-    s_M[h] = M;
-    s_L[h] = 1.f / L;
+    L = warp_sum(L);
+    if (lane == 0) s_L[h] = 1.f / L;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * AB_D; i += AB_THREADS) {
-    const int h = i / AB_D, d = i % AB_D;
-    float o = 0.f;
-    for (int s0 = 0; s0 < ns; s0 += 8) {
-      float vv[8], mm[8];
+  const float4* pacc = reinterpret_cast<const float4*>(a.part_acc) + hbase * (AB_D / 4);
+  for (int it = threadIdx.x; it < G * (AB_D / 4); it += AB_THREADS) {
+    const int h = it / (AB_D / 4), d4 = it % (AB_D / 4);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < ns; s0 += 16) {
+      float4 vv[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 16; ++u)
+        if (s0 + u < ns) vv[u] = __ldcg(pacc + ((size_t)(s0 + u) * G + h) * (AB_D / 4) + d4);
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
         if (s0 + u < ns) {
-          vv[u] = __ldcg(a.part_acc + (hbase + (size_t)(s0 + u) * G + h) * AB_D + d);
-          mm[u] = __ldcg(&a.part_ml[hbase + (size_t)(s0 + u) * G + h].x);
+          const float w = t_w[(s0 + u) * G + h];
+          o.x += w * vv[u].x;
+          o.y += w * vv[u].y;
+          o.z += w * vv[u].z;
+          o.w += w * vv[u].w;
         }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (s0 + u < ns && mm[u] != -INFINITY) o += ex2_ab(mm[u] - s_M[h]) * vv[u];
     }
-    float y = round_bf16(o * s_L[h]);
-    if (a.gate) y *= bf2f(a.gate[(size_t)b * a.Hq + hk * G + h]);
-    a.out[((size_t)b * a.Hq + hk * G + h) * AB_D + d] = __float2bfloat16_rn(y);
+    const float il = s_L[h];
+    const float gt = a.gate ? bf2f(a.gate[(size_t)b * a.Hq + hk * G + h]) : 1.f;
+    const float ov[4] = {o.x, o.y, o.z, o.w};
+    __nv_bfloat16* dst = a.out + ((size_t)b * a.Hq + hk * G + h) * AB_D + 4 * d4;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float y = round_bf16(ov[c] * il);
+      if (a.gate) y *= gt;
+      dst[c] = __float2bfloat16_rn(y);
+    }
   }
   if (threadIdx.x == 0) ctr[0] = 0;  // leave the counter at zero for the next call
 }
@@ -350,14 +377,17 @@ static int ab_sm_count() {
 }
 
 // splits per (batch, kv head) for a planned length: about two CTAs per SM in total, at least
-// one tile per warp; one split when B * Hkv is large (no merge, no counters).
+// four tiles per warp (shorter splits spend more on the merge than they save); one split when
+// B * Hkv is large (no merge, no counters).
 static void ab_split(int B, int Hkv, int n_plan, int* tpc, int* nsplit) {
   const int BH = B * Hkv;
   const int tiles = (n_plan + AB_TK - 1) / AB_TK;
   int ns = (2 * ab_sm_count()) / BH;
-  ns = min(ns, (tiles + AB_WARPS - 1) / AB_WARPS);
+  ns = min(ns, (tiles + AB_WARPS * AB_MIN_WARP_TILES - 1) / (AB_WARPS * AB_MIN_WARP_TILES));
   if (BH > AB_CTRL_SLOTS) ns = 1;
   ns = max(1, min(ns, 296));
+  const int G = 16;  // worst case for the merge's weight table
+  ns = min(ns, AB_MERGE_MAX / G);
   const int t = max(1, (tiles + ns - 1) / ns);
   *tpc = t;
   *nsplit = max(1, (tiles + t - 1) / t);
@@ -428,9 +458,9 @@ extern "C" int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, i
   dim3 grid(a.nsplit, Hkv, B);
   prof_begin("bf16_decode", st);
   if (a.G <= 8)
-    bf16_decode_kernel<1><<<grid, AB_THREADS, 0, st>>>(a);
+    LG_CUDA_TRY(launch_k(bf16_decode_kernel<1>, grid, dim3(AB_THREADS), 0, st, a));
   else
-    bf16_decode_kernel<2><<<grid, AB_THREADS, 0, st>>>(a);
+    LG_CUDA_TRY(launch_k(bf16_decode_kernel<2>, grid, dim3(AB_THREADS), 0, st, a));
   prof_end("bf16_decode", st);
   LG_LAUNCH_CHECK("bf16_decode");
   return LG_OK;

@@ -7,6 +7,8 @@
 #include <stdint.h>
 #include <stddef.h>
 
+#include <utility>
+
 #include "../../include/laguna_b200.h"
 
 namespace lg {
@@ -103,6 +105,39 @@ __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float
   asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
                "f"(d)
                : "memory");
+}
+
+// ---- programmatic dependent launch (PDL) -------------------------------------------------
+// Kernels of the decode chain may be launched so that they start while the previous kernel in
+// the stream is still running (lg_set_pdl). Each such kernel calls pdl_wait() before it reads
+// anything the previous kernel may write, and pdl_trigger() only after its own wait, so when a
+// kernel starts, every kernel before its immediate predecessor has completed: before its wait
+// it may read static data (weights) and data from earlier kernels, never its predecessor's
+// output. Without the launch attribute both instructions return at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+// Launch with the programmatic-serialization attribute when PDL is on (plain launch otherwise).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  if (pdl_enabled()) {
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Block-wide exclusive scan of one int per thread (blockDim.x <= 1024); returns the exclusive

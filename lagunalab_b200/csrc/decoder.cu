@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16
                                                              float eps, __nv_bfloat16* sum_out,
                                                              __nv_bfloat16* out) {
   __shared__ float red[RN_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H);
   const uint4* rr = res ? reinterpret_cast<const uint4*>(res + (size_t)t * H) : nullptr;
@@ -124,7 +126,9 @@ struct QlArgs {
   int T, K, N;
 };
 
-template <int NTT>
+// NG: groups per warp handled per pass; the first pass's weights and scales are loaded before
+// the PDL wait (weights are static), so they stream while the previous kernel finishes.
+template <int NTT, int NG>
 __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
   __shared__ float red[QL_WARPS][32][4 * NTT];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -135,33 +139,53 @@ __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
   float acc[NTT][4];
 #pragma unroll
   for (int tt = 0; tt < NTT; ++tt) acc[tt][0] = acc[tt][1] = acc[tt][2] = acc[tt][3] = 0.f;
-#pragma unroll 4
-  for (int gg = warp; gg < gpr; gg += QL_WARPS) {
-    const size_t wo = (size_t)gg * 8 + 2 * c4;
-    const uint2 w0 = ldg_stream_u2(a.wq + (size_t)ra * wpr + wo);
-    const uint2 w8 = ldg_stream_u2(a.wq + (size_t)rb * wpr + wo);
-    const float s0 = bf2f(a.ws[(size_t)ra * gpr + gg]), s8 = bf2f(a.ws[(size_t)rb * gpr + gg]);
-    const float b0 = bf2f(a.wb[(size_t)ra * gpr + gg]), b8 = bf2f(a.wb[(size_t)rb * gpr + gg]);
+  bool waited = false;
+  for (int g0 = warp; g0 < gpr || !waited; g0 += NG * QL_WARPS) {
+    uint2 w0[NG], w8[NG];
+    float s0[NG], s8[NG], b0[NG], b8[NG];
 #pragma unroll
-    for (int tt = 0; tt < NTT; ++tt) {
-      const int tok = 8 * tt + r;
-      uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
-      if (tok < a.T) {
-        const __nv_bfloat16* xr = a.x + (size_t)tok * K + gg * 64 + 16 * c4;
-        xa0 = *reinterpret_cast<const uint4*>(xr);
-        xa1 = *reinterpret_cast<const uint4*>(xr + 8);
+    for (int i = 0; i < NG; ++i) {
+      const int gg = g0 + i * QL_WARPS;
+      if (gg < gpr) {
+        const size_t wo = (size_t)gg * 8 + 2 * c4;
+        w0[i] = ldg_stream_u2(a.wq + (size_t)ra * wpr + wo);
+        w8[i] = ldg_stream_u2(a.wq + (size_t)rb * wpr + wo);
+        s0[i] = bf2f(a.ws[(size_t)ra * gpr + gg]);
+        s8[i] = bf2f(a.ws[(size_t)rb * gpr + gg]);
+        b0[i] = bf2f(a.wb[(size_t)ra * gpr + gg]);
+        b8[i] = bf2f(a.wb[(size_t)rb * gpr + gg]);
       }
-      float xs = xsum16(xa0, xa1);
-      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
-      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
-      const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
-      const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      group_mma(d, w0, w8, xa0, xa1);
-      acc[tt][0] += s0 * d[0] + b0 * xs0;
-      acc[tt][1] += s0 * d[1] + b0 * xs1;
-      acc[tt][2] += s8 * d[2] + b8 * xs0;
-      acc[tt][3] += s8 * d[3] + b8 * xs1;
+    }
+    if (!waited) {  // x comes from the previous kernel
+      pdl_wait();
+      pdl_trigger();
+      waited = true;
+    }
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+      const int gg = g0 + i * QL_WARPS;
+      if (gg >= gpr) break;
+#pragma unroll
+      for (int tt = 0; tt < NTT; ++tt) {
+        const int tok = 8 * tt + r;
+        uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
+        if (tok < a.T) {
+          const __nv_bfloat16* xr = a.x + (size_t)tok * K + gg * 64 + 16 * c4;
+          xa0 = *reinterpret_cast<const uint4*>(xr);
+          xa1 = *reinterpret_cast<const uint4*>(xr + 8);
+        }
+        float xs = xsum16(xa0, xa1);
+        xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+        xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+        const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
+        const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        group_mma(d, w0[i], w8[i], xa0, xa1);
+        acc[tt][0] += s0[i] * d[0] + b0[i] * xs0;
+        acc[tt][1] += s0[i] * d[1] + b0[i] * xs1;
+        acc[tt][2] += s8[i] * d[2] + b8[i] * xs0;
+        acc[tt][3] += s8[i] * d[3] + b8[i] * xs1;
+      }
     }
   }
 #pragma unroll
@@ -192,6 +216,8 @@ __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
 // ---------------------------------------------------------------------------------------
 __global__ void embed_kernel(const int32_t* ids, const uint32_t* wq, const __nv_bfloat16* ws,
                              const __nv_bfloat16* wb, int V, int H, __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int id = ids[t];
   const bool ok = id >= 0 && id < V;
@@ -239,6 +265,8 @@ struct PrepArgs {
 // [Hq+Hkv, Hq+2Hkv) v heads
 __global__ void attn_prep_kernel(PrepArgs a) {
   __shared__ float red[8];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
   const int D = a.D, half = D / 2;
   const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
@@ -305,6 +333,8 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(const __nv_bfloat16*
                                                             int32_t* ids, int32_t* pos, int inc) {
   __shared__ float sv[AM_THREADS / 32];
   __shared__ int si[AM_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const __nv_bfloat16* row = logits + (size_t)t * V;
   float best = -INFINITY;
@@ -363,11 +393,12 @@ extern "C" int lg_rmsnorm(const void* x, const void* residual, const void* w, in
                    (!residual || aligned(residual, 16)) && (!sum_out || aligned(sum_out, 16)),
                "rmsnorm: tensors must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rmsnorm_kernel<<<T, RN_THREADS, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
-      static_cast<const __nv_bfloat16*>(w), H, eps,
-      residual ? static_cast<__nv_bfloat16*>(sum_out) : nullptr,
-      static_cast<__nv_bfloat16*>(out));
+  LG_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(T), dim3(RN_THREADS), 0, st,
+                       static_cast<const __nv_bfloat16*>(x),
+                       static_cast<const __nv_bfloat16*>(residual),
+                       static_cast<const __nv_bfloat16*>(w), H, eps,
+                       residual ? static_cast<__nv_bfloat16*>(sum_out) : nullptr,
+                       static_cast<__nv_bfloat16*>(out)));
   LG_LAUNCH_CHECK("rmsnorm");
   return LG_OK;
 }
@@ -394,10 +425,17 @@ extern "C" int lg_qlinear(const void* x, int T, int K, int N, const uint32_t* w_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int tiles = (N + 15) / 16;
   prof_begin("qlinear", st);
+  const int gpw = (K / 64 + QL_WARPS - 1) / QL_WARPS;  // groups per warp
+  cudaError_t e;
   if (T <= 8)
-    qlinear_kernel<1><<<tiles, QL_WARPS * 32, 0, st>>>(a);
+    e = gpw <= 2 ? launch_k(qlinear_kernel<1, 2>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
+        : gpw <= 4 ? launch_k(qlinear_kernel<1, 4>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
+                   : launch_k(qlinear_kernel<1, 8>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a);
   else
-    qlinear_kernel<2><<<tiles, QL_WARPS * 32, 0, st>>>(a);
+    e = gpw <= 2 ? launch_k(qlinear_kernel<2, 2>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
+        : gpw <= 4 ? launch_k(qlinear_kernel<2, 4>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
+                   : launch_k(qlinear_kernel<2, 8>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a);
+  LG_CUDA_TRY(e);
   prof_end("qlinear", st);
   LG_LAUNCH_CHECK("qlinear");
   return LG_OK;
@@ -411,9 +449,10 @@ extern "C" int lg_embed(const int32_t* ids, int T, const uint32_t* w_q, const vo
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(ids && w_q && w_s && w_b && out && aligned(out, 16), "embed: NULL or misaligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  embed_kernel<<<T, 128, 0, st>>>(ids, w_q, static_cast<const __nv_bfloat16*>(w_s),
-                                  static_cast<const __nv_bfloat16*>(w_b), V, H,
-                                  static_cast<__nv_bfloat16*>(out));
+  LG_CUDA_TRY(launch_k(embed_kernel, dim3(T), dim3(128), 0, st, ids, w_q,
+                       static_cast<const __nv_bfloat16*>(w_s),
+                       static_cast<const __nv_bfloat16*>(w_b), V, H,
+                       static_cast<__nv_bfloat16*>(out)));
   LG_LAUNCH_CHECK("embed");
   return LG_OK;
 }
@@ -450,7 +489,7 @@ extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, con
   a.gate_out = static_cast<__nv_bfloat16*>(gate_out);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 grid(Hq + 2 * Hkv, T);
-  attn_prep_kernel<<<grid, D / 2, 0, st>>>(a);
+  LG_CUDA_TRY(launch_k(attn_prep_kernel, grid, dim3(D / 2), 0, st, a));
   LG_LAUNCH_CHECK("attn_prep");
   return LG_OK;
 }
@@ -461,8 +500,8 @@ extern "C" int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(logits && ids, "argmax: NULL pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  argmax_kernel<<<T, AM_THREADS, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), V, ids, pos,
-                                          inc);
+  LG_CUDA_TRY(launch_k(argmax_kernel, dim3(T), dim3(AM_THREADS), 0, st,
+                       static_cast<const __nv_bfloat16*>(logits), V, ids, pos, inc));
   LG_LAUNCH_CHECK("argmax");
   return LG_OK;
 }

@@ -42,6 +42,8 @@ static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh,
 
 __global__ void finalize_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
                                      size_t n4) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
        i += (size_t)gridDim.x * blockDim.x) {
     float4 v = reinterpret_cast<const float4*>(acc)[i];
@@ -161,7 +163,9 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
     int blocks = (int)((n4 + 255) / 256);
     if (blocks > 148 * 8) blocks = 148 * 8;
     prof_begin("finalize", st);
-    finalize_bf16_kernel<<<blocks, 256, 0, st>>>(w.out_acc, static_cast<__nv_bfloat16*>(out), n4);
+    LG_CUDA_TRY(launch_k(finalize_bf16_kernel, dim3(blocks), dim3(256), 0, st,
+                         static_cast<const float*>(w.out_acc), static_cast<__nv_bfloat16*>(out),
+                         n4));
     prof_end("finalize", st);
     LG_LAUNCH_CHECK("finalize_bf16");
   }

@@ -33,6 +33,8 @@ __device__ __forceinline__ int row_token(int p, int P, int k) { return p < P ? p
 constexpr int GV_WARPS = 4;
 
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs a) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ float red[GV_WARPS][2][32][4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int na = a.active[0];
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
 
 template <bool SCATTER>
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ float red[GV_WARPS][32][4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int na = a.active[0];
@@ -205,15 +209,15 @@ int launch_gemv(const GemvArgs& a, int max_groups, bool scatter, cudaStream_t s)
   const int Imax = a.I > a.I_sh ? a.I : a.I_sh;
   dim3 g1((Imax + 15) / 16, max_groups);
   prof_begin("experts_gateup", s);
-  moe_gemv_gateup_kernel<<<g1, GV_WARPS * 32, 0, s>>>(a);
+  LG_CUDA_TRY(launch_k(moe_gemv_gateup_kernel, g1, dim3(GV_WARPS * 32), 0, s, a));
   prof_end("experts_gateup", s);
   LG_LAUNCH_CHECK("moe_gemv_gateup");
   dim3 g2((a.H + 15) / 16, max_groups);
   prof_begin("experts_down", s);
   if (scatter)
-    moe_gemv_down_kernel<true><<<g2, GV_WARPS * 32, 0, s>>>(a);
+    LG_CUDA_TRY(launch_k(moe_gemv_down_kernel<true>, g2, dim3(GV_WARPS * 32), 0, s, a));
   else
-    moe_gemv_down_kernel<false><<<g2, GV_WARPS * 32, 0, s>>>(a);
+    LG_CUDA_TRY(launch_k(moe_gemv_down_kernel<false>, g2, dim3(GV_WARPS * 32), 0, s, a));
   prof_end("experts_down", s);
   LG_LAUNCH_CHECK("moe_gemv_down");
   return LG_OK;

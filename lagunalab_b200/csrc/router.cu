@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int H, const void* __restrict__ gw,
     const __nv_bfloat16* __restrict__ gs, const __nv_bfloat16* __restrict__ gb, int E,
     float* __restrict__ logits) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ float xs[RL_KC][RL_TT + 1];
   __shared__ float ws[RL_KC][RL_EB + 1];
   const int tid = threadIdx.x;
@@ -116,6 +118,8 @@ __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloa
                                                                 int T, int H,
                                                                 const float* __restrict__ W,
                                                                 int E, float* __restrict__ logits) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ __align__(16) __nv_bfloat16 xs[RM_TT][RM_LD];
   __shared__ __align__(16) __nv_bfloat16 ws[3][RM_EB][RM_LD];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -199,6 +203,8 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int H, const void* __restrict__ gw,
     const __nv_bfloat16* __restrict__ gs, const __nv_bfloat16* __restrict__ gb, int E,
     float* __restrict__ logits) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (e >= E) return;
@@ -240,6 +246,8 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
     const float* __restrict__ logits, int T, int E, const float* __restrict__ ebias, int k,
     int norm, int score_fn, int32_t* __restrict__ inds, __nv_bfloat16* __restrict__ wout,
     int32_t* __restrict__ counts) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ int hist[256];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
@@ -341,6 +349,8 @@ __global__ void __launch_bounds__(512) moe_plan_kernel(const int32_t* __restrict
                                                        int32_t* __restrict__ offsets,
                                                        int32_t* __restrict__ perm,
                                                        int32_t* __restrict__ active) {
+  pdl_wait();  // inputs come from the previous kernel
+  pdl_trigger();
   __shared__ int warp_tot[32];
   __shared__ int s_total, s_before;
   const int g = blockIdx.x;
@@ -424,31 +434,35 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
   prof_begin("router_logits", s);
   if (T <= 32) {
     // decode: one warp per expert, weight row in registers
+    const __nv_bfloat16* nb = nullptr;
     if (gate_bits == 0)
-      router_logits_gemv_kernel<0><<<(E + 7) / 8, 256, 0, s>>>(xb, T, H, gate_w, nullptr, nullptr,
-                                                               E, logits);
+      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<0>, dim3((E + 7) / 8), dim3(256), 0, s, xb, T,
+                           H, gate_w, nb, nb, E, logits));
     else
-      router_logits_gemv_kernel<8><<<(E + 7) / 8, 256, 0, s>>>(xb, T, H, gate_w, gsb, gbb, E,
-                                                               logits);
+      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<8>, dim3((E + 7) / 8), dim3(256), 0, s, xb, T,
+                           H, gate_w, gsb, gbb, E, logits));
   } else if (gate_bits == 0 && xa) {
     dim3 g((E + RM_EB - 1) / RM_EB, (T + RM_TT - 1) / RM_TT);
-    router_logits_mma_kernel<<<g, 128, 0, s>>>(xb, T, H, static_cast<const float*>(gate_w), E,
-                                               logits);
+    LG_CUDA_TRY(launch_k(router_logits_mma_kernel, g, dim3(128), 0, s, xb, T, H,
+                         static_cast<const float*>(gate_w), E, logits));
   } else {
     dim3 g1((E + RL_EB - 1) / RL_EB, (T + RL_TT - 1) / RL_TT);
+    const __nv_bfloat16* nb = nullptr;
     if (gate_bits == 0)
-      router_logits_kernel<0><<<g1, 256, 0, s>>>(xb, T, H, gate_w, nullptr, nullptr, E, logits);
+      LG_CUDA_TRY(launch_k(router_logits_kernel<0>, g1, dim3(256), 0, s, xb, T, H, gate_w, nb, nb,
+                           E, logits));
     else
-      router_logits_kernel<8><<<g1, 256, 0, s>>>(xb, T, H, gate_w, gsb, gbb, E, logits);
+      LG_CUDA_TRY(launch_k(router_logits_kernel<8>, g1, dim3(256), 0, s, xb, T, H, gate_w, gsb,
+                           gbb, E, logits));
   }
   prof_end("router_logits", s);
   LG_LAUNCH_CHECK("router_logits");
   int blocks = (T + TK_WARPS - 1) / TK_WARPS;
   if (blocks > 1184) blocks = 1184;
   prof_begin("router_topk", s);
-  router_topk_kernel<<<blocks, TK_WARPS * 32, 0, s>>>(logits, T, E, e_bias, k, norm_topk_prob,
-                                                      score_fn, inds,
-                                                      static_cast<__nv_bfloat16*>(weights), counts);
+  LG_CUDA_TRY(launch_k(router_topk_kernel, dim3(blocks), dim3(TK_WARPS * 32), 0, s,
+                       static_cast<const float*>(logits), T, E, e_bias, k, norm_topk_prob,
+                       score_fn, inds, static_cast<__nv_bfloat16*>(weights), counts));
   prof_end("router_topk", s);
   LG_LAUNCH_CHECK("router_topk");
   return LG_OK;
@@ -462,7 +476,8 @@ int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32
   if (G == 0) return LG_OK;
   if (active) LG_CUDA_TRY(cudaMemsetAsync(active, 0, sizeof(int32_t), s));
   prof_begin("plan", s);
-  moe_plan_kernel<<<G, 512, 0, s>>>(inds, T, k, E, with_shared, counts, offsets, perm, active);
+  LG_CUDA_TRY(launch_k(moe_plan_kernel, dim3(G), dim3(512), 0, s, inds, T, k, E, with_shared,
+                       counts, offsets, perm, active));
   prof_end("plan", s);
   LG_LAUNCH_CHECK("moe_plan");
   return LG_OK;

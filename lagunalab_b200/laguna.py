@@ -508,7 +508,7 @@ class DecodeGraph:
     ``tok`` (device int32 [1]) is the next input token. The first step runs eagerly (it also
     sizes every workspace) before the graph is captured."""
 
-    def __init__(self, model, cache, tok):
+    def __init__(self, model, cache, tok, pdl=True):
         self.model, self.cache = model, cache
         self.tok = tok.reshape(1).to(torch.int32).clone()
         self.pos = torch.tensor([cache[0].offset], dtype=torch.int32, device=self.tok.device)
@@ -518,8 +518,15 @@ class DecodeGraph:
         self.steps = 1
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self._body()
+        # the step's kernels are captured with programmatic dependent launch: each starts
+        # while its predecessor runs and streams its weights before waiting for it
+        from . import _lib
+        prev = _lib.lib().lg_set_pdl(1 if pdl else 0)
+        try:
+            with torch.cuda.graph(self.graph):
+                self._body()
+        finally:
+            _lib.lib().lg_set_pdl(prev)
 
     def _body(self):
         h = self.model.model(self.tok.view(1, 1), self.cache, pos_dev=self.pos)

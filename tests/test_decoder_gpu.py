@@ -192,3 +192,26 @@ def test_graph_replayed_decode_equals_eager_decode():
         toks.append(int(dg.tok))
     assert toks == eager
     assert dg.position() == 9 + 7
+
+
+def test_decode_with_dependent_launch_equals_plain_launch():
+    """The same decode steps eagerly with programmatic dependent launch on and off, and a
+    graph captured without it: identical tokens."""
+    from lagunalab_b200 import _lib, laguna, ops
+    args, model, _, _ = _tiny(6)
+    prompt = torch.randint(0, 512, (7,), generator=torch.Generator().manual_seed(8)).cuda()
+    plain = laguna.generate(model, prompt, 6)
+    prev = _lib.lib().lg_set_pdl(1)
+    try:
+        with_pdl = laguna.generate(model, prompt, 6)
+    finally:
+        _lib.lib().lg_set_pdl(prev)
+    assert with_pdl == plain
+    cache = model.make_cache(capacity=256)
+    tok = ops.argmax(model.last_logits(prompt.to(torch.int32).view(1, -1), cache).view(1, -1))
+    dg = laguna.DecodeGraph(model, cache, tok, pdl=False)
+    toks = [int(tok), int(dg.tok)]
+    for _ in range(4):
+        dg.step()
+        toks.append(int(dg.tok))
+    assert toks == plain
