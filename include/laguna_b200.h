@@ -303,6 +303,85 @@ int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, int D, const
 int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,
               void* stream);
 
+/* ---- one-token (bs1 decode) kernels -------------------------------------------------------
+ * Each streams its weights into shared memory with bulk copies; with lg_set_pdl on, those of
+ * the static weights are issued before the kernel waits for its predecessor. They have no
+ * separate counterparts in the reference: they are the decode-size forms of the linears
+ * (nn.QuantizedLinear, laguna.py:84-92, :197), the decoder layer's RMSNorms (laguna.py:158-161,
+ * :189), SparseMoeBlock.__call__ (laguna.py:137-150) and MLP (laguna.py:114-122), fused the way
+ * one decode step of the decoder (laguna.py:169-206) chains them.
+ */
+
+/*
+ * One token through a 4-bit g64 linear [N, K] (w_q/w_s/w_b): out[n] = bf16(W x)[n]
+ * (+ residual[n], bf16 add). norm_w != NULL: x is the residual stream and is first
+ * RMS-normalised, bf16(bf16(x * rsqrt(mean(x^2) + eps)) * norm_w), bit-identical to
+ * lg_rmsnorm. u_q != NULL (with u_s/u_b, same shape): gate/up pair, out = SwiGLU(W_g x, W_u x)
+ * with the MLX rounding points (no residual then). K % 64 == 0, K <= 16384; x, weights,
+ * scales, biases and norm_w 16-byte aligned.
+ */
+int lg_decode_gemv(const void* x, int K, int N, const uint32_t* w_q, const void* w_s,
+                   const void* w_b, const uint32_t* u_q, const void* u_s, const void* u_b,
+                   const void* norm_w, float eps, const void* residual, void* out, void* stream);
+
+/*
+ * One token's post-attention RMSNorm and router (laguna.py:137-145) in one launch: xn_out =
+ * rmsnorm(h) (bf16 [H], bit-identical to lg_rmsnorm), logits = bf16(xn . W^T) for the 8-bit g64
+ * router W [E, H] (bit-identical to lg_router_topk's), then the same sigmoid/softmax, bias,
+ * top-k and weights as lg_router_topk: inds int32 [k], weights bf16 [k], logits fp32 [E]
+ * (optional). CTAs of 8 experts each; the last one to finish selects. The workspace
+ * (lg_router_decode_workspace_bytes) must start with 16 zero bytes; completed calls leave them
+ * so. k <= 32; LG_ERR_UNSUPPORTED unless lg_router_decode_supported(H, E).
+ */
+int lg_router_decode(const void* h, const void* norm_w, float eps, int H, const uint32_t* gate_q,
+                     const void* gate_s, const void* gate_b, const float* e_bias, int E, int k,
+                     int norm_topk_prob, int score_fn, void* xn_out, int32_t* inds,
+                     void* weights, float* logits, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Workspace bytes of lg_router_decode for E experts. */
+size_t lg_router_decode_workspace_bytes(int E);
+
+/* 1 if lg_router_decode takes an E x H router (E <= 256, H % 64 == 0, H <= 16384, and
+ * H % 512 == 0 or E % 8 == 0), else 0. */
+int lg_router_decode_supported(int H, int E);
+
+/* Workspace bytes of lg_moe_decode (the SwiGLU outputs of the k + 1 groups). */
+size_t lg_moe_decode_workspace_bytes(int I, int I_shared, int k);
+
+/* 1 if lg_moe_decode takes these sizes (its shared-memory tiles fit), else 0. */
+int lg_moe_decode_supported(int H, int I, int I_shared, int k);
+
+/*
+ * One token through the MoE experts (laguna.py:147-150 after route): out = bf16(
+ * sum_j bf16(w[j]) * routed_scale * y_j + y_shared) (+ residual, bf16 add), where y_j =
+ * bf16(down_e(SwiGLU(gate_e xn, up_e xn))) for e = inds[j] (picks outside [0, E) contribute
+ * nothing), y_shared the shared expert's output (I_shared = 0: none). Fixed summation order
+ * (fp32, one rounding), two launches (gate/up + SwiGLU, then down + combine + residual).
+ * Weights as lg_moe_experts, 16-byte aligned; H, I, I_shared multiples of 64.
+ */
+int lg_moe_decode(const void* xn, const int32_t* inds, const void* weights, int H, int I, int E,
+                  int k, float routed_scale, const uint32_t* g_q, const void* g_s,
+                  const void* g_b, const uint32_t* u_q, const void* u_s, const void* u_b,
+                  const uint32_t* d_q, const void* d_s, const void* d_b, int I_shared,
+                  const uint32_t* sg_q, const void* sg_s, const void* sg_b,
+                  const uint32_t* su_q, const void* su_s, const void* su_b,
+                  const uint32_t* sd_q, const void* sd_s, const void* sd_b,
+                  const void* residual, void* out, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+
+/*
+ * Check word of the one-token kernels' shared-memory staging: every 16-byte asynchronous copy
+ * verifies that both addresses are 16-byte aligned and that its destination lies inside the
+ * CTA's dynamic shared memory; a copy that fails is skipped (its tile's results are then
+ * wrong) and the first failure is recorded here: check[0] = 1, check[1] = the destination's
+ * shared-memory offset, check[2] = the source address, check[3] = blockIdx.y << 48 |
+ * blockIdx.x << 16 | threadIdx.x. All zero when no check failed. Synchronous; reset != 0
+ * clears it.
+ */
+int lg_decode_status(unsigned long long check[4], int reset);
+
 #ifdef __cplusplus
 }
 #endif

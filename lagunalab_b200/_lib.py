@@ -52,6 +52,16 @@ SIGNATURES = {
     "lg_bf16_decode_attention": (c_int, [P, I, I, I, I, P, P, I, I, P, I, I, c_float, P, P, P,
                                          c_size_t, P]),
     "lg_argmax": (c_int, [P, I, I, P, P, I, P]),
+    "lg_decode_gemv": (c_int, [P, I, I, P, P, P, P, P, P, P, c_float, P, P, P]),
+    "lg_router_decode": (c_int, [P, P, c_float, I, P, P, P, P, I, I, I, I, P, P, P, P, P,
+                                 c_size_t, P]),
+    "lg_router_decode_workspace_bytes": (c_size_t, [I]),
+    "lg_moe_decode_workspace_bytes": (c_size_t, [I, I, I]),
+    "lg_moe_decode_supported": (c_int, [I, I, I, I]),
+    "lg_router_decode_supported": (c_int, [I, I]),
+    "lg_decode_status": (c_int, [P, I]),
+    "lg_moe_decode": (c_int, [P, P, P, I, I, I, I, c_float, P, P, P, P, P, P, P, P, P, I,
+                              P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
 }
 
 _lib = None

@@ -34,6 +34,24 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 static std::atomic<int> g_pdl{0};
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
+int device_sm_count() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return 148;
+  }
+  int c = cached[dev].load(std::memory_order_relaxed);
+  if (c <= 0) {
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) {
+      (void)cudaGetLastError();
+      c = 148;
+    }
+    cached[dev].store(c, std::memory_order_relaxed);
+  }
+  return c;
+}
+
 // Inside a stream capture the record becomes a graph node that timestamps on every replay
 // (an "external" event record); outside it is an ordinary record.
 static void prof_record(cudaEvent_t ev, cudaStream_t s) {

@@ -140,6 +140,9 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Multiprocessor count of the current device (cached per device).
+int device_sm_count();
+
 // Block-wide exclusive scan of one int per thread (blockDim.x <= 1024); returns the exclusive
 // prefix and writes the block total to *total.
 __device__ __forceinline__ int block_excl_scan(int v, int* warp_tot, int* total) {

@@ -7,6 +7,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "decode_core.cuh"
 #include "gemv_core.cuh"
 
 namespace lg {
@@ -31,80 +32,28 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16
                                                              const __nv_bfloat16* w, int H,
                                                              float eps, __nv_bfloat16* sum_out,
                                                              __nv_bfloat16* out) {
-  __shared__ float red[RN_THREADS / 32];
+  extern __shared__ __align__(16) uint4 hsm[];  // the row being normalised, [H / 8]
+  __shared__ float red[8];
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * H);
   const uint4* rr = res ? reinterpret_cast<const uint4*>(res + (size_t)t * H) : nullptr;
+  uint4* so = sum_out ? reinterpret_cast<uint4*>(sum_out + (size_t)t * H) : nullptr;
   const int nv = H / 8;
-  float ss = 0.f;
   for (int i = threadIdx.x; i < nv; i += RN_THREADS) {
     uint4 v = xr[i];
     if (rr) {
-      const uint4 b = rr[i];
-      uint32_t* pv = &v.x;
-      const uint32_t* pb = &b.x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const __nv_bfloat162 s = __floats2bfloat162_rn(
-            __uint_as_float(pv[j] << 16) + __uint_as_float(pb[j] << 16),
-            __uint_as_float(pv[j] & 0xffff0000u) + __uint_as_float(pb[j] & 0xffff0000u));
-        pv[j] = *reinterpret_cast<const uint32_t*>(&s);
-      }
-      if (sum_out) reinterpret_cast<uint4*>(sum_out + (size_t)t * H)[i] = v;
+      v = add8_bf16(v, rr[i]);
+      if (so) so[i] = v;
     }
-    const uint32_t* pv = &v.x;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = __uint_as_float(pv[j] << 16), b = __uint_as_float(pv[j] & 0xffff0000u);
-      ss += a * a + b * b;
-    }
+    hsm[i] = v;
   }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < RN_THREADS / 32; ++i) tot += red[i];
-  const float r = 1.0f / sqrtf(tot / (float)H + eps);
+  const float r = block_rms_scale(hsm, H, eps, red);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
-  const uint4* src = (rr && sum_out) ? reinterpret_cast<const uint4*>(sum_out + (size_t)t * H)
-                                     : nullptr;
-  for (int i = threadIdx.x; i < nv; i += RN_THREADS) {
-    uint4 v;
-    if (src) {
-      v = src[i];  // this thread wrote it above
-    } else {
-      v = xr[i];
-      if (rr) {
-        const uint4 b = rr[i];
-        uint32_t* pv = &v.x;
-        const uint32_t* pb = &b.x;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const __nv_bfloat162 s = __floats2bfloat162_rn(
-              __uint_as_float(pv[j] << 16) + __uint_as_float(pb[j] << 16),
-              __uint_as_float(pv[j] & 0xffff0000u) + __uint_as_float(pb[j] & 0xffff0000u));
-          pv[j] = *reinterpret_cast<const uint32_t*>(&s);
-        }
-      }
-    }
-    const uint4 wv = wr[i];
-    const uint32_t* pv = &v.x;
-    const uint32_t* pw = &wv.x;
-    uint4 o;
-    uint32_t* po = &o.x;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = round_bf16(__uint_as_float(pv[j] << 16) * r) * __uint_as_float(pw[j] << 16);
-      const float b = round_bf16(__uint_as_float(pv[j] & 0xffff0000u) * r) *
-                      __uint_as_float(pw[j] & 0xffff0000u);
-      const __nv_bfloat162 s = __floats2bfloat162_rn(a, b);
-      po[j] = *reinterpret_cast<const uint32_t*>(&s);
-    }
-    reinterpret_cast<uint4*>(out + (size_t)t * H)[i] = o;
-  }
+  uint4* orow = reinterpret_cast<uint4*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < nv; i += RN_THREADS) orow[i] = rms_apply8(hsm[i], wr[i], r);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -386,14 +335,15 @@ using namespace lg;
 
 extern "C" int lg_rmsnorm(const void* x, const void* residual, const void* w, int T, int H,
                           float eps, void* sum_out, void* out, void* stream) {
-  LG_CHECK_ARG(T >= 0 && H > 0 && H % 8 == 0, "rmsnorm: need H %% 8 == 0 (H=%d, T=%d)", H, T);
+  LG_CHECK_ARG(T >= 0 && H > 0 && H % 8 == 0 && H <= 16384,
+               "rmsnorm: need H %% 8 == 0 and H <= 16384 (H=%d, T=%d)", H, T);
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(x && w && out, "rmsnorm: NULL pointer");
   LG_CHECK_ARG(aligned(x, 16) && aligned(w, 16) && aligned(out, 16) &&
                    (!residual || aligned(residual, 16)) && (!sum_out || aligned(sum_out, 16)),
                "rmsnorm: tensors must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  LG_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(T), dim3(RN_THREADS), 0, st,
+  LG_CUDA_TRY(launch_k(rmsnorm_kernel, dim3(T), dim3(RN_THREADS), (size_t)H * 2, st,
                        static_cast<const __nv_bfloat16*>(x),
                        static_cast<const __nv_bfloat16*>(residual),
                        static_cast<const __nv_bfloat16*>(w), H, eps,

@@ -14,6 +14,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "decode_core.cuh"
 
 namespace lg {
 
@@ -210,37 +211,26 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
   if (e >= E) return;
   for (int t = 0; t < T; ++t) {
     const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (size_t)t * H);
+    if (GBITS == 8) {  // the fused one-token router computes the same function
+      const float v = router_logit8(xr, static_cast<const uint32_t*>(gw) + (size_t)e * (H / 4),
+                                    gs + (size_t)e * (H / 64), gb + (size_t)e * (H / 64), H);
+      if (lane == 0) logits[(size_t)t * E + e] = v;
+      continue;
+    }
     float acc = 0.f;
     for (int k2 = lane; k2 < H / 2; k2 += 32) {
       const float2 xv = __bfloat1622float2(xr[k2]);
-      float w0, w1;
-      if (GBITS == 0) {
-        const float2 wv = reinterpret_cast<const float2*>(static_cast<const float*>(gw) +
-                                                          (size_t)e * H)[k2];
-        w0 = wv.x;
-        w1 = wv.y;
-      } else {
-        const int k = 2 * k2;
-        const uint32_t word = static_cast<const uint32_t*>(gw)[(size_t)e * (H / 4) + (k >> 2)];
-        const float sc = bf2f(gs[(size_t)e * (H / 64) + k / 64]);
-        const float bi = bf2f(gb[(size_t)e * (H / 64) + k / 64]);
-        w0 = fmaf(sc, code_to_f((word >> (8 * (k & 3))) & 0xffu), bi);
-        w1 = fmaf(sc, code_to_f((word >> (8 * ((k + 1) & 3))) & 0xffu), bi);
-      }
-      acc = fmaf(xv.x, w0, acc);
-      acc = fmaf(xv.y, w1, acc);
+      const float2 wv = reinterpret_cast<const float2*>(static_cast<const float*>(gw) +
+                                                        (size_t)e * H)[k2];
+      acc = fmaf(xv.x, wv.x, acc);
+      acc = fmaf(xv.y, wv.y, acc);
     }
     acc = warp_sum(acc);
-    if (lane == 0) logits[(size_t)t * E + e] = (GBITS == 8) ? round_bf16(acc) : acc;
+    if (lane == 0) logits[(size_t)t * E + e] = acc;
   }
 }
 
-__device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
-  return (a > b) || (a == b && ia < ib);
-}
-
 constexpr int TK_WARPS = 8;
-constexpr int MAXE_PER_LANE = 8;  // E <= 256
 
 __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
     const float* __restrict__ logits, int T, int E, const float* __restrict__ ebias, int k,
@@ -249,86 +239,19 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
   __shared__ int hist[256];
+  __shared__ float kv[TK_WARPS][2 * 256 + 32];  // per warp: keys [E], scores [E], picks [k]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  const int nper = (E + 31) / 32;
   for (int t = blockIdx.x * TK_WARPS + warp; t < T; t += gridDim.x * TK_WARPS) {
-    float sc[MAXE_PER_LANE], sl[MAXE_PER_LANE];
     const float* row = logits + (size_t)t * E;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < MAXE_PER_LANE; ++j) {
-      int e = lane + 32 * j;
-      float l = (j < nper && e < E) ? row[e] : -INFINITY;
-      sc[j] = l;
-      mx = fmaxf(mx, l);
-    }
-    if (score_fn == LG_SCORE_SOFTMAX) {
-      mx = warp_max(mx);
-      float sum = 0.f;
-#pragma unroll
-      for (int j = 0; j < MAXE_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        float v = (j < nper && e < E) ? expf(sc[j] - mx) : 0.f;
-        sc[j] = v;
-        sum += v;
-      }
-      sum = warp_sum(sum);
-#pragma unroll
-      for (int j = 0; j < MAXE_PER_LANE; ++j) sc[j] = sc[j] / sum;
-    } else {
-#pragma unroll
-      for (int j = 0; j < MAXE_PER_LANE; ++j) sc[j] = 1.0f / (1.0f + expf(-sc[j]));
-    }
-#pragma unroll
-    for (int j = 0; j < MAXE_PER_LANE; ++j) {
-      int e = lane + 32 * j;
-      bool ok = (j < nper && e < E);
-      sl[j] = ok ? sc[j] + (ebias ? ebias[e] : 0.f) : -INFINITY;
-      if (!ok) sc[j] = 0.f;
-    }
-    unsigned taken = 0;  // bit j: expert lane + 32 j already selected
-    float my_w = 0.f, wsum = 0.f;
-    int my_i = -1;
-    for (int r = 0; r < k; ++r) {
-      // local best among untaken
-      float bv = -INFINITY, bs = 0.f;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < MAXE_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        if (j < nper && e < E && !((taken >> j) & 1u) && better(sl[j], e, bv, bi)) {
-          bv = sl[j];
-          bs = sc[j];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        float os = __shfl_xor_sync(0xffffffffu, bs, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (better(ov, oi, bv, bi)) {
-          bv = ov;
-          bs = os;
-          bi = oi;
-        }
-      }
-      const bool valid = bi >= 0 && bi < E;  // false only if every candidate is NaN
-      if (valid && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-      if (lane == r) {
-        my_i = valid ? bi : -1;
-        my_w = valid ? bs : 0.f;
-      }
-      wsum += valid ? bs : 0.f;
-      if (lane == 0 && valid) atomicAdd(&hist[bi], 1);  // one shared atomic per pick
-    }
+    int idx = -1;
+    float wt = 0.f;
+    topk_warp([&](int e) { return row[e]; }, E, ebias, k, norm, score_fn, &idx, &wt, hist,
+              kv[warp], kv[warp] + E);
     if (lane < k) {
-      float w = my_w;
-      if (norm) w = w / wsum;
-      inds[(size_t)t * k + lane] = my_i;
-      wout[(size_t)t * k + lane] = __float2bfloat16_rn(w);
+      inds[(size_t)t * k + lane] = idx;
+      wout[(size_t)t * k + lane] = __float2bfloat16_rn(wt);
     }
   }
   __syncthreads();

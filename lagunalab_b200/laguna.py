@@ -127,6 +127,16 @@ class MLP:
                        bits=self.gate_proj.bits)
         return out.reshape(shape)
 
+    def token(self, h, norm):
+        """One token's dense MLP sub-block from the residual stream h [1, H]:
+        ``h + self(norm(h))`` as two launches (norm + gate/up + SwiGLU, down + residual)."""
+        if (self.gate_proj.bits, self.gate_proj.group_size) != (4, 64):
+            return None
+        H = h.shape[-1]
+        a = ops.decode_gemv(h.reshape(1, H), self.gate_proj.mat, norm=(norm.weight, norm.eps),
+                            up=self.up_proj.mat)
+        return ops.decode_gemv(a, self.down_proj.mat, residual=h.reshape(1, H))
+
 
 class SwitchLinear(QuantizedLinear):
     """mlx-lm QuantizedSwitchLinear storage: stacked [E, out, in*bits/32] words and
@@ -215,6 +225,46 @@ class SparseMoeBlock:
         if self.shared_expert is not None:
             y = y + self.shared_expert(x)
         return y
+
+
+    def token_experts(self, H):
+        """The SwitchGLU the one-token router + expert kernels can use, or None: ``route`` not
+        wrapped or overridden (instrumentation sees every routing), an 8-bit router, 4-bit
+        experts and sizes the kernels take."""
+        if "route" in self.__dict__ or type(self).route is not SparseMoeBlock.route:
+            return None
+        g = self.gate
+        if not isinstance(g, QuantizedLinear) or (g.bits, g.group_size) != (8, 64):
+            return None
+        fused = _fused_experts(self.switch_mlp)
+        if fused is None or (fused.gate_proj.bits, fused.gate_proj.group_size) != (4, 64):
+            return None
+        Ish = 0
+        if self.shared_expert is not None:
+            sh = self.shared_expert
+            if not isinstance(sh, MLP) or (sh.gate_proj.bits, sh.gate_proj.group_size) != (4, 64):
+                return None
+            Ish = sh.hidden
+        if not ops.moe_decode_supported(H, fused.hidden_dims, Ish, self.top_k):
+            return None
+        if not ops.router_decode_supported(H, self.num_experts):
+            return None
+        return fused
+
+    def token(self, h, norm):
+        """One token's MoE sub-block from the residual stream h [1, H]:
+        ``h + self(norm(h))`` (laguna.py:163-164) as a router launch and two expert launches;
+        None when ``token_experts`` declines."""
+        H = h.shape[-1]
+        fused = self.token_experts(H)
+        if fused is None:
+            return None
+        xn, inds, w = ops.router_decode(h.reshape(1, H), norm.weight, norm.eps, self.gate.mat,
+                                        self.e_score_correction_bias, self.top_k,
+                                        self.norm_topk_prob, self.score_fn)
+        sh = self.shared_expert.mats if self.shared_expert is not None else None
+        return ops.moe_decode(xn, inds, w, self.routed_scaling_factor, fused.mats, sh,
+                              residual=h.reshape(1, H))
 
 
 def _fused_experts(sw):
@@ -343,15 +393,22 @@ class Attention:
         self.q_proj, self.k_proj, self.v_proj, self.g_proj = views
         self.o_proj = o_proj
 
-    def __call__(self, x, mask=None, cache=None, residual=None, pos_dev=None):
+    def __call__(self, x, mask=None, cache=None, residual=None, pos_dev=None, in_norm=None):
         """``pos_dev`` (device int32 [1]): the cache position lives on the device (one-token
         steps replayed from a CUDA graph); the cache must already hold the capacity and its
-        host ``offset`` is left alone."""
+        host ``offset`` is left alone. ``in_norm`` (an RMSNorm): x is the un-normalised
+        residual stream and the norm runs fused into the q/k/v/g projection."""
         B, L, H = x.shape
         if B != 1:
             raise NotImplementedError("batch size 1 only on this path")
         Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
-        qkvg = self._qkvg(x.reshape(L, H))
+        if in_norm is None:
+            qkvg = self._qkvg(x.reshape(L, H))
+        elif L == 1:
+            qkvg = ops.decode_gemv(x.reshape(1, H), self._qkvg.mat,
+                                   norm=(in_norm.weight, in_norm.eps))
+        else:
+            qkvg = self._qkvg(in_norm(x).reshape(L, H))
         if cache is None:
             cache = KVCache()
         if pos_dev is not None:
@@ -428,12 +485,19 @@ class LagunaModel:
                                     device=embed_tokens.weight.device)
         self.layer_types = args.layer_types
 
-    def __call__(self, inputs, cache=None, pos_dev=None):
+    def __call__(self, inputs, cache=None, pos_dev=None, normed=True):
+        """Final hidden states (normalised; ``normed=False`` returns the residual stream of a
+        one-token step un-normalised, for a consumer that fuses the final norm)."""
         if inputs.dim() == 1:
             inputs = inputs[None]
         x = self.embed_tokens(inputs)
         if cache is None:
             cache = [None] * len(self.layers)
+        if x.shape[0] == 1 and x.shape[1] == 1:
+            x = self._token(x, cache, pos_dev)
+            return ops.rmsnorm(x, self.norm.weight, self.norm.eps) if normed else x
+        if not normed:
+            raise ValueError("normed=False is for one-token steps")
         xn = self.layers[0].input_layernorm(x)
         for i, (layer, c) in enumerate(zip(self.layers, cache)):
             h = layer.self_attn(xn, None, c, residual=x, pos_dev=pos_dev)
@@ -441,6 +505,19 @@ class LagunaModel:
             nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else self.norm
             x, xn = ops.rmsnorm(m, nxt.weight, nxt.eps, residual=h)
         return xn
+
+    def _token(self, x, cache, pos_dev):
+        """One token through every layer: per layer the input norm runs inside the q/k/v/g
+        GEMV, the attention residual inside o_proj, and the MLP sub-block (norm, router,
+        experts, combine, residual) in the one-token kernels."""
+        for layer, c in zip(self.layers, cache):
+            h = layer.self_attn(x, None, c, residual=x, pos_dev=pos_dev,
+                                in_norm=layer.input_layernorm)
+            mlp, pn = layer.mlp, layer.post_attention_layernorm
+            tok = getattr(mlp, "token", None)
+            y = tok(h, pn) if tok is not None else None
+            x = y.reshape(h.shape) if y is not None else h + mlp(pn(h))  # bf16 add
+        return x
 
 
 class Model:
@@ -455,9 +532,17 @@ class Model:
     def __call__(self, inputs, cache=None):
         return self.lm_head(self.model(inputs, cache))
 
-    def last_logits(self, inputs, cache=None):
-        """Logits of the last position only (what generation needs after a prefill)."""
-        h = self.model(inputs, cache)
+    def last_logits(self, inputs, cache=None, pos_dev=None):
+        """Logits of the last position only (what generation needs after a prefill). A
+        one-token step runs the final norm inside the head's GEMV."""
+        ids = inputs if inputs.dim() > 1 else inputs[None]
+        if ids.shape[0] == 1 and ids.shape[1] == 1:
+            x = self.model(ids, cache, pos_dev=pos_dev, normed=False)
+            n = self.model.norm
+            H = x.shape[-1]
+            return ops.decode_gemv(x.reshape(1, H), self.lm_head.mat,
+                                   norm=(n.weight, n.eps)).reshape(1, 1, -1)
+        h = self.model(ids, cache, pos_dev=pos_dev)
         return self.lm_head(h[:, -1:])
 
     @property
@@ -529,8 +614,7 @@ class DecodeGraph:
             _lib.lib().lg_set_pdl(prev)
 
     def _body(self):
-        h = self.model.model(self.tok.view(1, 1), self.cache, pos_dev=self.pos)
-        logits = self.model.lm_head(h)
+        logits = self.model.last_logits(self.tok.view(1, 1), self.cache, pos_dev=self.pos)
         ops.argmax(logits.view(1, -1), ids=self.tok, pos=self.pos, inc=1)
 
     def step(self):

@@ -311,9 +311,118 @@ def qlinear(x, mat, residual=None, group_size=64, bits=4, out=None):
     if out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
     res = None if residual is None else _c(residual, torch.bfloat16)
+    if T == 1 and _stageable(x2, q, s, b, group_size, bits):
+        _lib.call("lg_decode_gemv", _p(x2), K, N, _p(q), _p(s), _p(b), None, None, None, None,
+                  0.0, _p(res), _p(out), _stream(x2.device))
+        return out
     _lib.call("lg_qlinear", _p(x2), T, K, N, _p(q), _p(s), _p(b), group_size, bits, _p(res),
               _p(out), _stream(x2.device))
     return out
+
+
+def _stageable(x, q, s, b, group_size, bits):
+    """Operands the shared-memory-staged one-token kernels take (16-byte aligned)."""
+    return (bits == 4 and group_size == 64 and x.shape[-1] % 64 == 0
+            and all(t.data_ptr() % 16 == 0 for t in (x, q, s, b)))
+
+
+def decode_gemv(x, mat, norm=None, residual=None, up=None, out=None, group_size=64, bits=4):
+    """One token through an MLX 4-bit [N, K] linear: ``W @ x`` (+ ``residual``), where x is
+    first RMS-normalised when ``norm=(weight, eps)`` is given. With ``up`` (the up projection of
+    the same shape), returns the SwiGLU ``silu(W_gate x) * (W_up x)`` instead. x [K] or [1, K]
+    bf16 -> [..., N] bf16."""
+    if (group_size, bits) != (64, 4):
+        raise ValueError("decode_gemv: 4-bit group-64 weights only")
+    q, s, b = _qm(mat)
+    K = x.shape[-1]
+    N = q.shape[0]
+    x2 = _c(x, torch.bfloat16).reshape(-1, K)
+    if x2.shape[0] != 1:
+        raise ValueError("decode_gemv: one token")
+    uq = us = ub = None
+    if up is not None:
+        uq, us, ub = _qm(up)
+    nw, eps = (None, 0.0) if norm is None else (_c(norm[0], torch.bfloat16), float(norm[1]))
+    res = None if residual is None else _c(residual, torch.bfloat16)
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    _lib.call("lg_decode_gemv", _p(x2), K, N, _p(q), _p(s), _p(b), _p(uq), _p(us), _p(ub),
+              _p(nw), eps, _p(res), _p(out), _stream(x2.device))
+    return out
+
+
+def router_decode(h, norm_w, eps, gate, e_bias, k, norm_topk_prob=True, score_fn="sigmoid",
+                  logits=False):
+    """One token's post-attention RMSNorm and router in one launch: from the residual stream
+    h [1, H] returns (xn [1, H] normalised, inds int32 [1, k], w bf16 [1, k][, logits fp32
+    [1, E]]). ``gate`` is the 8-bit group-64 router (weight, scales, biases)."""
+    H = h.shape[-1]
+    h2 = _c(h, torch.bfloat16).reshape(1, H)
+    gw, gs, gb = _qm(gate)
+    E = gw.shape[0]
+    dev = h2.device
+    eb = _c(e_bias.to(torch.float32)) if e_bias is not None else None
+    xn = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+    inds = torch.empty(1, k, dtype=torch.int32, device=dev)
+    w = torch.empty(1, k, dtype=torch.bfloat16, device=dev)
+    lg = torch.empty(1, E, dtype=torch.float32, device=dev) if logits else None
+    sf = _lib.LG_SCORE_SOFTMAX if score_fn == "softmax" else _lib.LG_SCORE_SIGMOID
+    ws = workspace(dev, "router_decode", _lib.lib().lg_router_decode_workspace_bytes(E), zero=True)
+    _lib.call("lg_router_decode", _p(h2), _p(_c(norm_w, torch.bfloat16)), float(eps), H,
+              _p(gw), _p(gs), _p(gb), _p(eb), E, k, int(bool(norm_topk_prob)), sf, _p(xn),
+              _p(inds), _p(w), _p(lg), _p(ws), ws.numel(), _stream(dev))
+    return (xn, inds, w, lg) if logits else (xn, inds, w)
+
+
+def moe_decode(xn, inds, w, routed_scaling_factor, experts, shared=None, residual=None,
+               out=None):
+    """One token through the MoE experts: ``sum_j w_j * SwitchGLU_j(xn) * scale + shared(xn)``
+    (+ ``residual``), bf16 [1, H]. inds int32 [1, k], w bf16 [1, k]."""
+    xn = _c(xn, torch.bfloat16)
+    dev = xn.device
+    H = xn.shape[-1]
+    inds = _c(inds, torch.int32)
+    w = _c(w, torch.bfloat16)
+    k = inds.shape[-1]
+    g, u, d = (_qm(m) for m in experts)
+    E, I = g[0].shape[0], g[0].shape[1]
+    if shared is not None:
+        sg, su, sd = (_qm(m) for m in shared)
+        Ish = sg[0].shape[0]
+    else:
+        sg = su = sd = (None, None, None)
+        Ish = 0
+    res = None if residual is None else _c(residual, torch.bfloat16)
+    if out is None:
+        out = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+    nb = _lib.lib().lg_moe_decode_workspace_bytes(I, Ish, k)
+    ws = workspace(dev, "moe_decode", nb)
+    _lib.call("lg_moe_decode", _p(xn), _p(inds), _p(w), H, I, E, k,
+              float(routed_scaling_factor), *map(_p, g), *map(_p, u), *map(_p, d), Ish,
+              *map(_p, sg), *map(_p, su), *map(_p, sd), _p(res), _p(out), _p(ws), ws.numel(),
+              _stream(dev))
+    return out
+
+
+def router_decode_supported(H, E):
+    """Whether the one-token router kernel takes an E x H router (one CTA's shared memory)."""
+    return bool(_lib.lib().lg_router_decode_supported(H, E))
+
+
+def moe_decode_supported(H, I, Ish, k):
+    """Whether the one-token expert kernels take these sizes (shared memory bound)."""
+    return bool(_lib.lib().lg_moe_decode_supported(H, I, Ish, k))
+
+
+
+def decode_status(reset=True):
+    """Check word of the one-token kernels' staging copies: (failed, smem offset, source
+    address, block/thread) of the first copy that failed its alignment or bounds check, all
+    zero when none did. Synchronises."""
+    import ctypes
+    buf = (ctypes.c_ulonglong * 4)()
+    _lib.call("lg_decode_status", ctypes.addressof(buf), int(bool(reset)))
+    return tuple(int(v) for v in buf)
 
 
 def embed(ids, mat, group_size=64, bits=4):
