@@ -45,7 +45,13 @@ WORKLOADS = {
     "decode": dict(prefill=8192, new=256, seed=1, vocab=100352, hidden=2048, layers=40, heads=32,
                    kv_heads=4, head_dim=128, experts=64, top_k=8, moe_inter=1024,
                    shared_inter=1024, dense_inter=8192, rope_theta=1e6, kv="bf16"),
+    # the headline: the same decoder, bs1 greedy decode at an 82,671-token context over the
+    # 8-bit quantized KV cache (DequantKVCache with fused_decode; BASELINE config 4's context)
+    "decode_q8": dict(prefill=82671, new=256, seed=1, vocab=100352, hidden=2048, layers=40,
+                      heads=32, kv_heads=4, head_dim=128, experts=64, top_k=8, moe_inter=1024,
+                      shared_inter=1024, dense_inter=8192, rope_theta=1e6, kv="q8"),
 }
+DECODE_WORKLOADS = ("decode", "decode_q8")
 
 
 def profile_traffic(name):
@@ -345,18 +351,20 @@ def decode_model(wl):
     return a, synth.decoder(a, seed=wl["seed"])
 
 
-def decode_bytes_per_token(model, ctx):
+def decode_bytes_per_token(model, ctx, kv="bf16"):
     """HBM bytes one decode step must read: every dense weight of the step (attention,
     router, shared expert, dense layer 0, lm_head), the top-k routed experts of each MoE
-    layer, one embedding row, and the bf16 K/V rows of ctx keys per layer."""
+    layer, one embedding row, and the K/V rows of ctx keys per layer (bf16: 2 B per element;
+    8-bit g64: 1 B per element plus a bf16 scale and bias per 64)."""
     from lagunalab_b200 import laguna
     nb = lambda m: sum(t.numel() * t.element_size() for t in m.mat)
     a = model.args
+    row = a.head_dim * 2 if kv == "bf16" else a.head_dim + (a.head_dim // 64) * 4
     total = sum(nb(x) for x in (model.lm_head,)) + nb(model.model.embed_tokens) // a.vocab_size
     for L in model.layers:
         at = L.self_attn
         total += nb(at._qkvg) + nb(at.o_proj)
-        total += 2 * a.num_key_value_heads * ctx * a.head_dim * 2
+        total += 2 * a.num_key_value_heads * ctx * row
         m = L.mlp
         if isinstance(m, laguna.MLP):
             total += sum(nb(p) for p in (m.gate_proj, m.up_proj, m.down_proj))
@@ -373,7 +381,7 @@ def decode_bytes_per_token(model, ctx):
 def run_decode(args, wl, ws, rank):
     """prefill wl["prefill"] uniform-random ids (seed 1), then greedy decode
     one token per step, each step one replay of a CUDA graph of the whole model (token id and
-    cache position stay on the device)."""
+    cache position stay on the device). kv "q8": the 8-bit quantized cache."""
     from lagunalab_b200 import laguna, ops
     margs, model = decode_model(wl)
     V = margs.vocab_size
@@ -381,7 +389,11 @@ def run_decode(args, wl, ws, rank):
     prompt = torch.randint(0, V, (wl["prefill"],), generator=g).to(torch.int32).cuda()
     n_steps = 1 + args.warmup + args.steps + 1 + max(1, args.warmup) + args.steps
     cap = (wl["prefill"] + n_steps + 255) // 256 * 256
-    cache = model.make_cache(capacity=cap)
+    if wl.get("kv") == "q8":
+        from lagunalab_b200 import cache as qcache
+        cache = qcache.make_quantized_cache(model, fused_decode=True, capacity=cap)
+    else:
+        cache = model.make_cache(capacity=cap)
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -435,7 +447,8 @@ def run_decode(args, wl, ws, rank):
     ctx = (ctx0 + ctx1) / 2
     del ge
     return dict(ms=ms, e2e_ms=e2e_ms, launches=per_replay * args.steps, clocks=clocks,
-                bytes=decode_bytes_per_token(model, ctx), ctx=(ctx0, ctx1), prefill_ms=prefill_ms,
+                bytes=decode_bytes_per_token(model, ctx, wl.get("kv", "bf16")), ctx=(ctx0, ctx1),
+                prefill_ms=prefill_ms,
                 h2d=4, d2h=4)
 
 
@@ -613,7 +626,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=list(WORKLOADS), default="moe_prefill")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="decode_q8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
                     help="q8_decode only: layers per step (default: the config's 40; fewer "
@@ -629,7 +642,7 @@ def main():
         if rank == 0:
             if args.workload == "q8_decode":
                 ref = cpu_q8(wl, args.steps, args.warmup)
-            elif args.workload == "decode":
+            elif args.workload in DECODE_WORKLOADS:
                 ref = cpu_decode(wl, min(args.steps, 5), 1)
             else:
                 ref = cpu_moe(wl, args.steps, args.warmup)
@@ -648,7 +661,7 @@ def main():
         return
 
     pk, pk_kind = peaks()
-    if args.workload == "decode":
+    if args.workload in DECODE_WORKLOADS:
         r = run_decode(args, wl, ws, rank)
         value = 1000.0 / r["ms"]
         e2e = 1000.0 / r["e2e_ms"]
@@ -657,7 +670,8 @@ def main():
                 "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk_kind,
                 "algorithmic": f"{r['bytes']:.0f} B per token (weights read by one step, top-k "
-                               f"experts, bf16 K/V at mean context {sum(r['ctx']) / 2:.0f})",
+                               f"experts, {wl['kv']} K/V at mean context "
+                               f"{sum(r['ctx']) / 2:.0f})",
                 "duration": "graph step time (one replay per token)"}
         wl = dict(wl, prefill_ms=r["prefill_ms"], context=list(r["ctx"]))
         dtype = "bf16"
@@ -709,7 +723,7 @@ def main():
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else
-              cpu_decode(wl, 3, 1) if args.workload == "decode" else cpu_moe(wl, 5, 1))
+              cpu_decode(wl, 3, 1) if args.workload in DECODE_WORKLOADS else cpu_moe(wl, 5, 1))
         line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -719,6 +733,8 @@ def main():
 def metric_unit(workload):
     if workload == "decode":
         return "bs1 decode tok/s @8k ctx (config 3, bf16 KV)", "tokens/s"
+    if workload == "decode_q8":
+        return "bs1 decode tok/s @82k ctx (config 3 model, 8-bit KV)", "tokens/s"
     if workload == "q8_decode":
         return "q8 decode attention HBM GB/s (40 layers @82,671 ctx)", "GB/s"
     if workload == "moe_decode":
@@ -729,7 +745,7 @@ def metric_unit(workload):
 def config(args, wl, ws):
     c = {"workload": args.workload, **{k: v for k, v in wl.items()}}
     c["l2"] = "inputs larger than L2 (126 MB): weights/KV streamed from HBM each step"
-    if args.workload == "decode":
+    if args.workload in DECODE_WORKLOADS:
         c["launch"] = ("prefill through the module API, then one CUDA-graph replay per decoded "
                        "token (token id and cache position kept on the device); e2e feeds each "
                        "token through pinned host memory and synchronises every step")
@@ -738,7 +754,7 @@ def config(args, wl, ws):
         c["launch"] = ("the step's 40 public-API calls captured once in a CUDA graph and "
                        "replayed per step; the e2e graph also holds each layer's q upload from "
                        "pinned host memory and the output read-back")
-    c["parallelism"] = f"ep{ws}" if ws > 1 and args.workload not in ("q8_decode", "decode") else \
+    c["parallelism"] = f"ep{ws}" if ws > 1 and args.workload not in ("q8_decode", *DECODE_WORKLOADS) else \
         (f"replicas{ws}" if ws > 1 else "single")
     return c
 

@@ -277,6 +277,18 @@ int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn
                  int pos_host, int gate_per_head, void* q_out, void* k_cache, void* v_cache,
                  int cap, void* gate_out, void* stream);
 
+/*
+ * lg_attn_prep with an 8-bit group-64 KV cache (DequantKVCache, laguna_mlx/cache.py:66-106):
+ * the new k/v rows are quantized straight into the packed cache rows pos + t (words
+ * [Hkv, cap, D/4], bf16 scales/biases [Hkv, cap, D/64]) with the arithmetic of
+ * lg_quantize_rows (bit-identical to lg_attn_prep followed by lg_quantize_rows). D <= 256.
+ */
+int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                    const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                    int pos_host, int gate_per_head, void* q_out, uint32_t* k_q, void* k_s,
+                    void* k_b, uint32_t* v_q, void* v_s, void* v_b, int cap, void* gate_out,
+                    void* stream);
+
 /* Workspace bytes for lg_bf16_decode_attention planned for n_plan keys. */
 size_t lg_bf16_decode_workspace_bytes(int B, int Hq, int Hkv, int n_plan);
 
@@ -370,6 +382,19 @@ int lg_moe_decode(const void* xn, const int32_t* inds, const void* weights, int 
                   const void* residual, void* out, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+
+/*
+ * lg_q8_decode_attention for decode steps that run without the host (a CUDA graph replayed per
+ * token): the valid length is *n_dev + n_add, read on the device (n_dev: the cache position
+ * before the step); the work split is planned for n_plan >= that length (<= cap) and the
+ * workspace sized by lg_q8_decode_workspace_bytes(B, Hq, Hkv, n_plan). gate: bf16 [B, Hq]
+ * per-head output gate (laguna.py:105-106), out = bf16(bf16(attention) * gate), or NULL.
+ */
+int lg_q8_decode_attention_dev(const void* q, int B, int Hq, int Hkv, int D, const uint32_t* k_q,
+                               const void* k_s, const void* k_b, const uint32_t* v_q,
+                               const void* v_s, const void* v_b, int cap, int n_plan,
+                               const int32_t* n_dev, int n_add, float scale, const void* gate,
+                               void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Check word of the one-token kernels' shared-memory staging: every 16-byte asynchronous copy

@@ -60,6 +60,10 @@ SIGNATURES = {
     "lg_moe_decode_supported": (c_int, [I, I, I, I]),
     "lg_router_decode_supported": (c_int, [I, I]),
     "lg_decode_status": (c_int, [P, I]),
+    "lg_attn_prep_q8": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, P, P, P,
+                                P, I, P, P]),
+    "lg_q8_decode_attention_dev": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, P, I, c_float,
+                                           P, P, P, c_size_t, P]),
     "lg_moe_decode": (c_int, [P, P, P, I, I, I, I, c_float, P, P, P, P, P, P, P, P, P, I,
                               P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
 }

@@ -16,10 +16,24 @@ from . import ops
 class QuantizedKVCache:
     step = 256
 
-    def __init__(self, group_size=64, bits=8):
+    def __init__(self, group_size=64, bits=8, capacity=0):
         self.group_size, self.bits = group_size, bits
         self.keys = self.values = None
         self.offset = 0
+        self.capacity_hint = capacity
+
+    def reserve(self, B, H, D, L, device):
+        """Room for L more rows without moving the valid ones: a first buffer holds at least
+        ``capacity`` rows; growth keeps the 256-row steps."""
+        need = self.offset + L
+        if self.keys is not None and self.keys[0].shape[2] >= need:
+            return
+        rows = max(self.capacity_hint, (need + self.step - 1) // self.step * self.step)
+        k, v = self._alloc(B, H, rows, D, device), self._alloc(B, H, rows, D, device)
+        if self.keys is not None and self.offset:
+            for dst, src in zip(k + v, self.keys + self.values):
+                dst[:, :, :self.offset] = src[:, :, :self.offset]
+        self.keys, self.values = k, v
 
     def _alloc(self, B, H, rows, D, device):
         wpr = D * self.bits // 32
@@ -83,10 +97,11 @@ class DequantKVCache:
     """laguna_mlx/cache.py:66-145 on B200. Single-token steps with ``fused_decode`` run the
     fused q8 decode kernel through ``attend``; other steps hand attention bf16 K/V."""
 
-    def __init__(self, group_size=64, bits=8, quantized_decode=False, fused_decode=False):
+    def __init__(self, group_size=64, bits=8, quantized_decode=False, fused_decode=False,
+                 capacity=0):
         if fused_decode and (bits, group_size) != (8, 64):
             raise ValueError("fused_decode needs 8-bit, group_size 64")
-        self.q = QuantizedKVCache(group_size=group_size, bits=bits)
+        self.q = QuantizedKVCache(group_size=group_size, bits=bits, capacity=capacity)
         self.quantized_decode = quantized_decode
         self.fused_decode = fused_decode
         self._quantized_step = False
@@ -149,8 +164,10 @@ class DequantKVCache:
         return self.q.nbytes
 
 
-def make_quantized_cache(model, bits=8, group_size=64, quantized_decode=False, fused_decode=False):
-    """laguna_mlx/cache.py:147-157: quantized K/V on full-attention layers. Sliding layers
+def make_quantized_cache(model, bits=8, group_size=64, quantized_decode=False, fused_decode=False,
+                         capacity=0):
+    """laguna_mlx/cache.py:147-157: quantized K/V on full-attention layers (``capacity``
+    preallocates rows, as one-token steps replayed from a CUDA graph need). Sliding layers
     are outside this build's scope (every BASELINE config uses full attention)."""
     a = model.args
     if a.head_dim % group_size:
@@ -160,5 +177,6 @@ def make_quantized_cache(model, bits=8, group_size=64, quantized_decode=False, f
         if lt == "sliding_attention":
             raise NotImplementedError("sliding-window layers are not part of this build")
         caches.append(DequantKVCache(group_size=group_size, bits=bits,
-                                     quantized_decode=quantized_decode, fused_decode=fused_decode))
+                                     quantized_decode=quantized_decode, fused_decode=fused_decode,
+                                     capacity=capacity))
     return caches

@@ -107,6 +107,20 @@ __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float
                : "memory");
 }
 
+// ---- MLX affine quantization of one group (the library's quantizer arithmetic) ------------
+// scale = bf16((max - min) / (2^bits - 1)), bias = bf16(min) (IEEE division); a value's code is
+// rint((v - bias) / scale) clamped to [0, 2^bits - 1] (0 when scale == 0).
+__device__ __forceinline__ void quant_group_params(float lo, float hi, float nb,
+                                                   __nv_bfloat16* sbf, __nv_bfloat16* bbf) {
+  *sbf = __float2bfloat16_rn(__fdiv_rn(hi - lo, nb));
+  *bbf = __float2bfloat16_rn(lo);
+}
+__device__ __forceinline__ uint32_t quant_code(float v, float s, float bv, float nb) {
+  float q = (s == 0.f) ? 0.f : rintf(__fdiv_rn(v - bv, s));
+  q = fminf(fmaxf(q, 0.f), nb);
+  return (uint32_t)q;
+}
+
 // ---- programmatic dependent launch (PDL) -------------------------------------------------
 // Kernels of the decode chain may be launched so that they start while the previous kernel in
 // the stream is still running (lg_set_pdl). Each such kernel calls pdl_wait() before it reads

@@ -208,15 +208,55 @@ struct PrepArgs {
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   __nv_bfloat16* gate_out;
+  // 8-bit g64 cache destination instead of k_cache / v_cache (null: bf16 cache): words
+  // [Hkv, cap, D/4], scales and biases [Hkv, cap, D/64]
+  uint32_t* kq;
+  __nv_bfloat16 *ks, *kb;
+  uint32_t* vq;
+  __nv_bfloat16 *vs, *vb;
 };
 
-// one CTA (D/2 threads) per (token, head slot): slots [0, Hq) q heads, [Hq, Hq+Hkv) k heads,
+// Quantize a staged row (bf16-valued floats, D of them, D % 64 == 0) into cache row `row` of an
+// 8-bit g64 packed cache; the arithmetic of quantize_rows_kernel (quant.cu). The CTA's first
+// D/4 threads take part; contains barriers (every thread calls it).
+__device__ __forceinline__ void quantize_row8(const float* v, int D, size_t row, uint32_t* q,
+                                              __nv_bfloat16* sc, __nv_bfloat16* bi,
+                                              float* sgrp) {
+  const int i = threadIdx.x, ng = D / 64;
+  if (i < ng) {
+    float lo = INFINITY, hi = -INFINITY;
+    for (int j = 0; j < 64; ++j) {
+      lo = fminf(lo, v[i * 64 + j]);
+      hi = fmaxf(hi, v[i * 64 + j]);
+    }
+    __nv_bfloat16 sbf, bbf;
+    quant_group_params(lo, hi, 255.f, &sbf, &bbf);
+    sgrp[2 * i] = bf2f(sbf);
+    sgrp[2 * i + 1] = bf2f(bbf);
+    sc[row * ng + i] = sbf;
+    bi[row * ng + i] = bbf;
+  }
+  __syncthreads();
+  if (i < D / 4) {
+    const int g = i / 16;
+    const float s = sgrp[2 * g], bv = sgrp[2 * g + 1];
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) word |= quant_code(v[4 * i + j], s, bv, 255.f) << (8 * j);
+    q[row * (D / 4) + i] = word;
+  }
+}
+
+// one CTA (D/2 threads) per (token, head slot) (grid x: tokens, y: slots): slots [0, Hq) q
+// heads, [Hq, Hq+Hkv) k heads,
 // [Hq+Hkv, Hq+2Hkv) v heads
 __global__ void attn_prep_kernel(PrepArgs a) {
   __shared__ float red[8];
+  __shared__ float stage[256];  // a k/v row on its way into an 8-bit cache
+  __shared__ float sgrp[8];
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
+  const int t = blockIdx.x, slot = blockIdx.y, i = threadIdx.x;
   const int D = a.D, half = D / 2;
   const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
   const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
@@ -224,7 +264,12 @@ __global__ void attn_prep_kernel(PrepArgs a) {
   if (slot >= a.Hq + a.Hkv) {  // v: copy into the cache
     const int h = slot - a.Hq - a.Hkv;
     const __nv_bfloat16* src = row + (a.Hq + a.Hkv + h) * D;
-    if (pos < a.cap) {
+    if (a.vq) {
+      stage[i] = bf2f(src[i]);
+      stage[i + half] = bf2f(src[i + half]);
+      __syncthreads();
+      if (pos < a.cap) quantize_row8(stage, D, (size_t)h * a.cap + pos, a.vq, a.vs, a.vb, sgrp);
+    } else if (pos < a.cap) {
       __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + pos) * D;
       dst[i] = src[i];
       dst[i + half] = src[i + half];
@@ -265,6 +310,11 @@ __global__ void attn_prep_kernel(PrepArgs a) {
       go[i] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i])));
       go[i + half] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i + half])));
     }
+  } else if (a.kq) {
+    stage[i] = round_bf16(o0);
+    stage[i + half] = round_bf16(o1);
+    __syncthreads();
+    if (pos < a.cap) quantize_row8(stage, D, (size_t)h * a.cap + pos, a.kq, a.ks, a.kb, sgrp);
   } else if (pos < a.cap) {
     __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + pos) * D;
     dst[i] = __float2bfloat16_rn(o0);
@@ -407,14 +457,15 @@ extern "C" int lg_embed(const int32_t* ids, int T, const uint32_t* w_q, const vo
   return LG_OK;
 }
 
-extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
-                            const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
-                            int pos_host, int gate_per_head, void* q_out, void* k_cache,
-                            void* v_cache, int cap, void* gate_out, void* stream) {
+static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                         const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                         int pos_host, int gate_per_head, void* q_out, void* k_cache,
+                         void* v_cache, const uint32_t* const* q8, const void* const* q8sb,
+                         int cap, void* gate_out, void* stream) {
   LG_CHECK_ARG(D % 64 == 0 && D <= 256 && Hq > 0 && Hkv > 0 && T >= 0,
                "attn_prep: head_dim %d (need a multiple of 64, <= 256)", D);
   if (T == 0) return LG_OK;
-  LG_CHECK_ARG(qkvg && qn_w && kn_w && q_out && k_cache && v_cache && gate_out,
+  LG_CHECK_ARG(qkvg && qn_w && kn_w && q_out && ((k_cache && v_cache) || q8) && gate_out,
                "attn_prep: NULL pointer");
   LG_CHECK_ARG(pos_dev || (pos_host >= 0 && pos_host + T <= cap),
                "attn_prep: positions %d..%d beyond the cache capacity %d", pos_host,
@@ -437,11 +488,40 @@ extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, con
   a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
   a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
   a.gate_out = static_cast<__nv_bfloat16*>(gate_out);
+  a.kq = q8 ? const_cast<uint32_t*>(q8[0]) : nullptr;
+  a.vq = q8 ? const_cast<uint32_t*>(q8[1]) : nullptr;
+  a.ks = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[0])) : nullptr;
+  a.kb = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[1])) : nullptr;
+  a.vs = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[2])) : nullptr;
+  a.vb = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[3])) : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dim3 grid(Hq + 2 * Hkv, T);
+  dim3 grid(T, Hq + 2 * Hkv);  // tokens on x: prefill lengths beyond 65,535
   LG_CUDA_TRY(launch_k(attn_prep_kernel, grid, dim3(D / 2), 0, st, a));
   LG_LAUNCH_CHECK("attn_prep");
   return LG_OK;
+}
+
+extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                            const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                            int pos_host, int gate_per_head, void* q_out, void* k_cache,
+                            void* v_cache, int cap, void* gate_out, void* stream) {
+  LG_CHECK_ARG(k_cache && v_cache, "attn_prep: NULL cache");
+  return attn_prep_run(qkvg, T, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, pos_host,
+                       gate_per_head, q_out, k_cache, v_cache, nullptr, nullptr, cap, gate_out,
+                       stream);
+}
+
+extern "C" int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
+                               const void* kn_w, float eps, float rope_theta,
+                               const int32_t* pos_dev, int pos_host, int gate_per_head,
+                               void* q_out, uint32_t* k_q, void* k_s, void* k_b, uint32_t* v_q,
+                               void* v_s, void* v_b, int cap, void* gate_out, void* stream) {
+  LG_CHECK_ARG(k_q && k_s && k_b && v_q && v_s && v_b, "attn_prep_q8: NULL cache");
+  LG_CHECK_ARG(D <= 256, "attn_prep_q8: head_dim %d > 256", D);
+  const uint32_t* q8[2] = {k_q, v_q};
+  const void* sb[4] = {k_s, k_b, v_s, v_b};
+  return attn_prep_run(qkvg, T, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, pos_host,
+                       gate_per_head, q_out, nullptr, nullptr, q8, sb, cap, gate_out, stream);
 }
 
 extern "C" int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,

@@ -149,7 +149,15 @@ struct Q8Args {
   float2* part_ml;          // [B * Hkv][q8_ml_stride]: (max, sum) per split and head
   float* part_acc;          // [B * Hkv, nsplit, G, D]
   __nv_bfloat16* out;       // [B, Hq, D]
+  const int* n_dev;         // the valid length is *n_dev + n_add (<= n, the planned length)
+  int n_add;
+  const __nv_bfloat16* gate;  // [B, Hq] per-head output gate, or null
 };
+
+// bf16(bf16(v) * gate) (the attention output times the per-head gate, laguna.py:105-106)
+__device__ __forceinline__ float q8_gated(float v, const Q8Args& a, size_t head) {
+  return a.gate ? round_bf16(v) * bf2f(a.gate[head]) : v;
+}
 
 template <int NT, bool SC_TMA>
 __global__ void __launch_bounds__(QA_THREADS, 1)
@@ -164,7 +172,8 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
   const int bh = b * a.Hkv + hk;
   const int head_row0 = bh * a.cap;  // < 2^31 (checked on the host)
   const int tile0 = split * a.tpc;     // this CTA's tiles: [tile0, tile0 + tpc) of the head
-  const int k_end = a.n;
+  const int n_valid = a.n_dev ? min(*a.n_dev + a.n_add, a.n) : a.n;
+  const int k_end = n_valid;
 
   uint8_t* kvw = sm + QA_OFF_KV + warp * QA_STAGES * 2 * QA_TILE;
   uint8_t* scw = sm + QA_OFF_SC + warp * QA_STAGES * 4 * QA_SCS;
@@ -175,7 +184,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
   float* s_M = reinterpret_cast<float*>(sm + QA_OFF_HEAD);
   float* s_L = s_M + 16;
   int* s_flag = reinterpret_cast<int*>(sm + QA_OFF_FLAG);  // [0] wait error, [1] merge role
-  const int ntile = min(a.tpc, (a.n + QA_TK - 1) / QA_TK - tile0);
+  const int ntile = min(a.tpc, (n_valid + QA_TK - 1) / QA_TK - tile0);
   const int nw = ntile > warp ? (ntile - warp + QA_WARPS - 1) / QA_WARPS : 0;  // warp's tiles
 
   uint64_t* mbar_m = reinterpret_cast<uint64_t*>(sm + QA_OFF_MBAR);
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
     const uint8_t* Vt = Kt + QA_TILE;
     uint8_t* St = scw + s * 4 * QA_SCS;
     if (!SC_TMA) {  // scale arrays not 16-byte addressable per tile: plain loads
-      const size_t row = (size_t)head_row0 + min(t0 + lane, a.n - 1);
+      const size_t row = (size_t)head_row0 + min(t0 + lane, n_valid - 1);
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         reinterpret_cast<uint32_t*>(St + q * QA_SCS)[lane] = __ldg(a.sc[q] + row);
@@ -556,8 +565,9 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
       }
       const float inv = 1.f / s_L[h];
       if (bad) v0 = v1 = __int_as_float(0x7fc00000);
-      *reinterpret_cast<__nv_bfloat162*>(a.out + ((size_t)b * a.Hq + hk * G + h) * QA_D + d) =
-          __floats2bfloat162_rn(v0 * inv, v1 * inv);
+      const size_t head = (size_t)b * a.Hq + hk * G + h;
+      *reinterpret_cast<__nv_bfloat162*>(a.out + head * QA_D + d) =
+          __floats2bfloat162_rn(q8_gated(v0 * inv, a, head), q8_gated(v1 * inv, a, head));
     }
     return;
   }
@@ -661,10 +671,10 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
       }
     }
     if (bad) o.x = o.y = o.z = o.w = __int_as_float(0x7fc00000);
-    __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(
-        a.out + ((size_t)b * a.Hq + hk * G + h) * QA_D + 4 * d4);
-    dst[0] = __floats2bfloat162_rn(o.x, o.y);
-    dst[1] = __floats2bfloat162_rn(o.z, o.w);
+    const size_t head = (size_t)b * a.Hq + hk * G + h;
+    __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(a.out + head * QA_D + 4 * d4);
+    dst[0] = __floats2bfloat162_rn(q8_gated(o.x, a, head), q8_gated(o.y, a, head));
+    dst[1] = __floats2bfloat162_rn(q8_gated(o.z, a, head), q8_gated(o.w, a, head));
   }
   if (threadIdx.x == 0) a.counters[bh * 32] = 0;  // leave the counter at zero for the next call
 }
@@ -782,6 +792,9 @@ struct Q8Call {
   const void* sc[4];  // ks, kb, vs, vb
   int B, Hq, Hkv, cap, n;
   __nv_bfloat16* out;
+  const int* n_dev = nullptr;  // device-side length (*n_dev + n_add), planned for n
+  int n_add = 0;
+  const __nv_bfloat16* gate = nullptr;
 };
 
 template <int NT, bool SCT>
@@ -809,6 +822,9 @@ int launch_q8_decode(const Q8Call& c, float scale, void* ws, cudaStream_t st) {
   a.cap = c.cap;
   a.n = c.n;
   a.out = c.out;
+  a.n_dev = c.n_dev;
+  a.n_add = c.n_add;
+  a.gate = c.gate;
   q8_split(a.B, a.Hkv, a.n, &a.tpc, &a.nsplit);
   if (a.nsplit > 1 && a.B * a.Hkv > QA_CTRL_SLOTS)
     return fail(LG_ERR_UNSUPPORTED, "q8 decode: %d splits for %d (batch, kv head) pairs",
@@ -971,4 +987,24 @@ extern "C" int lg_q8_decode_attention_noalloc(const void* q, int B, int Hq, int 
   LG_CUDA_TRY(cudaMemsetAsync(base, 0, cb, st));
   return launch_q8_decode(make_call(q, B, Hq, Hkv, k_q, k_s, k_b, v_q, v_s, v_b, cap, n, out),
                           scale, base, st);
+}
+
+extern "C" int lg_q8_decode_attention_dev(const void* q, int B, int Hq, int Hkv, int D,
+                                          const uint32_t* k_q, const void* k_s, const void* k_b,
+                                          const uint32_t* v_q, const void* v_s, const void* v_b,
+                                          int cap, int n_plan, const int32_t* n_dev, int n_add,
+                                          float scale, const void* gate, void* out,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_q8_args(q, B, Hq, Hkv, D, k_q, k_s, k_b, v_q, v_s, v_b, cap, n_plan, out);
+  if (rc) return rc;
+  LG_CHECK_ARG(n_dev != nullptr, "q8 decode: n_dev is NULL (use lg_q8_decode_attention)");
+  LG_CHECK_ARG(!gate || aligned(gate, 2), "q8 decode: gate must be 2-byte aligned");
+  const size_t need = lg_q8_decode_workspace_bytes(B, Hq, Hkv, n_plan);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(LG_ERR_WORKSPACE, "q8 decode: workspace needs %zu bytes (256-aligned)", need);
+  Q8Call c = make_call(q, B, Hq, Hkv, k_q, k_s, k_b, v_q, v_s, v_b, cap, n_plan, out);
+  c.n_dev = n_dev;
+  c.n_add = n_add;
+  c.gate = static_cast<const __nv_bfloat16*>(gate);
+  return launch_q8_decode(c, scale, workspace, static_cast<cudaStream_t>(stream));
 }

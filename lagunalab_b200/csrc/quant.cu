@@ -41,18 +41,15 @@ __global__ void quantize_rows_kernel(const void* __restrict__ x, int x_f32, int 
       lo = fminf(lo, v);
       hi = fmaxf(hi, v);
     }
-    const __nv_bfloat16 sbf = __float2bfloat16_rn(__fdiv_rn(hi - lo, nb));
-    const __nv_bfloat16 bbf = __float2bfloat16_rn(lo);
+    __nv_bfloat16 sbf, bbf;
+    quant_group_params(lo, hi, nb, &sbf, &bbf);
     const float s = bf2f(sbf), bv = bf2f(bbf);
     const size_t row = ((size_t)b * H + h) * cap + offset + l;
     uint32_t* wrow = dq + row * (D * BITS / 32) + (size_t)g * (group * BITS / 32);
     for (int w = 0; w < group / per_word; ++w) {
       uint32_t word = 0;
       for (int j = 0; j < per_word; ++j) {
-        float v = ld(w * per_word + j);
-        float q = (s == 0.f) ? 0.f : rintf(__fdiv_rn(v - bv, s));
-        q = fminf(fmaxf(q, 0.f), nb);
-        word |= (uint32_t)q << (BITS * j);
+        word |= quant_code(ld(w * per_word + j), s, bv, nb) << (BITS * j);
       }
       wrow[w] = word;
     }

@@ -411,6 +411,10 @@ class Attention:
             qkvg = self._qkvg(in_norm(x).reshape(L, H))
         if cache is None:
             cache = KVCache()
+        if getattr(cache, "q", None) is not None:  # 8-bit quantized cache (DequantKVCache)
+            o = self._q8_attention(qkvg, L, cache, pos_dev, x.device)
+            out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
+            return out.reshape(B, L, H)
         if pos_dev is not None:
             if L != 1 or cache.keys is None:
                 raise ValueError("device-position steps are single-token steps on a sized cache")
@@ -452,6 +456,49 @@ class Attention:
             o = (o * g).reshape(L, Hq * D)
         out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
         return out.reshape(B, L, H)
+
+
+    def _q8_attention(self, qkvg, L, cache, pos_dev, device):
+        """Attention over an 8-bit group-64 DequantKVCache (laguna_mlx/cache.py:89-106): the new
+        k, v rows are quantized into the packed cache; single-token steps with ``fused_decode``
+        attend straight off the packed rows (q8 kernel), other steps over dequantized rows."""
+        Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
+        qc = cache.q
+        qc.reserve(1, Hkv, D, L, device)
+        cap = qc.keys[0].shape[2]
+        per_head = self.per_head_gate
+        if pos_dev is not None:
+            if L != 1 or not cache.fused_decode:
+                raise ValueError("device-position steps are fused single-token steps")
+            q, gate = ops.attn_prep_q8(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                       self.eps, self.rope_theta, qc.keys, qc.values,
+                                       pos_dev=pos_dev, gate_per_head=per_head)
+            o = ops.q8_decode_attention_dev(q.view(1, Hq, D), qc.keys, qc.values, cap, pos_dev,
+                                            1, self.scale, gate=gate if per_head else None)
+            o = o.view(1, Hq * D)
+            return o if per_head else o * gate.view(1, Hq * D)
+        pos = qc.offset
+        q, gate = ops.attn_prep_q8(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                   self.eps, self.rope_theta, qc.keys, qc.values, pos=pos,
+                                   gate_per_head=per_head)
+        qc.offset += L
+        n = pos + L
+        cache.fused_step = cache.fused_decode and L == 1
+        if cache.fused_step:
+            o = ops.q8_decode_attention(q.view(1, Hq, 1, D), qc.keys, qc.values, n, self.scale)
+            g = gate.view(1, Hq, 1) if per_head else gate.view(1, Hq, D)
+            return (o.view(1, Hq, D) * g).reshape(1, Hq * D)
+        k = ops.dequantize_rows(qc.keys, n, qc.group_size, qc.bits)
+        v = ops.dequantize_rows(qc.values, n, qc.group_size, qc.bits)
+        mask_ = None
+        if pos:
+            qp = torch.arange(L, device=device)[:, None] + pos
+            mask_ = torch.arange(n, device=device)[None, :] <= qp
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q.unsqueeze(0), k, v, attn_mask=mask_, is_causal=mask_ is None and L > 1,
+            scale=self.scale, enable_gqa=True)[0].transpose(0, 1)  # [L, Hq, D]
+        g = gate[..., None] if per_head else gate.view(L, Hq, D)
+        return (o * g).reshape(L, Hq * D)
 
 
 class DecoderLayer:
@@ -597,7 +644,8 @@ class DecodeGraph:
         self.model, self.cache = model, cache
         self.tok = tok.reshape(1).to(torch.int32).clone()
         self.pos = torch.tensor([cache[0].offset], dtype=torch.int32, device=self.tok.device)
-        self.cap = cache[0].keys.shape[2]
+        c0 = cache[0]
+        self.cap = c0.q.keys[0].shape[2] if getattr(c0, "q", None) is not None else c0.keys.shape[2]
         self.steps = 0
         self._body()  # one real step, eagerly
         self.steps = 1

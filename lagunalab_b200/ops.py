@@ -451,6 +451,43 @@ def attn_prep(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos=0,
     return q, gate
 
 
+def attn_prep_q8(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, keys, values, pos=0, pos_dev=None,
+                 gate_per_head=True):
+    """attn_prep with an 8-bit group-64 cache: the new k, v rows are quantized into rows
+    pos + t of the packed caches keys/values = (words [B=1, Hkv, cap, D/4], scales, biases)."""
+    qkvg = _c(qkvg, torch.bfloat16)
+    T = qkvg.shape[0]
+    kq, ks, kb = keys
+    vq, vs, vb = values
+    cap = kq.shape[-2]
+    q = torch.empty(Hq, T, D, dtype=torch.bfloat16, device=qkvg.device)
+    gate = torch.empty(T, Hq if gate_per_head else Hq * D, dtype=torch.bfloat16, device=qkvg.device)
+    _lib.call("lg_attn_prep_q8", _p(qkvg), T, Hq, Hkv, D, _p(_c(qn_w)), _p(_c(kn_w)), float(eps),
+              float(theta), _p(pos_dev), int(pos), int(bool(gate_per_head)), _p(q),
+              _p(kq), _p(ks), _p(kb), _p(vq), _p(vs), _p(vb), cap, _p(gate),
+              _stream(qkvg.device))
+    return q, gate
+
+
+def q8_decode_attention_dev(q, keys, values, n_plan, n_dev, n_add, scale, gate=None, out=None):
+    """Single-token attention over the packed 8-bit cache with the valid length on the device
+    (n_dev[0] + n_add), planned for n_plan keys; optional per-head gate [B, Hq]. q [B, Hq, D]
+    -> [B, Hq, D] bf16."""
+    q = _c(q, torch.bfloat16)
+    B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
+    kq, ks, kb = (_c(t) for t in keys)
+    vq, vs, vb = (_c(t) for t in values)
+    Hkv, cap = kq.shape[1], kq.shape[2]
+    nb = _lib.lib().lg_q8_decode_workspace_bytes(B, Hq, Hkv, int(n_plan))
+    ws = workspace(q.device, "q8", nb, zero=True)
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
+    _lib.call("lg_q8_decode_attention_dev", _p(q), B, Hq, Hkv, D, _p(kq), _p(ks), _p(kb), _p(vq),
+              _p(vs), _p(vb), cap, int(n_plan), _p(n_dev), int(n_add), float(scale),
+              _p(_c(gate)), _p(out), _p(ws), ws.numel(), _stream(q.device))
+    return out
+
+
 def bf16_decode_attention(q, k_cache, v_cache, n, scale, gate=None, n_dev=None, n_add=0,
                           n_plan=None, out=None):
     """Single-token attention over a bf16 cache. q [B, Hq, D]; caches [B, Hkv, cap, D];

@@ -80,16 +80,30 @@ def sdpa(q, k, v, scale, q_pos0):
 
 
 class Cache:
-    """bf16-valued K/V per layer ([Hkv, S, D] fp32 tensors)."""
+    """K/V per layer ([Hkv, S, D] fp32 tensors): bf16-valued, or with ``kv_bits=8`` the rows
+    as an 8-bit group-64 DequantKVCache holds them (laguna_mlx/cache.py:66-106): quantized by
+    the build's quantizer on append, dequantized as fp32 scale * code + bias (the fused
+    single-token kernel's view, q8_attn.py:50) — multi-token steps see them rounded to bf16
+    (mx.dequantize's output, cache.py:99-100)."""
 
-    def __init__(self, n_layers):
+    def __init__(self, n_layers, kv_bits=None):
         self.k = [None] * n_layers
         self.v = [None] * n_layers
         self.offset = 0
+        self.kv_bits = kv_bits
+
+    def _qdq(self, x):
+        from . import attn_ref, mlx_quant
+        packed, s_bits, b_bits = attn_ref.quantize_rows(x.numpy(), 64, self.kv_bits)
+        return torch.from_numpy(mlx_quant.dequantize(packed, s_bits, b_bits, 64, self.kv_bits))
 
     def update(self, i, k, v):
+        if self.kv_bits:
+            k, v = self._qdq(k), self._qdq(v)
         self.k[i] = k if self.k[i] is None else torch.cat([self.k[i], k], dim=1)
         self.v[i] = v if self.v[i] is None else torch.cat([self.v[i], v], dim=1)
+        if self.kv_bits and k.shape[1] > 1:
+            return _bf(self.k[i]), _bf(self.v[i])
         return self.k[i], self.v[i]
 
 
@@ -139,11 +153,12 @@ def forward(W, args, ids, cache=None):
     return moe_ref.qlinear(rmsnorm(x, W["norm"], eps), W["lm_head"])
 
 
-def greedy(W, args, prompt, steps):
+def greedy(W, args, prompt, steps, kv_bits=None):
     """Greedy decode (prefill, then one token at a time). Returns (tokens, gaps): gaps[i] is
     the logit margin between the chosen token and the runner-up at step i (a margin within
-    a bf16 rounding of the logits marks a near-tie that other rounding orders may flip)."""
-    cache = Cache(len(W["layers"]))
+    a bf16 rounding of the logits marks a near-tie that other rounding orders may flip).
+    ``kv_bits=8``: an 8-bit quantized KV cache (see ``Cache``)."""
+    cache = Cache(len(W["layers"]), kv_bits)
     logits = forward(W, args, prompt, cache)
     toks, gaps = [], []
     for _ in range(steps):
