@@ -214,6 +214,7 @@ class SparseMoeBlock:
         sw = self.switch_mlp
         fused = _fused_experts(sw)
         if fused is not None:
+            _note_picks(sw, inds.numel())
             sh = self.shared_expert.mats if self.shared_expert is not None else None
             out = ops.moe_experts(x.reshape(-1, H), inds.reshape(-1, self.top_k),
                                   w.reshape(-1, self.top_k), self.routed_scaling_factor,
@@ -263,8 +264,16 @@ class SparseMoeBlock:
                                         self.e_score_correction_bias, self.top_k,
                                         self.norm_topk_prob, self.score_fn)
         sh = self.shared_expert.mats if self.shared_expert is not None else None
+        _note_picks(self.switch_mlp, self.top_k)
         return ops.moe_decode(xn, inds, w, self.routed_scaling_factor, fused.mats, sh,
                               residual=h.reshape(1, H))
+
+
+def _note_picks(sw, n):
+    """Expert picks served by the fused kernels, for a resident expert store's statistics."""
+    note = getattr(sw, "note_picks", None)
+    if note is not None:
+        note(n)
 
 
 def _fused_experts(sw):
@@ -628,6 +637,71 @@ class Model:
             return True
 
         return predicate
+
+
+def model_from_weights(args, weights, quantization=None, device="cuda", switch_mlps=None):
+    """A ``Model`` from MLX parameter names (laguna.py:169-241 after ``sanitize`` and
+    ``nn.quantize``): quantized linears as ``<path>.weight`` (uint32 words), ``.scales``,
+    ``.biases``; norms as ``<path>.weight``; the router's ``e_score_correction_bias`` in fp32.
+    ``quantization``: {"group_size", "bits", "<path>": {...} per-module overrides} (the
+    config's "quantization" entry). ``switch_mlps``: {layer: SwitchGLU-like} for MoE layers
+    whose routed experts come from elsewhere (an expert pack)."""
+    q = dict(quantization or {"group_size": 64, "bits": 4})
+    dev = torch.device(device)
+
+    def t(name, dtype=None):
+        v = weights[name]
+        if v.dtype == torch.uint32:
+            v = v.view(torch.int32)
+        v = v.to(dev)
+        return v.to(dtype) if dtype is not None else v
+
+    def qcfg(path):
+        o = q.get(path, {})
+        return o.get("group_size", q["group_size"]), o.get("bits", q["bits"])
+
+    def lin(path, cls=QuantizedLinear):
+        if f"{path}.scales" not in weights:  # unquantized (fp32 router)
+            return t(f"{path}.weight", torch.float32)
+        g, b = qcfg(path)
+        return cls(t(f"{path}.weight"), t(f"{path}.scales", torch.bfloat16),
+                   t(f"{path}.biases", torch.bfloat16), g, b)
+
+    def norm(path, n):
+        return RMSNorm(n, args.rms_norm_eps, t(f"{path}.weight", torch.bfloat16))
+
+    H, D = args.hidden_size, args.head_dim
+    layers = []
+    for i in range(args.num_hidden_layers):
+        p = f"model.layers.{i}"
+        at = Attention(args, i, *(lin(f"{p}.self_attn.{n}") for n in
+                                  ("q_proj", "k_proj", "v_proj", "o_proj", "g_proj")),
+                       norm(f"{p}.self_attn.q_norm", D), norm(f"{p}.self_attn.k_norm", D))
+        if i in args.mlp_only_layers:
+            I = args.intermediate_size
+            mlp = MLP(H, I, *(lin(f"{p}.mlp.{n}") for n in ("gate_proj", "up_proj", "down_proj")))
+        else:
+            if switch_mlps is not None and i in switch_mlps:
+                sw = switch_mlps[i]
+            else:
+                sw = SwitchGLU(H, args.moe_intermediate_size, args.num_experts,
+                               *(lin(f"{p}.mlp.switch_mlp.{n}", SwitchLinear)
+                                 for n in ("gate_proj", "up_proj", "down_proj")))
+            sh = None
+            if f"{p}.mlp.shared_expert.gate_proj.weight" in weights:
+                sh = MLP(H, args.shared_expert_intermediate_size,
+                         *(lin(f"{p}.mlp.shared_expert.{n}")
+                           for n in ("gate_proj", "up_proj", "down_proj")))
+            bias_key = f"{p}.mlp.e_score_correction_bias"
+            bias = t(bias_key, torch.float32) if bias_key in weights else \
+                torch.zeros(args.num_experts, device=dev)
+            mlp = SparseMoeBlock(args, lin(f"{p}.mlp.gate"), bias, sw, sh)
+        layers.append(DecoderLayer(args, i, at, mlp, norm(f"{p}.input_layernorm", H),
+                                   norm(f"{p}.post_attention_layernorm", H)))
+    emb = lin("model.embed_tokens")
+    embed = QuantizedEmbedding(emb.weight, emb.scales, emb.biases, emb.group_size, emb.bits)
+    model = LagunaModel(args, embed, layers, norm("model.norm", H))
+    return Model(args, model, lin("lm_head"))
 
 
 class DecodeGraph:
