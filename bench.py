@@ -387,7 +387,7 @@ def run_decode(args, wl, ws, rank):
     V = margs.vocab_size
     g = torch.Generator().manual_seed(wl["seed"])
     prompt = torch.randint(0, V, (wl["prefill"],), generator=g).to(torch.int32).cuda()
-    n_steps = 1 + args.warmup + args.steps + 1 + max(1, args.warmup) + args.steps
+    n_steps = 1 + args.warmup + args.steps + 1 + max(1, args.warmup) + args.steps + 2 + 12
     cap = (wl["prefill"] + n_steps + 255) // 256 * 256
     if wl.get("kv") == "q8":
         from lagunalab_b200 import cache as qcache
@@ -413,7 +413,9 @@ def run_decode(args, wl, ws, rank):
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.3)
     clocks.mark(True)
+    torch.cuda.nvtx.range_push("decode_step")
     ms, _ = timed_graph(dg.graph, args.steps, stream)
+    torch.cuda.nvtx.range_pop()
     dg.steps += args.steps
     ctx1 = dg.position()
     # end to end: every step uploads the input token from pinned host memory, runs the step
@@ -444,9 +446,45 @@ def run_decode(args, wl, ws, rank):
     torch.cuda.synchronize()
     e2e_ms = s0.elapsed_time(s1) / args.steps
     clocks.mark(False)
+    # the dominant kernel, timed live: a graph of the same step in which the library records
+    # an event pair around that stage's launches (the pair ends up around the step's last one)
+    from lagunalab_b200 import _lib
+    L = _lib.lib()
+    stage = "q8_decode" if wl.get("kv") == "q8" else "moe_decode"
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev[0].record()
+    ev[1].record()
+    L.lg_profile_stage(stage.encode(), ev[0].cuda_event, ev[1].cuda_event)
+    prev = L.lg_set_pdl(1)
+    gk = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(gk):
+            dg._body()
+    finally:
+        L.lg_set_pdl(prev)
+        L.lg_profile_stage(None, None, None)
+    kt = []
+    for _ in range(12):
+        gk.replay()
+        torch.cuda.synchronize()
+        kt.append(_lib.event_elapsed_ms(ev[0], ev[1]))
+    kernel_ms = statistics.median(kt[2:])
+    ctx_k = dg.position()
     ctx = (ctx0 + ctx1) / 2
-    del ge
+    del ge, gk
+    a_ = model.args
+    if stage == "q8_decode":
+        kbytes = ctx_k * a_.num_key_value_heads * (2 * (a_.head_dim + 4 * (a_.head_dim // 64)))
+    else:
+        nb = lambda m: sum(t.numel() * t.element_size() for t in m.mat)
+        m = next(l.mlp for l in model.layers if hasattr(l.mlp, "switch_mlp"))
+        per_expert = sum(nb(p) for p in (m.switch_mlp.gate_proj, m.switch_mlp.up_proj,
+                                         m.switch_mlp.down_proj)) // a_.num_experts
+        kbytes = a_.num_experts_per_tok * per_expert + sum(
+            nb(p) for p in (m.shared_expert.gate_proj, m.shared_expert.up_proj,
+                            m.shared_expert.down_proj))
     return dict(ms=ms, e2e_ms=e2e_ms, launches=per_replay * args.steps, clocks=clocks,
+                kernel=stage, kernel_ms=kernel_ms, kernel_bytes=kbytes, kernel_ctx=ctx_k,
                 bytes=decode_bytes_per_token(model, ctx, wl.get("kv", "bf16")), ctx=(ctx0, ctx1),
                 prefill_ms=prefill_ms,
                 h2d=4, d2h=4)
@@ -665,14 +703,26 @@ def main():
         r = run_decode(args, wl, ws, rank)
         value = 1000.0 / r["ms"]
         e2e = 1000.0 / r["e2e_ms"]
-        achieved = r["bytes"] / (r["ms"] * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "whole decode step (every kernel of one token)",
-                "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk_kind,
-                "algorithmic": f"{r['bytes']:.0f} B per token (weights read by one step, top-k "
-                               f"experts, {wl['kv']} K/V at mean context "
-                               f"{sum(r['ctx']) / 2:.0f})",
-                "duration": "graph step time (one replay per token)"}
+        step_gbs = r["bytes"] / (r["ms"] * 1e-3) / 1e9
+        achieved = r["kernel_bytes"] / (r["kernel_ms"] * 1e-3) / 1e9
+        if r["kernel"] == "q8_decode":
+            prof, name = "q8_decode_kernel_config4", "q8_decode_kernel"
+            alg = (f"{r['kernel_bytes']:.0f} B per launch ({r['kernel_ctx']} keys x 4 kv heads x "
+                   f"272 B: 8-bit K and V rows with their bf16 scales and biases)")
+        else:
+            prof, name = "moe_decode_config3", "moe_dec_gateup_kernel + moe_dec_down_kernel"
+            alg = (f"{r['kernel_bytes']:.0f} B per call (top-k picked experts + shared expert, "
+                   f"gate/up/down at 0.5625 B per weight)")
+        roof = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                "traffic": profile_traffic(prof), "peak_source": pk_kind, "algorithmic": alg,
+                "duration": "CUDA events around the stage's last launch in a replayed step graph",
+                "traffic_source": f"profiles/{prof}.md (ncu, one launch)",
+                "step": {"achieved": step_gbs, "frac": step_gbs / pk["hbm_gbs"],
+                         "algorithmic": f"{r['bytes']:.0f} B per token (weights read by one "
+                                        f"step, top-k experts, {wl['kv']} K/V at mean context "
+                                        f"{sum(r['ctx']) / 2:.0f})",
+                         "duration": "graph step time (one replay per token)"}}
         wl = dict(wl, prefill_ms=r["prefill_ms"], context=list(r["ctx"]))
         dtype = "bf16"
     elif args.workload == "q8_decode":
