@@ -389,6 +389,9 @@ int lg_moe_decode(const void* xn, const int32_t* inds, const void* weights, int 
  * before the step); the work split is planned for n_plan >= that length (<= cap) and the
  * workspace sized by lg_q8_decode_workspace_bytes(B, Hq, Hkv, n_plan). gate: bf16 [B, Hq]
  * per-head output gate (laguna.py:105-106), out = bf16(bf16(attention) * gate), or NULL.
+ * With lg_set_pdl on, the kernel may start while its predecessor runs and streams the K/V
+ * tiles before waiting for it, except the tile holding row *n_dev + n_add - 1: the kernel
+ * launched just before may write that row (the new key of the step), no other.
  */
 int lg_q8_decode_attention_dev(const void* q, int B, int Hq, int Hkv, int D, const uint32_t* k_q,
                                const void* k_s, const void* k_b, const uint32_t* v_q,

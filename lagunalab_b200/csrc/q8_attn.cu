@@ -152,6 +152,7 @@ struct Q8Args {
   const int* n_dev;         // the valid length is *n_dev + n_add (<= n, the planned length)
   int n_add;
   const __nv_bfloat16* gate;  // [B, Hq] per-head output gate, or null
+  int early;                  // stream K/V tiles before the PDL wait (device-length calls)
 };
 
 // bf16(bf16(v) * gate) (the attention output times the per-head gate, laguna.py:105-106)
@@ -212,10 +213,21 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
         tma_load_2d(scw + s * 4 * QA_SCS + q * QA_SCS, &mp.s[q], &bars[s], 0, row >> 2);
     }
   };
+  // With a device-side length the kernel may start before its predecessor (the prologue that
+  // appends the newest key) finishes: the first stages of every tile but the one holding that
+  // row stream before the wait; the rest, and q, follow it.
+  const int last_tile = (n_valid - 1) / QA_TK;
+  auto early = [&](int j) { return a.early && tile0 + warp + QA_WARPS * j != last_tile; };
   if (lane == 0) {
     pol = l2_evict_first_policy();
-    for (int j = 0; j < QA_STAGES && j < nw; ++j) issue(j, j, 0);
+    for (int j = 0; j < QA_STAGES && j < nw; ++j)
+      if (early(j)) issue(j, j, 0);
   }
+  pdl_wait();
+  pdl_trigger();
+  if (lane == 0)
+    for (int j = 0; j < QA_STAGES && j < nw; ++j)
+      if (!early(j)) issue(j, j, 0);
 
   // ---- Q^T fragments (B operand of S^T = K Q^T): column n = head r (+ 8 nt) ----
   // k-block kb (group g = kb / 4, word wi = kb % 4) covers dims 64g + 16c4 + 4wi + {0..3}
@@ -807,7 +819,7 @@ static int q8_launch_one(dim3 grid, const Q8Maps& mp, const Q8Args& a, cudaStrea
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, QA_SMEM));
     attr_done |= 1ull << dev;
   }
-  q8_decode_kernel<NT, SCT><<<grid, QA_THREADS, QA_SMEM, st>>>(mp, a);
+  LG_CUDA_TRY(launch_k(q8_decode_kernel<NT, SCT>, grid, dim3(QA_THREADS), QA_SMEM, st, mp, a));
   return LG_OK;
 }
 
@@ -825,6 +837,7 @@ int launch_q8_decode(const Q8Call& c, float scale, void* ws, cudaStream_t st) {
   a.n_dev = c.n_dev;
   a.n_add = c.n_add;
   a.gate = c.gate;
+  a.early = c.n_dev != nullptr;
   q8_split(a.B, a.Hkv, a.n, &a.tpc, &a.nsplit);
   if (a.nsplit > 1 && a.B * a.Hkv > QA_CTRL_SLOTS)
     return fail(LG_ERR_UNSUPPORTED, "q8 decode: %d splits for %d (batch, kv head) pairs",
