@@ -358,8 +358,10 @@ size_t lg_router_decode_workspace_bytes(int E);
  * H % 512 == 0 or E % 8 == 0), else 0. */
 int lg_router_decode_supported(int H, int E);
 
-/* Workspace bytes of lg_moe_decode (the SwiGLU outputs of the k + 1 groups). */
-size_t lg_moe_decode_workspace_bytes(int I, int I_shared, int k);
+/* Workspace bytes of lg_moe_decode: a 4 KiB block of completion counters first (must start
+ * zeroed; completed calls of any size leave it so), then the groups' down outputs and SwiGLU
+ * outputs. */
+size_t lg_moe_decode_workspace_bytes(int H, int I, int I_shared, int k);
 
 /* 1 if lg_moe_decode takes these sizes (its shared-memory tiles fit), else 0. */
 int lg_moe_decode_supported(int H, int I, int I_shared, int k);
@@ -369,7 +371,8 @@ int lg_moe_decode_supported(int H, int I, int I_shared, int k);
  * sum_j bf16(w[j]) * routed_scale * y_j + y_shared) (+ residual, bf16 add), where y_j =
  * bf16(down_e(SwiGLU(gate_e xn, up_e xn))) for e = inds[j] (picks outside [0, E) contribute
  * nothing), y_shared the shared expert's output (I_shared = 0: none). Fixed summation order
- * (fp32, one rounding), two launches (gate/up + SwiGLU, then down + combine + residual).
+ * (fp32, one rounding), two launches (gate/up + SwiGLU; down per (16-row slice, group), the
+ * last group of a slice combining the slice and adding the residual).
  * Weights as lg_moe_experts, 16-byte aligned; H, I, I_shared multiples of 64.
  */
 int lg_moe_decode(const void* xn, const int32_t* inds, const void* weights, int H, int I, int E,

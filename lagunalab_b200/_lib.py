@@ -56,7 +56,7 @@ SIGNATURES = {
     "lg_router_decode": (c_int, [P, P, c_float, I, P, P, P, P, I, I, I, I, P, P, P, P, P,
                                  c_size_t, P]),
     "lg_router_decode_workspace_bytes": (c_size_t, [I]),
-    "lg_moe_decode_workspace_bytes": (c_size_t, [I, I, I]),
+    "lg_moe_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
     "lg_moe_decode_supported": (c_int, [I, I, I, I]),
     "lg_router_decode_supported": (c_int, [I, I]),
     "lg_decode_status": (c_int, [P, I]),

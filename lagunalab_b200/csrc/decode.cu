@@ -359,10 +359,30 @@ struct MdArgs {
   __nv_bfloat16* hbuf;       // [k + 1, Imax] SwiGLU outputs
   const __nv_bfloat16* res;  // [H] residual, or null
   __nv_bfloat16* out;        // [H]
+  float* ypart;              // [H/16][k + 1][16] per-group down outputs (bf16-valued)
+  unsigned int* counters;    // [H/16] groups done per 16-row slice (zero between calls)
 };
 
+// Workspace of lg_moe_decode: counters (a fixed 4 KiB block, one per 16-row slice for any H up
+// to 16,384, so calls of different sizes sharing one workspace never overlap them with data) |
+// per-group outputs [ceil(H/16)][k+1][16] fp32 | SwiGLU outputs [k+1][Imax] bf16.
+constexpr size_t MD_CTRL_BYTES = 4096;
+struct MdWs {
+  size_t counters, ypart, hbuf, total;
+};
+__host__ __device__ __forceinline__ MdWs md_ws(int H, int Imax, int k) {
+  auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const size_t nt = (H + 15) / 16, G = k + 1;
+  MdWs w;
+  w.counters = 0;
+  w.ypart = MD_CTRL_BYTES;
+  w.hbuf = w.ypart + up(4 * nt * G * 16);
+  w.total = w.hbuf + up(2 * G * (size_t)Imax);
+  return w;
+}
+
 constexpr int GU_WARPS = 8;
-constexpr int DN_WARPS = 16;
+constexpr int DN_WARPS = 4;
 
 // grid (Imax/16, k + 1): group j < k is pick j, group k the shared expert. Shared memory as
 // dgemv_kernel's with a two-tile (gate, up) stage.
@@ -394,6 +414,11 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_dec_gateup_kernel(MdArgs a)
   pdl_wait();
   pdl_trigger();
   if (rows <= 0) return;
+  // the normalised token (the router's output): its copy overlaps the read of the pick
+  const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.xn);
+  for (int c = tid; c < H / 8; c += NW * 32)
+    cp_async16(reinterpret_cast<uint8_t*>(xs) + c * 16, xsrc + (size_t)c * 16, pol, smem, slim);
+  cp_async_commit();
   if (!sh) {
     const int e = a.inds[j];
     if (e < 0 || e >= a.E) return;  // no expert: the down kernel skips this pick
@@ -404,8 +429,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_dec_gateup_kernel(MdArgs a)
     tile_load(ring + tb, uq, us, ub, m0, rows, H, pol, smem, slim);
     cp_async_commit();
   }
-  const uint4* xg = reinterpret_cast<const uint4*>(a.xn);
-  for (int i = tid; i < H / 8; i += NW * 32) xs[i] = xg[i];
+  cp_async_wait(sh ? 0 : 1);  // the activations (for a shared-expert CTA: everything)
   __syncthreads();
   group_sums(xs, gpr, gsum);
   const int gpw = (gpr + NW - 1) / NW;
@@ -436,144 +460,119 @@ __global__ void __launch_bounds__(GU_WARPS * 32) moe_dec_gateup_kernel(MdArgs a)
   if (tid < rows) a.hbuf[(size_t)j * a.Imax + m0 + tid] = swiglu_mlx(red2[tid], red2[16 + tid]);
 }
 
-// down kernel shared memory: picks [k+1] ints | weights [k+1] floats | red
-// [(k+1)][DN_WARPS][16] | red2 [(k+1)][16] | hs [(k+1)][Imax/8] uint4 | gsum [(k+1)][Imax/64] |
-// ring (k+1) tiles
-struct MdDownLayout {
-  uint32_t pick, wt, red, red2, hs, gsum, ring, tb, total;
-};
-__host__ __device__ __forceinline__ MdDownLayout md_down_layout(int k, int Imax) {
-  MdDownLayout L;
-  const uint32_t G = k + 1;
-  L.pick = 0;
-  L.wt = L.pick + 4 * G;
-  L.red = (L.wt + 4 * G + 15) & ~15u;
-  L.red2 = L.red + 4 * G * DN_WARPS * 16;
-  L.hs = (L.red2 + 4 * G * 16 + 15) & ~15u;
-  L.gsum = L.hs + 2 * G * Imax;
-  L.ring = (L.gsum + 4 * G * (Imax / 64) + 127) & ~127u;
-  L.tb = tile_bytes(Imax);
-  L.total = L.ring + G * L.tb;
-  return L;
-}
-
-// grid (ceil(H/16)): all k + 1 groups for one 16-row slice of the hidden dimension; the
-// DN_WARPS warps share the (group, 64-group) work items.
+// grid (ceil(H/16), k + 1): one 16-row slice of the hidden dimension for one group (pick j < k,
+// the shared expert j = k). The CTA is small, so it becomes resident beside the gate/up CTAs
+// and streams its weight tile before its wait (the picks come from the router, two kernels
+// back). Each CTA writes its group's bf16-rounded outputs; the last CTA of a slice to finish
+// combines the groups in fixed order (fp32, one rounding) and adds the residual.
 template <int V>
 __global__ void __launch_bounds__(DN_WARPS * 32) moe_dec_down_kernel(MdArgs a) {
   constexpr int NW = DN_WARPS, NT = NW * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int G = a.k + 1, Imax = a.Imax, H = a.H;
-  const MdDownLayout L = md_down_layout(a.k, Imax);
-  int* pick = reinterpret_cast<int*>(smem + L.pick);
-  float* wt = reinterpret_cast<float*>(smem + L.wt);
-  float* red = reinterpret_cast<float*>(smem + L.red);
-  float* red2 = reinterpret_cast<float*>(smem + L.red2);
-  uint4* hs = reinterpret_cast<uint4*>(smem + L.hs);
-  float* gsum = reinterpret_cast<float*>(smem + L.gsum);
-  uint8_t* ring = smem + L.ring;
+  float* red = reinterpret_cast<float*>(smem);      // [NW][16]
+  float* cw = red + NW * 16;                        // [G] combine weights (last CTA)
+  int* ce = reinterpret_cast<int*>(cw + 33);        // [G] picks (last CTA)
+  int* flag = ce + 33;
+  uint4* hs = reinterpret_cast<uint4*>(smem + 1024);                  // [Imax/8]
+  float* gsum = reinterpret_cast<float*>(smem + 1024 + 2 * Imax);     // [Imax/64]
+  uint8_t* tile = smem + ((1024 + 2 * Imax + 4 * (Imax / 64) + 127) & ~127);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = lane >> 2, c4 = lane & 3;
-  const int m0 = blockIdx.x * 16;
+  const int mt = blockIdx.x, j = blockIdx.y;
+  const int m0 = mt * 16;
   const int rows = min(16, H - m0);
+  (void)lane;
   // The picks come from the router, two kernels back, and the residual from the attention
-  // output projection, three back: both kernels have completed (the kernel in between waited
-  // for its predecessor before letting this one start), so they are read before the wait
-  // (L2 loads, not L1).
-  if (tid < G) {
-    int e = -2;  // -2: the shared expert; -1: no expert
-    float w = 1.0f;
-    if (tid < a.k) {
-      e = __ldcg(a.inds + tid);
-      if (e < 0 || e >= a.E) e = -1;
-      w = bf2f(__ldcg(a.w + tid)) * a.routed_scale;
-    } else if (a.I_sh == 0) {
-      e = -1;
-    }
-    pick[tid] = e;
-    wt[tid] = w;
+  // output projection, three back: both have completed (the kernel in between waited for its
+  // predecessor before letting this one start), so they are read before the wait (L2 loads).
+  int e;
+  if (j < a.k) {
+    e = __ldcg(a.inds + j);
+    if (e < 0 || e >= a.E) e = -1;
+  } else {
+    e = a.I_sh > 0 ? -2 : -1;  // -2: the shared expert; -1: no expert
   }
   float resv = 0.f;
   if (a.res && tid < rows) resv = bf2f(__ldcg(a.res + m0 + tid));
-  __syncthreads();
+  const int Kj = e == -2 ? a.I_sh : a.I, gpr = Kj / 64;
+  const __nv_bfloat16* sg = e == -2 ? a.sd_s : a.d_s + (size_t)(e < 0 ? 0 : e) * H * (a.I / 64);
+  const __nv_bfloat16* bg = e == -2 ? a.sd_b : a.d_b + (size_t)(e < 0 ? 0 : e) * H * (a.I / 64);
   const uint64_t pol = l2_evict_first_policy();
   const uint32_t slim = dyn_smem_bytes();
-  for (int j = 0; j < G; ++j) {
-    const int e = pick[j];
-    if (e == -1) continue;
-    if (e == -2)
-      tile_load(ring + (size_t)j * L.tb, a.sd_q, a.sd_s, a.sd_b, m0, rows, a.I_sh, pol, smem,
-                slim);
-    else
-      tile_load(ring + (size_t)j * L.tb, a.d_q + (size_t)e * H * (a.I / 8),
-                a.d_s + (size_t)e * H * (a.I / 64), a.d_b + (size_t)e * H * (a.I / 64), m0, rows,
-                a.I, pol, smem, slim);
+  if (e != -1) {
+    const uint32_t* dq = e == -2 ? a.sd_q : a.d_q + (size_t)e * H * (a.I / 8);
+    tile_load(tile, dq, sg, bg, m0, rows, Kj, pol, smem, slim);
   }
   cp_async_commit();
   pdl_wait();
   pdl_trigger();
-  // the SwiGLU outputs of every group (the previous kernel's output), one batch of copies (every
-  // CTA reads them: keep them in L2)
-  const uint64_t pol_keep = l2_evict_normal_policy();
-  for (int q = tid; q < G * (Imax / 8); q += NT) {
-    const int j = q / (Imax / 8), i = q - j * (Imax / 8);
-    const int e = pick[j];
-    const int Kj = e == -2 ? a.I_sh : a.I;
-    if (e != -1 && i < Kj / 8)
-      cp_async16(hs + q, a.hbuf + (size_t)j * Imax + i * 8, pol_keep, smem, slim);
-  }
-  cp_async_commit();
-  cp_async_wait(0);
-  __syncthreads();
-  // per-64-group sums of every group's activations: 4 lanes per (group, 64-group)
-  const int gpr_max = Imax / 64;
-  for (int base = 0; base < G * gpr_max; base += NT / 4) {
-    const int q = base + tid / 4;
-    const int j = q / gpr_max, g = q - j * gpr_max;
-    float v = 0.f;
-    const bool ok = q < G * gpr_max && pick[min(j, G - 1)] != -1 &&
-                    g < (pick[min(j, G - 1)] == -2 ? a.I_sh : a.I) / 64;
-    if (ok) v = xsum16(hs[(size_t)j * (Imax / 8) + g * 8 + 2 * c4],
-                       hs[(size_t)j * (Imax / 8) + g * 8 + 2 * c4 + 1]);
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    if (ok && c4 == 0) gsum[j * gpr_max + g] = v;
-  }
-  __syncthreads();
-  for (int j = 0; j < G; ++j) {
-    const int e = pick[j];
-    if (e == -1) continue;
-    const int Kj = e == -2 ? a.I_sh : a.I, gpr = Kj / 64;
+  float y[2] = {0.f, 0.f};
+  if (e != -1) {
+    // this group's SwiGLU outputs (the previous kernel's output; every slice reads them)
+    const uint64_t pol_keep = l2_evict_normal_policy();
+    const uint8_t* hsrc = reinterpret_cast<const uint8_t*>(a.hbuf + (size_t)j * Imax);
+    for (int c = tid; c < Kj / 8; c += NT)
+      cp_async16(reinterpret_cast<uint8_t*>(hs) + c * 16, hsrc + (size_t)c * 16, pol_keep, smem,
+                 slim);
+    cp_async_commit();
+    cp_async_wait(0);
+    __syncthreads();
+    group_sums(hs, gpr, gsum);
+    __syncthreads();
     const int gpw = (gpr + NW - 1) / NW;
     const int gw0 = warp * gpw, gwn = max(0, min(gpr, gw0 + gpw) - gw0);
-    const uint8_t* tile = ring + (size_t)j * L.tb;
-    const __nv_bfloat16* sg = e == -2 ? a.sd_s : a.d_s + (size_t)e * H * (a.I / 64);
-    const __nv_bfloat16* bg = e == -2 ? a.sd_b : a.d_b + (size_t)e * H * (a.I / 64);
     const SbRows sr = sb_rows(tile, Kj, rows, m0, H, sg, bg, r);
     float y0 = 0.f, y8 = 0.f;
-    warp_tile_dot<V>(y0, y8, tile, tile_pitch(Kj), sr.s0, sr.s8, sr.b0, sr.b8, gw0, gwn,
-                     hs + (size_t)j * (Imax / 8), gsum + j * gpr_max, r, c4);
+    warp_tile_dot<V>(y0, y8, tile, tile_pitch(Kj), sr.s0, sr.s8, sr.b0, sr.b8, gw0, gwn, hs,
+                     gsum, r, c4);
     if (c4 == 0) {
-      red[(j * NW + warp) * 16 + r] = y0;
-      red[(j * NW + warp) * 16 + r + 8] = y8;
+      red[warp * 16 + r] = y0;
+      red[warp * 16 + r + 8] = y8;
+    }
+    __syncthreads();
+    if (tid < 16) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) v += red[w * 16 + tid];
+      y[0] = round_bf16(v);  // gather_qmm / quantized_matmul output
     }
   }
+  if (tid < 16) a.ypart[((size_t)mt * G + j) * 16 + tid] = y[0];
+  __threadfence();
   __syncthreads();
-  if (tid < G * 16) {  // (group, row): the group's product, rounded to bf16
-    const int j = tid >> 4, rr = tid & 15;
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) v += red[(j * NW + w) * 16 + rr];
-    red2[tid] = round_bf16(v);  // gather_qmm / quantized_matmul output
+  if (tid == 0) *flag = atomicAdd(a.counters + mt, 1u) == (unsigned)(G - 1);
+  __syncthreads();
+  if (!*flag) return;
+  // the last group of this slice: combine every group in order
+  __threadfence();
+  if (tid < G) {
+    int ej;
+    float wj = 1.0f;
+    if (tid < a.k) {
+      ej = __ldcg(a.inds + tid);
+      if (ej < 0 || ej >= a.E) ej = -1;
+      wj = bf2f(__ldcg(a.w + tid)) * a.routed_scale;
+    } else {
+      ej = a.I_sh > 0 ? -2 : -1;
+    }
+    ce[tid] = ej;
+    cw[tid] = wj;
   }
   __syncthreads();
   if (tid < rows) {
     float acc = 0.f;
-    for (int j = 0; j < G; ++j)
-      if (pick[j] != -1) acc = __fadd_rn(acc, __fmul_rn(wt[j], red2[j * 16 + tid]));
+    for (int g = 0; g < G; ++g)
+      if (ce[g] != -1)
+        acc = __fadd_rn(acc, __fmul_rn(cw[g], __ldcg(a.ypart + ((size_t)mt * G + g) * 16 + tid)));
     float o = round_bf16(acc);
     if (a.res) o = __fadd_rn(o, resv);
     a.out[m0 + tid] = __float2bfloat16_rn(o);
   }
+  if (tid == 0) a.counters[mt] = 0u;  // ready for the next call
+}
+
+__host__ __device__ __forceinline__ uint32_t md_down_smem(int Imax) {
+  return ((1024 + 2 * Imax + 4 * (Imax / 64) + 127) & ~127) + tile_bytes(Imax);
 }
 
 // ---- host side -------------------------------------------------------------------------------
@@ -766,9 +765,9 @@ extern "C" int lg_router_decode(const void* h, const void* norm_w, float eps, in
   return LG_OK;
 }
 
-extern "C" size_t lg_moe_decode_workspace_bytes(int I, int I_shared, int k) {
+extern "C" size_t lg_moe_decode_workspace_bytes(int H, int I, int I_shared, int k) {
   const int Imax = I > I_shared ? I : I_shared;
-  return align_up((size_t)(k + 1) * Imax * 2, 256);
+  return md_ws(H > 0 ? H : 0, Imax, k > 0 ? k : 0).total;
 }
 
 extern "C" int lg_moe_decode_supported(int H, int I, int I_shared, int k) {
@@ -776,7 +775,7 @@ extern "C" int lg_moe_decode_supported(int H, int I, int I_shared, int k) {
       k < 1 || k > 32)
     return 0;
   const int Imax = I > I_shared ? I : I_shared;
-  return md_down_layout(k, Imax).total <= SMEM_CAP &&
+  return md_down_smem(Imax) <= SMEM_CAP &&
          dg_ring_off(H, GU_WARPS) + 2 * (size_t)tile_bytes(H) <= SMEM_CAP;
 }
 
@@ -824,14 +823,15 @@ extern "C" int lg_moe_decode(const void* xn, const int32_t* inds, const void* we
        (rc = check_tile_mat(su_q, su_s, su_b, "moe_decode shared up")) ||
        (rc = check_tile_mat(sd_q, sd_s, sd_b, "moe_decode shared down"))))
     return rc;
-  const size_t need = lg_moe_decode_workspace_bytes(I, I_shared, k);
+  const size_t need = lg_moe_decode_workspace_bytes(H, I, I_shared, k);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
-    return fail(LG_ERR_WORKSPACE, "moe_decode: workspace needs %zu bytes (256-aligned)", need);
+    return fail(LG_ERR_WORKSPACE, "moe_decode: workspace needs %zu bytes (256-aligned, the "
+                "first %zu zero)", need, MD_CTRL_BYTES);
   if (!lg_moe_decode_supported(H, I, I_shared, k))
     return fail(LG_ERR_UNSUPPORTED, "moe_decode: k=%d I=%d/%d H=%d exceed the shared memory", k,
                 I, I_shared, H);
   const int Imax = I > I_shared ? I : I_shared;
-  const MdDownLayout L = md_down_layout(k, Imax);
+  const MdWs W = md_ws(H, Imax, k);
   MdArgs a;
   a.xn = static_cast<const __nv_bfloat16*>(xn);
   a.inds = inds;
@@ -857,7 +857,10 @@ extern "C" int lg_moe_decode(const void* xn, const int32_t* inds, const void* we
   a.su_b = static_cast<const __nv_bfloat16*>(su_b);
   a.sd_s = static_cast<const __nv_bfloat16*>(sd_s);
   a.sd_b = static_cast<const __nv_bfloat16*>(sd_b);
-  a.hbuf = static_cast<__nv_bfloat16*>(workspace);
+  char* wsb = static_cast<char*>(workspace);
+  a.counters = reinterpret_cast<unsigned int*>(wsb + W.counters);
+  a.ypart = reinterpret_cast<float*>(wsb + W.ypart);
+  a.hbuf = reinterpret_cast<__nv_bfloat16*>(wsb + W.hbuf);
   a.res = static_cast<const __nv_bfloat16*>(residual);
   a.out = static_cast<__nv_bfloat16*>(out);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -865,17 +868,18 @@ extern "C" int lg_moe_decode(const void* xn, const int32_t* inds, const void* we
   const int Vg = vec_width(H / 64, GU_WARPS);
   const int vi = vec_width(I / 64, DN_WARPS), vs = I_shared ? vec_width(I_shared / 64, DN_WARPS) : vi;
   const int Vd = vi < vs ? vi : vs;
-  dim3 g1((Imax + 15) / 16, k + 1), g2((H + 15) / 16);
+  dim3 g1((Imax + 15) / 16, k + 1), g2((H + 15) / 16, k + 1);
+  const size_t smem_dn = md_down_smem(Imax);
   prof_begin("moe_decode", st);
   LG_CUDA_TRY(Vg == 8   ? launch_moe_gateup<8>(a, g1, smem_gu, st)
               : Vg == 4 ? launch_moe_gateup<4>(a, g1, smem_gu, st)
               : Vg == 2 ? launch_moe_gateup<2>(a, g1, smem_gu, st)
                         : launch_moe_gateup<1>(a, g1, smem_gu, st));
   LG_LAUNCH_CHECK("moe_dec_gateup");
-  LG_CUDA_TRY(Vd == 8   ? launch_moe_down<8>(a, g2, L.total, st)
-              : Vd == 4 ? launch_moe_down<4>(a, g2, L.total, st)
-              : Vd == 2 ? launch_moe_down<2>(a, g2, L.total, st)
-                        : launch_moe_down<1>(a, g2, L.total, st));
+  LG_CUDA_TRY(Vd == 8   ? launch_moe_down<8>(a, g2, smem_dn, st)
+              : Vd == 4 ? launch_moe_down<4>(a, g2, smem_dn, st)
+              : Vd == 2 ? launch_moe_down<2>(a, g2, smem_dn, st)
+                        : launch_moe_down<1>(a, g2, smem_dn, st));
   prof_end("moe_decode", st);
   LG_LAUNCH_CHECK("moe_dec_down");
   return LG_OK;

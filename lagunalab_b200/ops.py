@@ -395,8 +395,8 @@ def moe_decode(xn, inds, w, routed_scaling_factor, experts, shared=None, residua
     res = None if residual is None else _c(residual, torch.bfloat16)
     if out is None:
         out = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
-    nb = _lib.lib().lg_moe_decode_workspace_bytes(I, Ish, k)
-    ws = workspace(dev, "moe_decode", nb)
+    nb = _lib.lib().lg_moe_decode_workspace_bytes(H, I, Ish, k)
+    ws = workspace(dev, "moe_decode", nb, zero=True)
     _lib.call("lg_moe_decode", _p(xn), _p(inds), _p(w), H, I, E, k,
               float(routed_scaling_factor), *map(_p, g), *map(_p, u), *map(_p, d), Ish,
               *map(_p, sg), *map(_p, su), *map(_p, sd), _p(res), _p(out), _p(ws), ws.numel(),

@@ -182,3 +182,22 @@ def test_routing_hooks_still_see_decode_steps():
         laguna.generate(model, prompt, 3)
     for c in rec.counts.values():
         assert c.sum() == (5 + 3) * 2  # prefill tokens + three one-token steps, k = 2
+
+
+def test_moe_decode_workspace_shared_by_growing_sizes():
+    """Calls of growing hidden size share one workspace: each finds its completion counters
+    zeroed (a small call's outputs never land where a larger call keeps counters)."""
+    from lagunalab_b200 import ops
+    outs = []
+    for H in (256, 512, 2048):
+        gc = torch.Generator(device="cuda")
+        gc.manual_seed(H)
+        experts = tuple(_gpu_mats(gc, 8, *shp) for shp in ((128, H), (128, H), (H, 128)))
+        xn = torch.randn(1, H, generator=gen(H)).to(torch.bfloat16).cuda()
+        inds = torch.tensor([[1, 6]], dtype=torch.int32).cuda()
+        w = torch.tensor([[0.7, 0.3]]).to(torch.bfloat16).cuda()
+        got = ops.moe_decode(xn, inds, w, 1.0, experts)
+        y = moe_ref.switch_glu(xn.cpu(), torch.arange(2).view(1, 2),
+                               *[tuple(t[inds[0].long()].cpu() for t in m) for m in experts])
+        want = moe_ref.combine(y, w.cpu(), 1.0, torch.zeros(1, H))
+        assert rel_err(got, want) <= REL_TOL and cos(got, want) >= COS_TOL, H
