@@ -413,9 +413,12 @@ def run_decode(args, wl, ws, rank):
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.3)
     clocks.mark(True)
+    barrier(ws)
+    torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("decode_step")
     ms, _ = timed_graph(dg.graph, args.steps, stream)
     torch.cuda.nvtx.range_pop()
+    barrier(ws)
     dg.steps += args.steps
     ctx1 = dg.position()
     # end to end: every step uploads the input token from pinned host memory, runs the step
@@ -436,6 +439,7 @@ def run_decode(args, wl, ws, rank):
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
+    barrier(ws)
     t0 = time.perf_counter()
     s0 = torch.cuda.Event(enable_timing=True)
     s1 = torch.cuda.Event(enable_timing=True)
@@ -470,6 +474,8 @@ def run_decode(args, wl, ws, rank):
         kt.append(_lib.event_elapsed_ms(ev[0], ev[1]))
     kernel_ms = statistics.median(kt[2:])
     ctx_k = dg.position()
+    # N GPUs run N independent replicas of the bs1 decode: the slowest rank sets the time
+    ms, e2e_ms, kernel_ms = (max_over_ranks(v, ws) for v in (ms, e2e_ms, kernel_ms))
     ctx = (ctx0 + ctx1) / 2
     del ge, gk
     a_ = model.args
@@ -701,8 +707,8 @@ def main():
     pk, pk_kind = peaks()
     if args.workload in DECODE_WORKLOADS:
         r = run_decode(args, wl, ws, rank)
-        value = 1000.0 / r["ms"]
-        e2e = 1000.0 / r["e2e_ms"]
+        value = ws * 1000.0 / r["ms"]  # every replica decodes one token per step
+        e2e = ws * 1000.0 / r["e2e_ms"]
         step_gbs = r["bytes"] / (r["ms"] * 1e-3) / 1e9
         achieved = r["kernel_bytes"] / (r["kernel_ms"] * 1e-3) / 1e9
         if r["kernel"] == "q8_decode":
@@ -768,7 +774,7 @@ def main():
         "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": r["h2d"],
                 "d2h_bytes_per_step": r["d2h"], "ms_per_step": r["e2e_ms"]},
         "roofline": roof,
-        "gpu_launches": r["launches"],
+        "gpu_launches": r["launches"] * (ws if args.workload in DECODE_WORKLOADS else 1),
         "clocks": r["clocks"].result(),
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
