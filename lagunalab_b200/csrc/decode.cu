@@ -387,7 +387,7 @@ constexpr int DN_WARPS = 4;
 // grid (Imax/16, k + 1): group j < k is pick j, group k the shared expert. Shared memory as
 // dgemv_kernel's with a two-tile (gate, up) stage.
 template <int V>
-__global__ void __launch_bounds__(GU_WARPS * 32) moe_dec_gateup_kernel(MdArgs a) {
+__global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs a) {
   constexpr int NW = GU_WARPS;
   extern __shared__ __align__(128) uint8_t smem[];
   const int H = a.H, gpr = H / 64;

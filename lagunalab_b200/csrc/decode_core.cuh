@@ -154,6 +154,7 @@ __device__ __forceinline__ void topk_rank(const float* keys, int E, int k, int* 
     const float ke = keys[e];
     if (ke != ke) continue;  // NaN keys are never picked
     int rank = 0;
+#pragma unroll 8
     for (int f = 0; f < E; ++f) rank += topk_better(keys[f], f, ke, e) ? 1 : 0;
     if (rank < k) slot[rank] = e;
   }
