@@ -67,12 +67,14 @@ constexpr int QA_OFF_MBAR = QA_OFF_HEAD + 2 * 16 * 4;                     // mer
 constexpr int QA_OFF_FLAG = QA_OFF_MBAR + 8;                              // err, last
 constexpr int QA_SMEM = QA_OFF_FLAG + 16 + 1024;                          // + alignment slack
 // after the key loop the ring is reused: per-warp outputs, then the split merge tables
-constexpr int QA_OFF_SLAB = 0;                                    // [warp][16][128] fp32
+constexpr int QA_OFF_SLAB = 0;                                    // [warp][16][QA_SLAB] fp32
+constexpr int QA_SLAB = QA_D + 1;  // padded row: the fragment stores of a warp spread over banks
 // final merge: split partials [split][G][D] fp32, then (max, sum) [split][G], weights
 // [split][G]; copied in whole when split x G <= QA_MERGE_SMEM, else read in batches
 constexpr int QA_MERGE_SMEM = 368;
 static_assert(QA_MERGE_SMEM * (QA_D * 4 + 8 + 4) + 32 <= QA_OFF_SC, "merge copy exceeds the ring");
 static_assert(QA_MAX_SPLITS * 16 * (8 + 4) + 32 <= QA_OFF_SC, "merge tables exceed the ring");
+static_assert(QA_WARPS * 16 * QA_SLAB * 4 <= QA_OFF_SC, "warp outputs exceed the ring");
 
 // float2 (max, sum) entries per (batch, kv head), padded to 16 bytes for the bulk copy
 __host__ __device__ constexpr int q8_ml_stride(int ns, int G) { return (ns * G + 1) & ~1; }
@@ -539,7 +541,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             const int d = 64 * g + 8 * r + 2 * (mt & 3) + h2;
-            slab[(warp * 16 + head) * QA_D + d] = acc[nt][mt][2 * h2 + hh] * (1.f / QA_PSCALE) + base;
+            slab[(warp * 16 + head) * QA_SLAB + d] = acc[nt][mt][2 * h2 + hh] * (1.f / QA_PSCALE) + base;
           }
         }
         if (r == 0) {
@@ -572,8 +574,8 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
       float v0 = 0.f, v1 = 0.f;
 #pragma unroll
       for (int w = 0; w < QA_WARPS; ++w) {
-        v0 += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_D + d];
-        v1 += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_D + d + 1];
+        v0 += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_SLAB + d];
+        v1 += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_SLAB + d + 1];
       }
       const float inv = 1.f / s_L[h];
       if (bad) v0 = v1 = __int_as_float(0x7fc00000);
@@ -590,7 +592,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
     const int h = i / QA_D, d = i % QA_D;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < QA_WARPS; ++w) v += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_D + d];
+    for (int w = 0; w < QA_WARPS; ++w) v += s_wt[w * 16 + h] * slab[(w * 16 + h) * QA_SLAB + d];
     a.part_acc[(pbase + h) * QA_D + d] = v;
   }
   if (threadIdx.x < G)
