@@ -252,13 +252,18 @@ struct RdArgs {
 };
 
 // shared memory: red8 [8] | keys [256] | vals [256] | slot [32] | flag | xs [H] bf16 |
-// codes [RD_WARPS][H] | scales, biases [RD_WARPS][H/64]
+// codes [RD_WARPS][H] | scales, biases [RD_WARPS][H/64] | norm weight [H] | bias [256]
 __host__ __device__ __forceinline__ uint32_t rd_xs_off() { return 32u + 2u * 1024u + 128u + 16u; }
 __host__ __device__ __forceinline__ uint32_t rd_w_off(int H) {
   return (rd_xs_off() + 2u * H + 127u) & ~127u;
 }
+// then the norm weight [H] bf16 and the selection bias [256] fp32 (both static: staged before
+// the wait)
+__host__ __device__ __forceinline__ uint32_t rd_nw_off(int H) {
+  return rd_w_off(H) + (uint32_t)RD_WARPS * H + 2u * RD_WARPS * (H / 64) * 2u;
+}
 __host__ __device__ __forceinline__ size_t rd_smem(int H) {
-  return rd_w_off(H) + (size_t)RD_WARPS * H + 2 * (size_t)RD_WARPS * (H / 64) * 2;
+  return rd_nw_off(H) + 2u * (size_t)H + 4u * 256u;
 }
 
 // grid ceil(E / RD_WARPS): each CTA streams its experts' router rows into shared memory
@@ -292,13 +297,20 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_decode_kernel(RdArgs a) 
       cp_async16((c < sb ? reinterpret_cast<uint8_t*>(ws) : reinterpret_cast<uint8_t*>(wb) -
                                                                 sb * 16) + c * 16,
                  (c < sb ? ss : sbp - sb * 16) + c * 16, pol, smem, slim);
+    const uint8_t* nsrc = reinterpret_cast<const uint8_t*>(a.norm_w);
+    for (int c = tid; c < H / 8; c += NT)
+      cp_async16(smem + rd_nw_off(H) + c * 16, nsrc + (size_t)c * 16, pol, smem, slim);
     cp_async_commit();
   }
+  float* ebs = reinterpret_cast<float*>(smem + rd_nw_off(H) + 2 * H);  // [E] selection bias
+  for (int e = tid; e < E; e += NT) ebs[e] = a.ebias ? a.ebias[e] : 0.f;
   pdl_wait();
   pdl_trigger();
   const uint4* hg = reinterpret_cast<const uint4*>(a.h);
   const float rs = block_rms_scale(hg, H, a.eps, red8);
-  const uint4* nw = reinterpret_cast<const uint4*>(a.norm_w);
+  const uint4* nw = reinterpret_cast<const uint4*>(smem + rd_nw_off(H));
+  cp_async_wait(0);
+  __syncthreads();
   for (int i = tid; i < H / 8; i += NT) {
     const uint4 v = rms_apply8(hg[i], nw[i], rs);
     xs[i] = v;
@@ -325,7 +337,7 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_decode_kernel(RdArgs a) 
   // last CTA: every CTA's logits are visible
   __threadfence();
   if (tid < 32) slot[tid] = -1;
-  if (warp == 0) topk_scores_warp([&](int e) { return __ldcg(a.lg_ws + e); }, E, a.ebias,
+  if (warp == 0) topk_scores_warp([&](int e) { return __ldcg(a.lg_ws + e); }, E, ebs,
                                   a.score_fn, keys, vals);
   __syncthreads();
   topk_rank(keys, E, a.k, slot, tid, NT);
