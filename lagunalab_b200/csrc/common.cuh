@@ -128,8 +128,15 @@ __device__ __forceinline__ uint32_t quant_code(float v, float s, float bv, float
 // kernel starts, every kernel before its immediate predecessor has completed: before its wait
 // it may read static data (weights) and data from earlier kernels, never its predecessor's
 // output. Without the launch attribute both instructions return at once.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Both are issued by a converged warp: code before them often branches on the lane (a thread
+// that zeroes a flag, the first threads reading a few words), and inline asm gives the compiler
+// no reason to rejoin the warp first.
+__device__ __forceinline__ void pdl_wait() {
+  __syncwarp();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 __device__ __forceinline__ void pdl_trigger() {
+  __syncwarp();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 

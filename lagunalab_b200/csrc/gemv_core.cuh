@@ -47,6 +47,9 @@ __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 
 //  xa: the thread's 16 activation values of token lane/4 (K 16*c4 .. 16*c4+15 of the group).
 __device__ __forceinline__ void group_mma(float (&acc)[4], uint2 wr0, uint2 wr8, uint4 xa0,
                                           uint4 xa1) {
+  // mma.sync.aligned needs the whole warp converged; the callers' lane-dependent loads just
+  // before may leave it split, and inline asm gives the compiler no reason to rejoin it
+  __syncwarp();
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint32_t w0 = i ? wr0.y : wr0.x;

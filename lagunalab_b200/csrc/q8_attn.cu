@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
         issue(j + QA_STAGES, s, static_cast<int>(gate) * a.zero);
       }
     }
+    __syncwarp();  // rejoin the warp (lane 0's refill, the per-lane stage wait) before the MMAs
 
     // ---- S^T = K Q^T per half (two accumulators: head-dim groups 0 and 1) ----
     float sa[2][NT][2][4];

@@ -108,6 +108,7 @@ __device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  __syncwarp();  // mma.sync.aligned needs the whole warp converged
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
