@@ -413,28 +413,23 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
   const bool sh = (j == a.k);
   const int Ig = sh ? a.I_sh : a.I;
   const int m0 = blockIdx.x * 16;
-  const int rows = min(16, Ig - m0);  // 16 or none (the intermediate sizes are multiples of 64)
+  const int rows = min(16, Ig - m0);
   const uint64_t pol = l2_evict_first_policy();
   const uint32_t slim = dyn_smem_bytes();
-  // this warp's groups of the tile pair: it stages and reduces only those, so it starts as
-  // soon as its own copies land; the warps meet only for the final sum over warps
-  const int gpw = (gpr + NW - 1) / NW;
-  const int gw0 = warp * gpw, gwn = max(0, min(gpr, gw0 + gpw) - gw0);
   const uint32_t *gq = a.sg_q, *uq = a.su_q;
   const __nv_bfloat16 *gs = a.sg_s, *gb = a.sg_b, *us = a.su_s, *ub = a.su_b;
-  if (sh && rows == 16) {  // the shared expert is static: stream it before the wait
-    tile_load_groups(ring, gq, gs, gb, m0, H, gw0, gwn, pol, smem, slim);
-    tile_load_groups(ring + tb, uq, us, ub, m0, H, gw0, gwn, pol, smem, slim);
+  if (sh && rows > 0) {  // the shared expert is static: stream it before the wait
+    tile_load(ring, gq, gs, gb, m0, rows, H, pol, smem, slim);
+    tile_load(ring + tb, uq, us, ub, m0, rows, H, pol, smem, slim);
     cp_async_commit();
   }
   pdl_wait();
   pdl_trigger();
-  if (rows != 16) return;  // no copy was issued
-  // the normalised token (the router's output), this warp's groups: it overlaps the pick read
+  if (rows <= 0) return;
+  // the normalised token (the router's output): its copy overlaps the read of the pick
   const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(a.xn);
-  for (int c = lane; c < gwn * 8; c += 32)
-    cp_async16(reinterpret_cast<uint8_t*>(xs) + (gw0 * 8 + c) * 16,
-               xsrc + (size_t)(gw0 * 8 + c) * 16, pol, smem, slim);
+  for (int c = tid; c < H / 8; c += NW * 32)
+    cp_async16(reinterpret_cast<uint8_t*>(xs) + c * 16, xsrc + (size_t)c * 16, pol, smem, slim);
   cp_async_commit();
   if (!sh) {
     const int e = a.inds[j];
@@ -445,26 +440,21 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
     const size_t wo = (size_t)e * a.I * (H / 8), so = (size_t)e * a.I * gpr;
     gq = a.g_q + wo; gs = a.g_s + so; gb = a.g_b + so;
     uq = a.u_q + wo; us = a.u_s + so; ub = a.u_b + so;
-    tile_load_groups(ring, gq, gs, gb, m0, H, gw0, gwn, pol, smem, slim);
-    tile_load_groups(ring + tb, uq, us, ub, m0, H, gw0, gwn, pol, smem, slim);
+    tile_load(ring, gq, gs, gb, m0, rows, H, pol, smem, slim);
+    tile_load(ring + tb, uq, us, ub, m0, rows, H, pol, smem, slim);
     cp_async_commit();
   }
+  cp_async_wait(sh ? 0 : 1);  // the activations (for a shared-expert CTA: everything)
+  __syncthreads();
+  group_sums(xs, gpr, gsum);
+  const int gpw = (gpr + NW - 1) / NW;
+  const int gw0 = warp * gpw, gwn = max(0, min(gpr, gw0 + gpw) - gw0);
   cp_async_wait(0);
-  __syncwarp();
-  // this warp's group sums (the group_sums order)
-  for (int g0 = 0; g0 < gwn; g0 += 8) {
-    const int gl = g0 + (lane >> 2), g = gw0 + gl;
-    float v = 0.f;
-    if (gl < gwn) v = xsum16(xs[g * 8 + 2 * c4], xs[g * 8 + 2 * c4 + 1]);
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    if (gl < gwn && c4 == 0) gsum[g] = v;
-  }
-  __syncwarp();
+  __syncthreads();
 #pragma unroll
   for (int m = 0; m < 2; ++m) {
     const uint8_t* tile = ring + m * tb;
-    const SbRows sr = sb_rows(tile, H, 16, m0, Ig, m ? us : gs, m ? ub : gb, r);
+    const SbRows sr = sb_rows(tile, H, rows, m0, Ig, m ? us : gs, m ? ub : gb, r);
     float y0 = 0.f, y8 = 0.f;
     warp_tile_dot<V>(y0, y8, tile, pitch, sr.s0, sr.s8, sr.b0, sr.b8, gw0, gwn, xs, gsum, r, c4);
     if (c4 == 0) {
@@ -482,7 +472,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
     red2[tid] = v;
   }
   __syncthreads();
-  if (tid < 16) a.hbuf[(size_t)j * a.Imax + m0 + tid] = swiglu_mlx(red2[tid], red2[16 + tid]);
+  if (tid < rows) a.hbuf[(size_t)j * a.Imax + m0 + tid] = swiglu_mlx(red2[tid], red2[16 + tid]);
 }
 
 // grid (ceil(H/16), k + 1): one 16-row slice of the hidden dimension for one group (pick j < k,

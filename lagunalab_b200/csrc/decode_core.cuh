@@ -317,31 +317,6 @@ __device__ __forceinline__ void tile_load(uint8_t* dst, const uint32_t* q, const
   }
 }
 
-// One warp's share of a full 16-row tile (rows [row0, row0 + 16) of a [*, K] matrix): the codes
-// of groups [g0, g0 + gn) with 16-byte cp.async copies (not committed), and their scales and
-// biases with plain loads stored into the tile's scale block (the warp's lanes take them in
-// turn; they are in shared memory when the warp's own loads return). The rest of the tile is
-// not touched.
-__device__ __forceinline__ void tile_load_groups(uint8_t* dst, const uint32_t* q,
-                                                 const __nv_bfloat16* s, const __nv_bfloat16* b,
-                                                 int row0, int K, int g0, int gn, uint64_t pol,
-                                                 const void* sbase, uint32_t slimit) {
-  const int lane = threadIdx.x & 31, gpr = K / 64, cpr = 2 * gn;  // 16-byte chunks per row
-  const uint32_t pitch = tile_pitch(K);
-  const uint8_t* qb = reinterpret_cast<const uint8_t*>(q + (size_t)row0 * (K / 8)) + g0 * 32;
-  for (int c = lane; c < 16 * cpr; c += 32) {
-    const int rr = c / cpr, cc = c - rr * cpr;
-    cp_async16(dst + rr * pitch + g0 * 32 + cc * 16, qb + (size_t)rr * (K / 2) + cc * 16, pol,
-               sbase, slimit);
-  }
-  __nv_bfloat16* sd = reinterpret_cast<__nv_bfloat16*>(dst + tile_sc_off(K));
-  for (int c = lane; c < 2 * 16 * gn; c += 32) {
-    const int sb = c / (16 * gn), rem = c - sb * 16 * gn, rr = rem / gn, gg = g0 + rem - rr * gn;
-    const __nv_bfloat16* src = (sb ? b : s) + (size_t)(row0 + rr) * gpr + gg;
-    sd[sb * 16 * gpr + rr * gpr + gg] = *src;
-  }
-}
-
 // One 64-group of a staged tile for a single token: the thread's A fragments (rows r, r + 8)
 // from shared memory, the token's activations xa (lanes with lane/4 == 0; zero elsewhere).
 __device__ __forceinline__ void tile_group(float (&d)[4], const uint8_t* tile, uint32_t pitch,
