@@ -418,10 +418,18 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
   const uint32_t slim = dyn_smem_bytes();
   const uint32_t *gq = a.sg_q, *uq = a.su_q;
   const __nv_bfloat16 *gs = a.sg_s, *gb = a.sg_b, *us = a.su_s, *ub = a.su_b;
-  if (sh && rows > 0) {  // the shared expert is static: stream it before the wait
-    tile_load(ring, gq, gs, gb, m0, rows, H, pol, smem, slim);
-    tile_load(ring + tb, uq, us, ub, m0, rows, H, pol, smem, slim);
-    cp_async_commit();
+  // the weight tiles come by bulk copies (issued by one thread) that complete on this barrier
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  int* berr = reinterpret_cast<int*>(smem + 8);
+  if (tid == 0) {
+    *berr = 0;
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    if (sh && rows == 16) {  // the shared expert is static: stream it before the wait
+      mbar_arrive_expect_tx(bar, 2u * tile_bulk_bytes(H));
+      tile_load_bulk(ring, gq, gs, gb, m0, H, bar);
+      tile_load_bulk(ring + tb, uq, us, ub, m0, H, bar);
+    }
   }
   pdl_wait();
   pdl_trigger();
@@ -440,16 +448,24 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
     const size_t wo = (size_t)e * a.I * (H / 8), so = (size_t)e * a.I * gpr;
     gq = a.g_q + wo; gs = a.g_s + so; gb = a.g_b + so;
     uq = a.u_q + wo; us = a.u_s + so; ub = a.u_b + so;
-    tile_load(ring, gq, gs, gb, m0, rows, H, pol, smem, slim);
-    tile_load(ring + tb, uq, us, ub, m0, rows, H, pol, smem, slim);
-    cp_async_commit();
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar, 2u * tile_bulk_bytes(H));
+      tile_load_bulk(ring, gq, gs, gb, m0, H, bar);
+      tile_load_bulk(ring + tb, uq, us, ub, m0, H, bar);
+    }
   }
-  cp_async_wait(sh ? 0 : 1);  // the activations (for a shared-expert CTA: everything)
+  cp_async_wait(0);  // the activations
   __syncthreads();
   group_sums(xs, gpr, gsum);
   const int gpw = (gpr + NW - 1) / NW;
   const int gw0 = warp * gpw, gwn = max(0, min(gpr, gw0 + gpw) - gw0);
-  cp_async_wait(0);
+  if (!mbar_wait(bar, 0, berr, 1, 400000000LL)) {
+    // the tiles never arrived: record it, let the copies drain (bounded), leave the rows unset
+    if (tid == 0 && atomicCAS(&g_stage_check[0], 0ull, 4ull) == 0ull) g_stage_check[3] = 0xB1u;
+    for (const long long t0 = clock64(); !mbar_try_wait(bar, 0) && clock64() - t0 < 400000000LL;) {
+    }
+    return;
+  }
   __syncthreads();
 #pragma unroll
   for (int m = 0; m < 2; ++m) {

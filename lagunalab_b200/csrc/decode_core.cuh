@@ -317,6 +317,23 @@ __device__ __forceinline__ void tile_load(uint8_t* dst, const uint32_t* q, const
   }
 }
 
+// One thread: a full tile (rows [row0, row0 + 16) of a [*, K] matrix) with bulk copies that
+// complete on bar: one per code row (into the padded pitch), one for the scale block and one for
+// the bias block. Not counted on bar: the caller adds tile_bulk_bytes(K) per tile to its
+// expected transaction count first.
+__host__ __device__ __forceinline__ uint32_t tile_bulk_bytes(int K) {
+  return 16u * (K / 2) + 2u * 16u * (K / 64) * 2u;
+}
+__device__ __forceinline__ void tile_load_bulk(uint8_t* dst, const uint32_t* q,
+                                               const __nv_bfloat16* s, const __nv_bfloat16* b,
+                                               int row0, int K, uint64_t* bar) {
+  const uint32_t pitch = tile_pitch(K), rb = K / 2, sbb = 16u * (K / 64) * 2u;
+  const uint8_t* qb = reinterpret_cast<const uint8_t*>(q + (size_t)row0 * (K / 8));
+  for (int rr = 0; rr < 16; ++rr) bulk_g2s(dst + rr * pitch, qb + (size_t)rr * rb, rb, bar);
+  bulk_g2s(dst + tile_sc_off(K), s + (size_t)row0 * (K / 64), sbb, bar);
+  bulk_g2s(dst + tile_sc_off(K) + sbb, b + (size_t)row0 * (K / 64), sbb, bar);
+}
+
 // One 64-group of a staged tile for a single token: the thread's A fragments (rows r, r + 8)
 // from shared memory, the token's activations xa (lanes with lane/4 == 0; zero elsewhere).
 __device__ __forceinline__ void tile_group(float (&d)[4], const uint8_t* tile, uint32_t pitch,
