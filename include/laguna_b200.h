@@ -289,6 +289,31 @@ int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void*
                     void* k_b, uint32_t* v_q, void* v_s, void* v_b, int cap, void* gate_out,
                     void* stream);
 
+/*
+ * One token's q/k/v/g projection (lg_decode_gemv with the layer's input RMSNorm fused in,
+ * laguna.py:94-99) followed by its attention prologue (lg_attn_prep / lg_attn_prep_q8,
+ * laguna.py:100-106) in one launch: qkvg_out = the projection row [q | k | v | g] (bf16,
+ * N = (Hq + 2 Hkv) D + (gate_per_head ? Hq : Hq D)), q_out [Hq, 1, D], gate_out [1, Hq or
+ * Hq D], and the new k/v rows written into row pos of the cache: the bf16 cache (k_cache,
+ * v_cache [Hkv, cap, D]) or the 8-bit cache (k_q, k_s, k_b, v_q, v_s, v_b as in
+ * lg_attn_prep_q8; the other pointers NULL). The same bits as lg_decode_gemv followed by the
+ * prologue: every 16-row tile of the projection is one CTA; gate rows are finished by their
+ * own CTA and the last CTA of each head to finish runs that head's prologue. The workspace
+ * (lg_decode_qkv_prep_workspace_bytes) holds one counter per head; it must start zeroed and
+ * completed calls leave it so. D % 64 == 0, D <= 256; LG_ERR_UNSUPPORTED when the projection's
+ * tiles do not all fit on the GPU at once.
+ */
+int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, const void* w_s,
+                       const void* w_b, const void* norm_w, float eps, int Hq, int Hkv, int D,
+                       const void* qn_w, const void* kn_w, float qk_eps, float rope_theta,
+                       const int32_t* pos_dev, int pos_host, int gate_per_head, void* qkvg_out,
+                       void* q_out, void* gate_out, void* k_cache, void* v_cache, uint32_t* k_q,
+                       void* k_s, void* k_b, uint32_t* v_q, void* v_s, void* v_b, int cap,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes of lg_decode_qkv_prep (one counter per head slot). */
+size_t lg_decode_qkv_prep_workspace_bytes(int Hq, int Hkv);
+
 /* Workspace bytes for lg_bf16_decode_attention planned for n_plan keys. */
 size_t lg_bf16_decode_workspace_bytes(int B, int Hq, int Hkv, int n_plan);
 

@@ -53,6 +53,9 @@ SIGNATURES = {
                                          c_size_t, P]),
     "lg_argmax": (c_int, [P, I, I, P, P, I, P]),
     "lg_decode_gemv": (c_int, [P, I, I, P, P, P, P, P, P, P, c_float, P, P, P]),
+    "lg_decode_qkv_prep": (c_int, [P, I, P, P, P, P, c_float, I, I, I, P, P, c_float, c_float, P,
+                                   I, I, P, P, P, P, P, P, P, P, P, P, P, I, P, c_size_t, P]),
+    "lg_decode_qkv_prep_workspace_bytes": (c_size_t, [I, I]),
     "lg_router_decode": (c_int, [P, P, c_float, I, P, P, P, P, I, I, I, I, P, P, P, P, P,
                                  c_size_t, P]),
     "lg_router_decode_workspace_bytes": (c_size_t, [I]),

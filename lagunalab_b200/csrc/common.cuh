@@ -88,6 +88,28 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// The warp-wide minimum and maximum, in place.
+__device__ __forceinline__ void warp_minmax(float& lo, float& hi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+}
+
+// Atomic add with acquire-release semantics at GPU scope, returning the old value: the
+// last-arriver pattern without full fences. Stores that the calling thread's CTA (or warp)
+// ordered before it with a barrier are released with it; the thread that sees the final count
+// acquires every earlier arriver's, and passes them on to its CTA (or warp) through a barrier.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // Read-only 128-bit global load that bypasses L1 allocation (weights are streamed once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 r;

@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "decode_core.cuh"
 #include "gemv_core.cuh"
+#include "prep_core.cuh"
 #include "tc_ptx.cuh"
 
 namespace lg {
@@ -135,6 +136,10 @@ struct DgArgs {
   const __nv_bfloat16* res;     // [N] or null (plain mode)
   __nv_bfloat16* out;           // [N]
   int K, N, tiles, stages;
+  // attention prologue fused behind the q/k/v/g projection (one tile per CTA, one token; its
+  // arguments travel as a second kernel parameter, so the plain variants keep a small one)
+  int prep;
+  unsigned int* head_cnt;  // [Hq + 2 Hkv] finished tiles per head (zero between calls)
 };
 
 // shared memory: red8 [8] | red [2][NM][NW][16] | xs [K] bf16 | gsum [K/64] | ring of stages
@@ -144,9 +149,11 @@ __host__ __device__ __forceinline__ uint32_t dg_ring_off(int K, int NW) {
 }
 
 // grid: CTAs take tiles blockIdx.x, blockIdx.x + gridDim.x, ...; `stages` tiles in flight.
-// NW warps split each tile's K groups.
-template <bool GLU, int NW, int V>
-__global__ void __launch_bounds__(NW * 32) dgemv_kernel(DgArgs a) {
+// NW warps split each tile's K groups. PREP: the attention prologue behind a q/k/v/g projection.
+template <bool GLU, int NW, int V, bool PREP>
+// The q/k/v/g projection keeps three 8-warp CTAs per SM (its tiles fit the GPU in one wave).
+__global__ void __launch_bounds__(NW * 32, PREP && NW == 8 ? 3 : 1)
+    dgemv_kernel(DgArgs a, PrepArgs p) {
   constexpr int NM = GLU ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, gpr = K / 64, S = a.stages;
@@ -228,6 +235,28 @@ __global__ void __launch_bounds__(NW * 32) dgemv_kernel(DgArgs a) {
     }
   }
   cp_async_wait(0);
+  if constexpr (PREP) {
+    // The projection row [q | k | v | gates] of one token, one 16-row tile per CTA, whose
+    // outputs warp 0 stored (tid < rows): gate rows become gates right here; the last CTA of a
+    // head (D / 16 tiles) to finish runs that head's prologue on the row its neighbours wrote.
+    if (warp != 0) return;
+    const int D = p.D, gate0 = (p.Hq + 2 * p.Hkv) * D;
+    const int row0 = (int)blockIdx.x * 16;
+    if (row0 >= gate0) {
+      if (lane < min(16, a.N - row0))
+        p.gate_out[row0 + lane - gate0] = prep_gate(bf2f(a.out[row0 + lane]));
+      return;
+    }
+    const int h = row0 / D;
+    __syncwarp();  // the tile's stores come before the release below
+    unsigned prev = 0;
+    if (lane == 0) prev = atom_add_acq_rel_gpu(&a.head_cnt[h], 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(D / 16 - 1)) return;
+    __syncwarp();  // ... and the other tiles' stores, acquired by lane 0, before the reads
+    if (lane == 0) a.head_cnt[h] = 0u;  // ready for the next call
+    prep_head(p, 0, h, false, reinterpret_cast<uint8_t*>(xs));
+  }
 }
 
 // ---- router ----------------------------------------------------------------------------------
@@ -635,21 +664,31 @@ static int vec_width(int gpr, int nw) {
   return gpw % 8 == 0 ? 8 : gpw % 4 == 0 ? 4 : gpw % 2 == 0 ? 2 : 1;
 }
 
-template <bool GLU, int NW, int V>
-static cudaError_t launch_dgemv_v(const DgArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-  cudaError_t e = allow_smem(dgemv_kernel<GLU, NW, V>, smem);
+template <bool GLU, int NW, int V, bool PREP>
+static cudaError_t launch_dgemv_k(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
+                                  cudaStream_t st) {
+  cudaError_t e = allow_smem(dgemv_kernel<GLU, NW, V, PREP>, smem);
   return e != cudaSuccess
              ? e
-             : launch_k(dgemv_kernel<GLU, NW, V>, grid, dim3(NW * 32), smem, st, a);
+             : launch_k(dgemv_kernel<GLU, NW, V, PREP>, grid, dim3(NW * 32), smem, st, a, p);
+}
+
+template <bool GLU, int NW, int V>
+static cudaError_t launch_dgemv_v(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
+                                  cudaStream_t st) {
+  if constexpr (!GLU)
+    if (a.prep) return launch_dgemv_k<false, NW, V, true>(a, p, grid, smem, st);
+  return launch_dgemv_k<GLU, NW, V, false>(a, p, grid, smem, st);
 }
 
 template <bool GLU, int NW>
-static cudaError_t launch_dgemv_nw(const DgArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+static cudaError_t launch_dgemv_nw(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
+                                   cudaStream_t st) {
   switch (vec_width(a.K / 64, NW)) {
-    case 8: return launch_dgemv_v<GLU, NW, 8>(a, grid, smem, st);
-    case 4: return launch_dgemv_v<GLU, NW, 4>(a, grid, smem, st);
-    case 2: return launch_dgemv_v<GLU, NW, 2>(a, grid, smem, st);
-    default: return launch_dgemv_v<GLU, NW, 1>(a, grid, smem, st);
+    case 8: return launch_dgemv_v<GLU, NW, 8>(a, p, grid, smem, st);
+    case 4: return launch_dgemv_v<GLU, NW, 4>(a, p, grid, smem, st);
+    case 2: return launch_dgemv_v<GLU, NW, 2>(a, p, grid, smem, st);
+    default: return launch_dgemv_v<GLU, NW, 1>(a, p, grid, smem, st);
   }
 }
 
@@ -657,9 +696,10 @@ static cudaError_t launch_dgemv_nw(const DgArgs& a, dim3 grid, size_t smem, cuda
 static int dg_warps(int K) { return K / 64 >= 64 ? 16 : 8; }
 
 template <bool GLU>
-static cudaError_t launch_dgemv(const DgArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-  return dg_warps(a.K) == 16 ? launch_dgemv_nw<GLU, 16>(a, grid, smem, st)
-                             : launch_dgemv_nw<GLU, 8>(a, grid, smem, st);
+static cudaError_t launch_dgemv(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
+                                cudaStream_t st) {
+  return dg_warps(a.K) == 16 ? launch_dgemv_nw<GLU, 16>(a, p, grid, smem, st)
+                             : launch_dgemv_nw<GLU, 8>(a, p, grid, smem, st);
 }
 
 static int check_tile_mat(const void* q, const void* s, const void* b, const char* what) {
@@ -672,6 +712,41 @@ static int check_tile_mat(const void* q, const void* s, const void* b, const cha
 }  // namespace lg
 
 using namespace lg;
+
+// Tile plan and launch of the dense decode GEMV. one_tile: fail unless every CTA gets exactly
+// one tile (the fused prologue needs it).
+static int dgemv_launch(DgArgs& a, const PrepArgs& p, bool glu, bool one_tile,
+                        cudaStream_t st) {
+  const int NM = glu ? 2 : 1, K = a.K;
+  a.tiles = (a.N + 15) / 16;
+  const size_t stage = (size_t)NM * tile_bytes(K), fixed = dg_ring_off(K, dg_warps(K));
+  const int sms = device_sm_count();
+  // one tile per CTA while all of them fit on the GPU at once, else a ring of tiles per CTA
+  const int per_sm = (int)((200 * 1024) / (fixed + stage));
+  int grid, stages;
+  if (per_sm >= 1 && a.tiles <= per_sm * sms) {
+    grid = a.tiles;
+    stages = 1;
+  } else {
+    if (one_tile)
+      return fail(LG_ERR_UNSUPPORTED, "decode_gemv: %d tiles do not fit one per CTA", a.tiles);
+    grid = 2 * sms;
+    const long long room = 96 * 1024 - (long long)fixed;
+    stages = room > 0 ? (int)(room / (long long)stage) : 1;
+    stages = stages < 1 ? 1 : stages > DG_MAX_STAGES ? DG_MAX_STAGES : stages;
+    const int need = (a.tiles + grid - 1) / grid;
+    if (stages > need) stages = need;
+  }
+  a.stages = stages;
+  const size_t smem = fixed + stages * stage;
+  LG_CHECK_ARG(smem <= SMEM_CAP, "decode_gemv: K=%d needs %zu bytes of shared memory", K, smem);
+  prof_begin("decode_gemv", st);
+  LG_CUDA_TRY(glu ? launch_dgemv<true>(a, p, dim3(grid), smem, st)
+                  : launch_dgemv<false>(a, p, dim3(grid), smem, st));
+  prof_end("decode_gemv", st);
+  LG_LAUNCH_CHECK("dgemv");
+  return LG_OK;
+}
 
 extern "C" int lg_decode_gemv(const void* x, int K, int N, const uint32_t* w_q, const void* w_s,
                               const void* w_b, const uint32_t* u_q, const void* u_s,
@@ -690,8 +765,7 @@ extern "C" int lg_decode_gemv(const void* x, int K, int N, const uint32_t* w_q, 
     if ((rc = check_tile_mat(u_q, u_s, u_b, "decode_gemv (up)"))) return rc;
     LG_CHECK_ARG(!residual, "decode_gemv: no residual with a gate/up pair");
   }
-  const int NM = glu ? 2 : 1;
-  DgArgs a;
+  DgArgs a = {};
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
   a.eps = eps;
@@ -705,33 +779,79 @@ extern "C" int lg_decode_gemv(const void* x, int K, int N, const uint32_t* w_q, 
   a.out = static_cast<__nv_bfloat16*>(out);
   a.K = K;
   a.N = N;
-  a.tiles = (N + 15) / 16;
-  const size_t stage = (size_t)NM * tile_bytes(K), fixed = dg_ring_off(K, dg_warps(K));
-  const int sms = device_sm_count();
-  // one tile per CTA while all of them fit on the GPU at once, else a ring of tiles per CTA
-  const int per_sm = (int)((200 * 1024) / (fixed + stage));
-  int grid, stages;
-  if (per_sm >= 1 && a.tiles <= per_sm * sms) {
-    grid = a.tiles;
-    stages = 1;
-  } else {
-    grid = 2 * sms;
-    const long long room = 96 * 1024 - (long long)fixed;
-    stages = room > 0 ? (int)(room / (long long)stage) : 1;
-    stages = stages < 1 ? 1 : stages > DG_MAX_STAGES ? DG_MAX_STAGES : stages;
-    const int need = (a.tiles + grid - 1) / grid;
-    if (stages > need) stages = need;
-  }
-  a.stages = stages;
-  const size_t smem = fixed + stages * stage;
-  LG_CHECK_ARG(smem <= SMEM_CAP, "decode_gemv: K=%d needs %zu bytes of shared memory", K, smem);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  prof_begin("decode_gemv", st);
-  LG_CUDA_TRY(glu ? launch_dgemv<true>(a, dim3(grid), smem, st)
-                  : launch_dgemv<false>(a, dim3(grid), smem, st));
-  prof_end("decode_gemv", st);
-  LG_LAUNCH_CHECK("dgemv");
-  return LG_OK;
+  a.prep = 0;
+  return dgemv_launch(a, PrepArgs{}, glu, false, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t lg_decode_qkv_prep_workspace_bytes(int Hq, int Hkv) {
+  return align_up(4 * (size_t)(Hq > 0 && Hkv > 0 ? Hq + 2 * Hkv : 0), 256);
+}
+
+extern "C" int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, const void* w_s,
+                                  const void* w_b, const void* norm_w, float eps, int Hq,
+                                  int Hkv, int D, const void* qn_w, const void* kn_w,
+                                  float qk_eps, float rope_theta, const int32_t* pos_dev,
+                                  int pos_host, int gate_per_head, void* qkvg_out, void* q_out,
+                                  void* gate_out, void* k_cache, void* v_cache, uint32_t* k_q,
+                                  void* k_s, void* k_b, uint32_t* v_q, void* v_s, void* v_b,
+                                  int cap, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  LG_CHECK_ARG(K > 0 && K % 64 == 0 && K <= 16384, "decode_qkv_prep: hidden %d", K);
+  LG_CHECK_ARG(Hq > 0 && Hkv > 0 && D % 64 == 0 && D <= 256,
+               "decode_qkv_prep: heads %d/%d, head_dim %d (a multiple of 64, <= 256)", Hq, Hkv, D);
+  LG_CHECK_ARG(x && norm_w && qn_w && kn_w && qkvg_out && q_out && gate_out,
+               "decode_qkv_prep: NULL pointer");
+  LG_CHECK_ARG(K >= 2 * D, "decode_qkv_prep: hidden %d below twice head_dim %d", K, D);
+  const bool q8 = k_q != nullptr;
+  LG_CHECK_ARG(q8 ? (k_s && k_b && v_q && v_s && v_b && !k_cache && !v_cache)
+                  : (k_cache && v_cache),
+               "decode_qkv_prep: give either the bf16 cache or the 8-bit cache");
+  LG_CHECK_ARG(aligned(x, 16) && aligned(norm_w, 16),
+               "decode_qkv_prep: x and the norm weight must be 16-byte aligned");
+  LG_CHECK_ARG(pos_dev || (pos_host >= 0 && pos_host < cap),
+               "decode_qkv_prep: position %d beyond the cache capacity %d", pos_host, cap);
+  int rc = check_tile_mat(w_q, w_s, w_b, "decode_qkv_prep");
+  if (rc) return rc;
+  const size_t need = lg_decode_qkv_prep_workspace_bytes(Hq, Hkv);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(LG_ERR_WORKSPACE, "decode_qkv_prep: workspace needs %zu zeroed bytes", need);
+  DgArgs a = {};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.eps = eps;
+  a.q[0] = w_q;
+  a.s[0] = static_cast<const __nv_bfloat16*>(w_s);
+  a.b[0] = static_cast<const __nv_bfloat16*>(w_b);
+  a.out = static_cast<__nv_bfloat16*>(qkvg_out);
+  a.K = K;
+  a.N = (Hq + 2 * Hkv) * D + (gate_per_head ? Hq : Hq * D);
+  a.prep = 1;
+  a.head_cnt = static_cast<unsigned int*>(workspace);
+  PrepArgs p = {};
+  p.qkvg = static_cast<const __nv_bfloat16*>(qkvg_out);
+  p.qn_w = static_cast<const __nv_bfloat16*>(qn_w);
+  p.kn_w = static_cast<const __nv_bfloat16*>(kn_w);
+  p.pos_dev = pos_dev;
+  p.pos_host = pos_host;
+  p.T = 1;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.D = D;
+  p.cap = cap;
+  p.gate_per_head = gate_per_head;
+  p.eps = qk_eps;
+  p.log2_theta = log2f(rope_theta);
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.gate_out = static_cast<__nv_bfloat16*>(gate_out);
+  p.kq = k_q;
+  p.ks = static_cast<__nv_bfloat16*>(k_s);
+  p.kb = static_cast<__nv_bfloat16*>(k_b);
+  p.vq = v_q;
+  p.vs = static_cast<__nv_bfloat16*>(v_s);
+  p.vb = static_cast<__nv_bfloat16*>(v_b);
+  return dgemv_launch(a, p, false, true, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int lg_router_decode_supported(int H, int E) {

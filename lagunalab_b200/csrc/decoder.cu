@@ -9,6 +9,7 @@
 #include "common.cuh"
 #include "decode_core.cuh"
 #include "gemv_core.cuh"
+#include "prep_core.cuh"
 
 namespace lg {
 
@@ -187,139 +188,13 @@ __global__ void embed_kernel(const int32_t* ids, const uint32_t* wq, const __nv_
   }
 }
 
-// ---------------------------------------------------------------------------------------
-// Attention prologue (laguna.py:94-104): from the fused projection row
-// [q (Hq*D) | k (Hkv*D) | v (Hkv*D) | g (Hq or Hq*D)] of token t at position p = pos + t:
-//   q = rope(bf16(rmsnorm(q_h, qn_w)), p)  -> q_out [Hq, T, D]
-//   k = rope(bf16(rmsnorm(k_h, kn_w)), p)  -> k_cache [Hkv, cap, D] row p
-//   v                                       -> v_cache row p
-//   gate = bf16(softplus(float(g)))         -> gate_out [T, Hq or Hq*D]
-// RoPE is the default non-interleaved form (pairs i, i + D/2; mx.fast.rope traditional=False)
-// with inv_freq_i = theta^(-2i/D), computed in fp32 with one bf16 rounding.
-// ---------------------------------------------------------------------------------------
-struct PrepArgs {
-  const __nv_bfloat16* qkvg;
-  const __nv_bfloat16* qn_w;
-  const __nv_bfloat16* kn_w;
-  const int* pos_dev;
-  int pos_host, T, Hq, Hkv, D, cap, gate_per_head;
-  float eps, log2_theta;
-  __nv_bfloat16* q_out;
-  __nv_bfloat16* k_cache;
-  __nv_bfloat16* v_cache;
-  __nv_bfloat16* gate_out;
-  // 8-bit g64 cache destination instead of k_cache / v_cache (null: bf16 cache): words
-  // [Hkv, cap, D/4], scales and biases [Hkv, cap, D/64]
-  uint32_t* kq;
-  __nv_bfloat16 *ks, *kb;
-  uint32_t* vq;
-  __nv_bfloat16 *vs, *vb;
-};
-
-// Quantize a staged row (bf16-valued floats, D of them, D % 64 == 0) into cache row `row` of an
-// 8-bit g64 packed cache; the arithmetic of quantize_rows_kernel (quant.cu). The CTA's first
-// D/4 threads take part; contains barriers (every thread calls it).
-__device__ __forceinline__ void quantize_row8(const float* v, int D, size_t row, uint32_t* q,
-                                              __nv_bfloat16* sc, __nv_bfloat16* bi,
-                                              float* sgrp) {
-  const int i = threadIdx.x, ng = D / 64;
-  if (i < ng) {
-    float lo = INFINITY, hi = -INFINITY;
-    for (int j = 0; j < 64; ++j) {
-      lo = fminf(lo, v[i * 64 + j]);
-      hi = fmaxf(hi, v[i * 64 + j]);
-    }
-    __nv_bfloat16 sbf, bbf;
-    quant_group_params(lo, hi, 255.f, &sbf, &bbf);
-    sgrp[2 * i] = bf2f(sbf);
-    sgrp[2 * i + 1] = bf2f(bbf);
-    sc[row * ng + i] = sbf;
-    bi[row * ng + i] = bbf;
-  }
-  __syncthreads();
-  if (i < D / 4) {
-    const int g = i / 16;
-    const float s = sgrp[2 * g], bv = sgrp[2 * g + 1];
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) word |= quant_code(v[4 * i + j], s, bv, 255.f) << (8 * j);
-    q[row * (D / 4) + i] = word;
-  }
-}
-
-// one CTA (D/2 threads) per (token, head slot) (grid x: tokens, y: slots): slots [0, Hq) q
-// heads, [Hq, Hq+Hkv) k heads,
-// [Hq+Hkv, Hq+2Hkv) v heads
-__global__ void attn_prep_kernel(PrepArgs a) {
-  __shared__ float red[8];
-  __shared__ float stage[256];  // a k/v row on its way into an 8-bit cache
-  __shared__ float sgrp[8];
+// One warp per (token, head slot), four slots a CTA: grid x tokens, y slot quads (prep_head).
+__global__ void __launch_bounds__(128) attn_prep_kernel(PrepArgs a) {
+  __shared__ __align__(16) uint8_t sb[4][256];  // each warp's k/v code bytes
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.x, slot = blockIdx.y, i = threadIdx.x;
-  const int D = a.D, half = D / 2;
-  const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
-  const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
-  const __nv_bfloat16* row = a.qkvg + (size_t)t * row_stride;
-  if (slot >= a.Hq + a.Hkv) {  // v: copy into the cache
-    const int h = slot - a.Hq - a.Hkv;
-    const __nv_bfloat16* src = row + (a.Hq + a.Hkv + h) * D;
-    if (a.vq) {
-      stage[i] = bf2f(src[i]);
-      stage[i + half] = bf2f(src[i + half]);
-      __syncthreads();
-      if (pos < a.cap) quantize_row8(stage, D, (size_t)h * a.cap + pos, a.vq, a.vs, a.vb, sgrp);
-    } else if (pos < a.cap) {
-      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + pos) * D;
-      dst[i] = src[i];
-      dst[i + half] = src[i + half];
-    }
-    return;
-  }
-  const bool is_q = slot < a.Hq;
-  const int h = is_q ? slot : slot - a.Hq;
-  const __nv_bfloat16* src = row + (is_q ? h : a.Hq + h) * D;
-  const float x0 = bf2f(src[i]), x1 = bf2f(src[i + half]);
-  float ss = x0 * x0 + x1 * x1;
-  ss = warp_sum(ss);
-  if ((i & 31) == 0) red[i >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int w = 0; w < (half + 31) / 32; ++w) tot += red[w];
-  const float rn = 1.0f / sqrtf(tot / (float)D + a.eps);
-  const __nv_bfloat16* nw = is_q ? a.qn_w : a.kn_w;
-  const float n0 = round_bf16(round_bf16(x0 * rn) * bf2f(nw[i]));
-  const float n1 = round_bf16(round_bf16(x1 * rn) * bf2f(nw[i + half]));
-  const float inv_freq = exp2f(-(float)(2 * i) / (float)D * a.log2_theta);
-  float sn, cs;
-  sincosf((float)pos * inv_freq, &sn, &cs);
-  const float o0 = n0 * cs - n1 * sn;
-  const float o1 = n0 * sn + n1 * cs;
-  if (is_q) {
-    __nv_bfloat16* dst = a.q_out + ((size_t)h * a.T + t) * D;
-    dst[i] = __float2bfloat16_rn(o0);
-    dst[i + half] = __float2bfloat16_rn(o1);
-    // the output gate of this head (softplus = logaddexp(g, 0), in fp32)
-    const __nv_bfloat16* g = row + (a.Hq + 2 * a.Hkv) * D;
-    auto softplus = [](float v) { return fmaxf(v, 0.f) + log1pf(expf(-fabsf(v))); };
-    if (a.gate_per_head) {
-      if (i == 0)
-        a.gate_out[(size_t)t * a.Hq + h] = __float2bfloat16_rn(softplus(bf2f(g[h])));
-    } else {
-      __nv_bfloat16* go = a.gate_out + (size_t)t * a.Hq * D + (size_t)h * D;
-      go[i] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i])));
-      go[i + half] = __float2bfloat16_rn(softplus(bf2f(g[h * D + i + half])));
-    }
-  } else if (a.kq) {
-    stage[i] = round_bf16(o0);
-    stage[i + half] = round_bf16(o1);
-    __syncthreads();
-    if (pos < a.cap) quantize_row8(stage, D, (size_t)h * a.cap + pos, a.kq, a.ks, a.kb, sgrp);
-  } else if (pos < a.cap) {
-    __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + pos) * D;
-    dst[i] = __float2bfloat16_rn(o0);
-    dst[i + half] = __float2bfloat16_rn(o1);
-  }
+  const int w = threadIdx.x >> 5, slot = (int)blockIdx.y * 4 + w;
+  if (slot < a.Hq + 2 * a.Hkv) prep_head(a, blockIdx.x, slot, true, sb[w]);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -495,8 +370,8 @@ static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const 
   a.vs = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[2])) : nullptr;
   a.vb = q8 ? static_cast<__nv_bfloat16*>(const_cast<void*>(q8sb[3])) : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dim3 grid(T, Hq + 2 * Hkv);  // tokens on x: prefill lengths beyond 65,535
-  LG_CUDA_TRY(launch_k(attn_prep_kernel, grid, dim3(D / 2), 0, st, a));
+  dim3 grid(T, (Hq + 2 * Hkv + 3) / 4);  // tokens on x: prefill lengths beyond 65,535
+  LG_CUDA_TRY(launch_k(attn_prep_kernel, grid, dim3(128), 0, st, a));
   LG_LAUNCH_CHECK("attn_prep");
   return LG_OK;
 }

@@ -1,0 +1,171 @@
+// The attention prologue of one (token, head slot), shared by the standalone prologue kernel
+// (decoder.cu) and the q/k/v/g projection GEMV that finishes each head itself (decode.cu), so
+// both give the same bits.
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+
+namespace lg {
+
+// ---------------------------------------------------------------------------------------
+// Attention prologue (laguna.py:94-104): from the fused projection row
+// [q (Hq*D) | k (Hkv*D) | v (Hkv*D) | g (Hq or Hq*D)] of token t at position p = pos + t:
+//   q = rope(bf16(rmsnorm(q_h, qn_w)), p)  -> q_out [Hq, T, D]
+//   k = rope(bf16(rmsnorm(k_h, kn_w)), p)  -> k_cache [Hkv, cap, D] row p
+//   v                                       -> v_cache row p
+//   gate = bf16(softplus(float(g)))         -> gate_out [T, Hq or Hq*D]
+// RoPE is the default non-interleaved form (pairs i, i + D/2; mx.fast.rope traditional=False)
+// with inv_freq_i = theta^(-2i/D), computed in fp32 with one bf16 rounding.
+// ---------------------------------------------------------------------------------------
+struct PrepArgs {
+  const __nv_bfloat16* qkvg;
+  const __nv_bfloat16* qn_w;
+  const __nv_bfloat16* kn_w;
+  const int* pos_dev;
+  int pos_host, T, Hq, Hkv, D, cap, gate_per_head;
+  float eps, log2_theta;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* gate_out;
+  // 8-bit g64 cache destination instead of k_cache / v_cache (null: bf16 cache): words
+  // [Hkv, cap, D/4], scales and biases [Hkv, cap, D/64]
+  uint32_t* kq;
+  __nv_bfloat16 *ks, *kb;
+  uint32_t* vq;
+  __nv_bfloat16 *vs, *vb;
+};
+
+// Quantize the row that one warp holds (lane l: elements l + 32 k, k < 2P, so element k's group
+// of 64 is k / 2) into cache row `row` of an 8-bit g64 packed cache; the arithmetic of
+// quantize_rows_kernel (quant.cu). sb: 64 P bytes of the warp's own shared memory.
+template <int P>
+__device__ __forceinline__ void quantize_row8_warp(const float (&v)[2 * P], size_t row,
+                                                   uint32_t* q, __nv_bfloat16* sc,
+                                                   __nv_bfloat16* bi, uint8_t* sb) {
+  constexpr int D = 64 * P;
+  const int l = threadIdx.x & 31;
+  float s[P], b[P];
+#pragma unroll
+  for (int g = 0; g < P; ++g) {
+    float lo = fminf(v[2 * g], v[2 * g + 1]), hi = fmaxf(v[2 * g], v[2 * g + 1]);
+    warp_minmax(lo, hi);
+    __nv_bfloat16 sbf, bbf;
+    quant_group_params(lo, hi, 255.f, &sbf, &bbf);
+    if (l == g) {
+      sc[row * P + g] = sbf;
+      bi[row * P + g] = bbf;
+    }
+    s[g] = bf2f(sbf);
+    b[g] = bf2f(bbf);
+  }
+#pragma unroll
+  for (int k = 0; k < 2 * P; ++k)
+    sb[l + 32 * k] = (uint8_t)quant_code(v[k], s[k / 2], b[k / 2], 255.f);
+  __syncwarp();
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(sb);  // byte j of word i: element 4i+j
+#pragma unroll
+  for (int i = l; i < D / 4; i += 32) q[row * (D / 4) + i] = w[i];
+  __syncwarp();
+}
+
+// The output gate bf16(softplus(float(g))) (laguna.py:105-106), softplus = logaddexp(g, 0).
+__device__ __forceinline__ __nv_bfloat16 prep_gate(float g) {
+  return __float2bfloat16_rn(fmaxf(g, 0.f) + log1pf(expf(-fabsf(g))));
+}
+
+// One (token t, head slot) of the prologue, by one warp: slots [0, Hq) q heads, [Hq, Hq+Hkv)
+// k heads, [Hq+Hkv, Hq+2Hkv) v heads; D = 64 P. Lane l holds elements l + 32 k (k < 2P), so the
+// rotary pairs (i, i + D/2) are its own slots (k, k + P) and no barrier is needed. write_gate: a
+// q head also writes its output gate(s). The projection row is read through L2 (it may come
+// from other CTAs of the same launch). sb: 64 P bytes of the warp's own shared memory.
+template <int P>
+__device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slot,
+                                               bool write_gate, uint8_t* sb) {
+  constexpr int D = 64 * P;
+  const int l = threadIdx.x & 31;
+  const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
+  const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
+  const __nv_bfloat16* row = a.qkvg + (size_t)t * row_stride;
+  float x[2 * P];
+  if (slot >= a.Hq + a.Hkv) {  // v: into the cache as it is
+    const int h = slot - a.Hq - a.Hkv;
+    const __nv_bfloat16* src = row + (a.Hq + a.Hkv + h) * D;
+    if (pos >= a.cap) return;
+    if (a.vq) {
+#pragma unroll
+      for (int k = 0; k < 2 * P; ++k) x[k] = bf2f(__ldcg(src + l + 32 * k));
+      quantize_row8_warp<P>(x, (size_t)h * a.cap + pos, a.vq, a.vs, a.vb, sb);
+    } else {
+      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + pos) * D;
+#pragma unroll
+      for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __ldcg(src + l + 32 * k);
+    }
+    return;
+  }
+  const bool is_q = slot < a.Hq;
+  const int h = is_q ? slot : slot - a.Hq;
+  const __nv_bfloat16* src = row + (is_q ? h : a.Hq + h) * D;
+  const __nv_bfloat16* nw = is_q ? a.qn_w : a.kn_w;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2 * P; ++k) {
+    x[k] = bf2f(__ldcg(src + l + 32 * k));
+    ss += x[k] * x[k];
+  }
+  ss = warp_sum(ss);
+  const float rn = 1.0f / sqrtf(ss / (float)D + a.eps);
+#pragma unroll
+  for (int k = 0; k < 2 * P; ++k) x[k] = round_bf16(round_bf16(x[k] * rn) * bf2f(nw[l + 32 * k]));
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int i = l + 32 * j;
+    const float inv_freq = exp2f(-(float)(2 * i) / (float)D * a.log2_theta);
+    float sn, cs;
+    sincosf((float)pos * inv_freq, &sn, &cs);
+    const float n0 = x[j], n1 = x[j + P];
+    x[j] = n0 * cs - n1 * sn;
+    x[j + P] = n0 * sn + n1 * cs;
+  }
+  if (is_q) {
+    __nv_bfloat16* dst = a.q_out + ((size_t)h * a.T + t) * D;
+#pragma unroll
+    for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __float2bfloat16_rn(x[k]);
+    if (write_gate) {
+      const __nv_bfloat16* g = row + (a.Hq + 2 * a.Hkv) * D;
+      if (a.gate_per_head) {
+        if (l == 0) a.gate_out[(size_t)t * a.Hq + h] = prep_gate(bf2f(__ldcg(g + h)));
+      } else {
+        __nv_bfloat16* go = a.gate_out + (size_t)t * a.Hq * D + (size_t)h * D;
+#pragma unroll
+        for (int k = 0; k < 2 * P; ++k)
+          go[l + 32 * k] = prep_gate(bf2f(__ldcg(g + h * D + l + 32 * k)));
+      }
+    }
+  } else if (pos < a.cap) {
+    if (a.kq) {
+#pragma unroll
+      for (int k = 0; k < 2 * P; ++k) x[k] = round_bf16(x[k]);
+      quantize_row8_warp<P>(x, (size_t)h * a.cap + pos, a.kq, a.ks, a.kb, sb);
+    } else {
+      __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + pos) * D;
+#pragma unroll
+      for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __float2bfloat16_rn(x[k]);
+    }
+  }
+}
+
+// prep_head_warp for the head size a.D (64, 128 or 256; the hosts check it).
+__device__ __forceinline__ void prep_head(const PrepArgs& a, int t, int slot, bool write_gate,
+                                          uint8_t* sb) {
+  if (a.D == 128)
+    prep_head_warp<2>(a, t, slot, write_gate, sb);
+  else if (a.D == 64)
+    prep_head_warp<1>(a, t, slot, write_gate, sb);
+  else
+    prep_head_warp<4>(a, t, slot, write_gate, sb);
+}
+
+}  // namespace lg

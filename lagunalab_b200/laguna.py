@@ -17,7 +17,7 @@ from typing import Any, Dict, List, Optional
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 
 @dataclass
@@ -411,6 +411,10 @@ class Attention:
         if B != 1:
             raise NotImplementedError("batch size 1 only on this path")
         Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
+        if in_norm is not None and L == 1 and pos_dev is not None and cache is not None:
+            out = self._fused_token(x.reshape(1, H), cache, residual, pos_dev, in_norm)
+            if out is not None:
+                return out.reshape(B, L, H)
         if in_norm is None:
             qkvg = self._qkvg(x.reshape(L, H))
         elif L == 1:
@@ -466,6 +470,44 @@ class Attention:
         out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
         return out.reshape(B, L, H)
 
+    def _fused_token(self, x, cache, residual, pos_dev, in_norm):
+        """A device-position single-token step with the q/k/v/g projection and the attention
+        prologue in one launch (``ops.decode_qkv_prep``); None when the shape needs the
+        two-launch form."""
+        Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
+        per_head = self.per_head_gate
+        q8 = getattr(cache, "q", None) is not None
+        if q8:
+            if not cache.fused_decode:
+                return None
+            qc = cache.q
+            qc.reserve(1, Hkv, D, 1, x.device)
+            ck, cv = qc.keys, qc.values
+        else:
+            if cache.keys is None:
+                return None
+            ck, cv = cache.keys[0], cache.values[0]
+        try:
+            _, q, gate = ops.decode_qkv_prep(x, self._qkvg.mat, (in_norm.weight, in_norm.eps),
+                                             Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                             self.eps, self.rope_theta, ck, cv, pos_dev=pos_dev,
+                                             gate_per_head=per_head)
+        except _lib.LagunaError as e:
+            if e.code != _lib.LG_ERR_UNSUPPORTED:
+                raise
+            return None
+        if q8:
+            cap = ck[0].shape[2]
+            o = ops.q8_decode_attention_dev(q.view(1, Hq, D), ck, cv, cap, pos_dev, 1,
+                                            self.scale, gate=gate if per_head else None)
+        else:
+            o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, 0,
+                                          self.scale, gate=gate if per_head else None,
+                                          n_dev=pos_dev, n_add=1)
+        o = o.view(1, Hq * D)
+        if not per_head:
+            o = o * gate.view(1, Hq * D)
+        return self.o_proj(o, residual=None if residual is None else residual.reshape(1, -1))
 
     def _q8_attention(self, qkvg, L, cache, pos_dev, device):
         """Attention over an 8-bit group-64 DequantKVCache (laguna_mlx/cache.py:89-106): the new

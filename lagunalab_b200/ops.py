@@ -351,6 +351,42 @@ def decode_gemv(x, mat, norm=None, residual=None, up=None, out=None, group_size=
     return out
 
 
+def decode_qkv_prep(x, mat, norm, Hq, Hkv, D, qn_w, kn_w, qk_eps, theta, cache_k, cache_v,
+                    pos=0, pos_dev=None, gate_per_head=True):
+    """One token's q/k/v/g projection (input RMSNorm ``norm=(weight, eps)`` fused in) and its
+    attention prologue in one launch; returns (qkvg [1, N], q [Hq, 1, D], gate). ``cache_k`` /
+    ``cache_v``: the bf16 cache [Hkv, cap, D] tensors, or the 8-bit cache's (words, scales,
+    biases) tuples; the new rows go to row ``pos`` (or ``pos_dev[0]``). The same bits as
+    ``decode_gemv`` followed by ``attn_prep`` / ``attn_prep_q8``."""
+    q_, s_, b_ = _qm(mat)
+    K = x.shape[-1]
+    N = q_.shape[0]
+    if N != (Hq + 2 * Hkv) * D + (Hq if gate_per_head else Hq * D):
+        raise ValueError(f"decode_qkv_prep: {N} projection rows for heads {Hq}/{Hkv} x {D}")
+    x2 = _c(x, torch.bfloat16).reshape(1, K)
+    dev = x2.device
+    qkvg = torch.empty(1, N, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(Hq, 1, D, dtype=torch.bfloat16, device=dev)
+    gate = torch.empty(1, Hq if gate_per_head else Hq * D, dtype=torch.bfloat16, device=dev)
+    if isinstance(cache_k, tuple):
+        kq, ks, kb = cache_k
+        vq, vs, vb = cache_v
+        cap = kq.shape[-2]
+        kc = vc = None
+    else:
+        kq = ks = kb = vq = vs = vb = None
+        kc, vc = cache_k, cache_v
+        cap = kc.shape[-2]
+    nws = _lib.lib().lg_decode_qkv_prep_workspace_bytes(Hq, Hkv)
+    ws = workspace(dev, "qkv_prep", nws, zero=True)
+    _lib.call("lg_decode_qkv_prep", _p(x2), K, _p(q_), _p(s_), _p(b_),
+              _p(_c(norm[0], torch.bfloat16)), float(norm[1]), Hq, Hkv, D, _p(_c(qn_w)),
+              _p(_c(kn_w)), float(qk_eps), float(theta), _p(pos_dev), int(pos),
+              int(bool(gate_per_head)), _p(qkvg), _p(q), _p(gate), _p(kc), _p(vc), _p(kq),
+              _p(ks), _p(kb), _p(vq), _p(vs), _p(vb), cap, _p(ws), ws.numel(), _stream(dev))
+    return qkvg, q, gate
+
+
 def router_decode(h, norm_w, eps, gate, e_bias, k, norm_topk_prob=True, score_fn="sigmoid",
                   logits=False):
     """One token's post-attention RMSNorm and router in one launch: from the residual stream
