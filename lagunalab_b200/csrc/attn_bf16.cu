@@ -297,13 +297,11 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
     a.part_acc[(pbase + h) * AB_D + d] = v;
   }
   if (threadIdx.x < G) a.part_ml[pbase + threadIdx.x] = make_float2(s_M[threadIdx.x], s_L[threadIdx.x]);
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // this split's partials are stored before thread 0 releases them
   int* ctr = a.counters + bh * 32;
-  if (threadIdx.x == 0) s_last = (atomicAdd(ctr, 1) == ns - 1);
-  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atom_add_acq_rel_gpu(ctr, 1) == ns - 1);
+  __syncthreads();  // the merger: every split's partials, acquired by thread 0, are visible
   if (!s_last) return;
-  __threadfence();
   // ---- the last CTA of this (batch, kv head) merges the splits: split weights staged in
   // shared memory (reusing the slab), then each thread sums its float4 items over the
   // splits with 16 loads in flight ----

@@ -109,6 +109,9 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v
                : "memory");
   return old;
 }
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  return (int)atom_add_acq_rel_gpu(reinterpret_cast<unsigned*>(p), (unsigned)v);
+}
 
 // Read-only 128-bit global load that bypasses L1 allocation (weights are streamed once).
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {

@@ -151,9 +151,7 @@ __host__ __device__ __forceinline__ uint32_t dg_ring_off(int K, int NW) {
 // grid: CTAs take tiles blockIdx.x, blockIdx.x + gridDim.x, ...; `stages` tiles in flight.
 // NW warps split each tile's K groups. PREP: the attention prologue behind a q/k/v/g projection.
 template <bool GLU, int NW, int V, bool PREP>
-// The q/k/v/g projection keeps three 8-warp CTAs per SM (its tiles fit the GPU in one wave).
-__global__ void __launch_bounds__(NW * 32, PREP && NW == 8 ? 3 : 1)
-    dgemv_kernel(DgArgs a, PrepArgs p) {
+__device__ __forceinline__ void dgemv_body(const DgArgs& a, const PrepArgs& p) {
   constexpr int NM = GLU ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, gpr = K / 64, S = a.stages;
@@ -259,6 +257,19 @@ __global__ void __launch_bounds__(NW * 32, PREP && NW == 8 ? 3 : 1)
   }
 }
 
+template <bool GLU, int NW, int V>
+__global__ void __launch_bounds__(NW * 32) dgemv_kernel(DgArgs a) {
+  dgemv_body<GLU, NW, V, false>(a, PrepArgs{});
+}
+
+// The q/k/v/g projection with the prologue: its tiles must fit the GPU in one wave (the per-head
+// counters need no co-residency, but a second wave would add its whole duration), so the
+// kernel keeps to three 8-warp CTAs per SM.
+template <int V>
+__global__ void __launch_bounds__(256, 3) dgemv_prep_kernel(DgArgs a, PrepArgs p) {
+  dgemv_body<false, 8, V, true>(a, p);
+}
+
 // ---- router ----------------------------------------------------------------------------------
 
 constexpr int RD_WARPS = 8;  // a warp per expert
@@ -351,20 +362,12 @@ __global__ void __launch_bounds__(RD_WARPS * 32) router_decode_kernel(RdArgs a) 
     const float v = router_logit8(reinterpret_cast<const __nv_bfloat162*>(xs),
                                   reinterpret_cast<const uint32_t*>(wq + (size_t)warp * H),
                                   ws + warp * gpr, wb + warp * gpr, H);
-    if (lane == 0) {
-      a.lg_ws[e0 + warp] = v;
-      __threadfence();
-    }
+    if (lane == 0) a.lg_ws[e0 + warp] = v;
   }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    *flag = atomicAdd(a.counter, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
+  __syncthreads();  // this CTA's logits are stored before thread 0 releases them
+  if (tid == 0) *flag = atom_add_acq_rel_gpu(a.counter, 1u) == gridDim.x - 1;
+  __syncthreads();  // the last CTA: every CTA's logits, acquired by thread 0, are visible
   if (!*flag) return;
-  // last CTA: every CTA's logits are visible
-  __threadfence();
   if (tid < 32) slot[tid] = -1;
   if (warp == 0) topk_scores_warp([&](int e) { return __ldcg(a.lg_ws + e); }, E, ebs,
                                   a.score_fn, keys, vals);
@@ -598,13 +601,11 @@ __global__ void __launch_bounds__(DN_WARPS * 32) moe_dec_down_kernel(MdArgs a) {
     }
   }
   if (tid < 16) a.ypart[((size_t)mt * G + j) * 16 + tid] = y[0];
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) *flag = atomicAdd(a.counters + mt, 1u) == (unsigned)(G - 1);
-  __syncthreads();
+  __syncthreads();  // the group's partial is stored before thread 0 releases it
+  if (tid == 0) *flag = atom_add_acq_rel_gpu(a.counters + mt, 1u) == (unsigned)(G - 1);
+  __syncthreads();  // the last group: every group's partial, acquired by thread 0, is visible
   if (!*flag) return;
   // the last group of this slice: combine every group in order
-  __threadfence();
   if (tid < G) {
     int ej;
     float wj = 1.0f;
@@ -664,21 +665,20 @@ static int vec_width(int gpr, int nw) {
   return gpw % 8 == 0 ? 8 : gpw % 4 == 0 ? 4 : gpw % 2 == 0 ? 2 : 1;
 }
 
-template <bool GLU, int NW, int V, bool PREP>
-static cudaError_t launch_dgemv_k(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
-                                  cudaStream_t st) {
-  cudaError_t e = allow_smem(dgemv_kernel<GLU, NW, V, PREP>, smem);
-  return e != cudaSuccess
-             ? e
-             : launch_k(dgemv_kernel<GLU, NW, V, PREP>, grid, dim3(NW * 32), smem, st, a, p);
-}
-
 template <bool GLU, int NW, int V>
 static cudaError_t launch_dgemv_v(const DgArgs& a, const PrepArgs& p, dim3 grid, size_t smem,
                                   cudaStream_t st) {
-  if constexpr (!GLU)
-    if (a.prep) return launch_dgemv_k<false, NW, V, true>(a, p, grid, smem, st);
-  return launch_dgemv_k<GLU, NW, V, false>(a, p, grid, smem, st);
+  if constexpr (!GLU && NW == 8) {
+    if (a.prep) {
+      cudaError_t e = allow_smem(dgemv_prep_kernel<V>, smem);
+      return e != cudaSuccess
+                 ? e
+                 : launch_k(dgemv_prep_kernel<V>, grid, dim3(NW * 32), smem, st, a, p);
+    }
+  }
+  cudaError_t e = allow_smem(dgemv_kernel<GLU, NW, V>, smem);
+  return e != cudaSuccess ? e
+                          : launch_k(dgemv_kernel<GLU, NW, V>, grid, dim3(NW * 32), smem, st, a);
 }
 
 template <bool GLU, int NW>
@@ -801,7 +801,9 @@ extern "C" int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, con
                "decode_qkv_prep: heads %d/%d, head_dim %d (a multiple of 64, <= 256)", Hq, Hkv, D);
   LG_CHECK_ARG(x && norm_w && qn_w && kn_w && qkvg_out && q_out && gate_out,
                "decode_qkv_prep: NULL pointer");
-  LG_CHECK_ARG(K >= 2 * D, "decode_qkv_prep: hidden %d below twice head_dim %d", K, D);
+  LG_CHECK_ARG(2 * K >= D, "decode_qkv_prep: hidden %d below half of head_dim %d", K, D);
+  if (dg_warps(K) != 8)  // the fused form is built for 8-warp CTAs (hidden < 4096)
+    return fail(LG_ERR_UNSUPPORTED, "decode_qkv_prep: hidden %d takes the two-launch form", K);
   const bool q8 = k_q != nullptr;
   LG_CHECK_ARG(q8 ? (k_s && k_b && v_q && v_s && v_b && !k_cache && !v_cache)
                   : (k_cache && v_cache),
@@ -915,6 +917,7 @@ extern "C" int lg_router_decode(const void* h, const void* norm_w, float eps, in
   LG_LAUNCH_CHECK("router_decode");
   return LG_OK;
 }
+
 
 extern "C" size_t lg_moe_decode_workspace_bytes(int H, int I, int I_shared, int k) {
   const int Imax = I > I_shared ? I : I_shared;

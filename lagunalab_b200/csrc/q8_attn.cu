@@ -600,16 +600,14 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
     a.part_ml[bh * mls + split * G + threadIdx.x] = make_float2(s_M[threadIdx.x], s_L[threadIdx.x]);
 
   // ---- the last CTA of this (batch, kv head) merges every split ----
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // this split's partials are stored before thread 0 releases them
   if (threadIdx.x == 0) {
     const int add = 1 + (s_flag[0] ? (1 << 20) : 0);
-    const int total = atomicAdd(&a.counters[bh * 32], add) + add;
+    const int total = atom_add_acq_rel_gpu(&a.counters[bh * 32], add) + add;
     s_flag[1] = ((total & 0xFFFFF) == ns) ? ((total >> 20) ? 2 : 1) : 0;
   }
-  __syncthreads();
+  __syncthreads();  // the merger: every split's partials, acquired by thread 0, are visible
   if (s_flag[1] == 0) return;
-  __threadfence();
   const int nsg = ns * G;
   const float2* gml = a.part_ml + bh * mls;
   const float* gacc = a.part_acc + (size_t)bh * nsg * QA_D;
