@@ -1,0 +1,45 @@
+"""Replay scoring through the B200 decoder (lagunaLab replay/replay.py:23-124): a reference
+built by the sm_100a engine scores against itself (whole and chunked prefill through one
+cache), the CPU oracle decoder scored through the ``forward=`` contract against that
+reference agrees within bf16 noise, and the stored greedy actions reproduce."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model_ref
+from tests._replay_util import CharTokenizer, write_capture
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny():
+    from lagunalab_b200 import synth
+    args = synth.decoder_args(vocab=512, hidden=256, layers=3, heads=4, kv_heads=2, head_dim=128,
+                              experts=8, top_k=2, moe_inter=128, shared_inter=128, dense_inter=256,
+                              rope_theta=1e4)
+    model = synth.decoder(args, seed=4, std=0.05, norm_noise=0.1, router_bias_std=0.3)
+    return args, model, synth.oracle_weights(model), synth.oracle_args(args)
+
+
+def test_replay_scores_on_b200(tmp_path):
+    from lagunalab_b200 import replay
+    args, model, W, oargs = _tiny()
+    tok = CharTokenizer(vocab=512)
+    out = tmp_path / "s.npz"
+    replay.build_ref(model, tok, write_capture(tmp_path / "s.jsonl"), out, n_actions=2,
+                     max_new=4, model_id="tiny")
+    ref = np.load(out)
+    assert ref["top_ids"].shape == (len(ref["pos"]), replay.TOPK)
+
+    same = replay.score(model, out)
+    assert same["kl_top64_mean"] < 1e-4 and same["top1_agree"] >= 0.95
+    chunked = replay.score(model, out, chunk=16)
+    assert chunked["kl_top64_mean"] < 1e-3 and chunked["top1_agree"] >= 0.9
+    assert same["peak_mem_gb"] > 0
+
+    n_layers = len(W["layers"])
+    fwd = lambda x, c: model_ref.forward(W, oargs, x[0].long(), c)[None]
+    oracle = replay.score(None, out, make_cache=lambda: model_ref.Cache(n_layers), forward=fwd)
+    assert oracle["kl_top64_mean"] < 1e-2 and oracle["top1_agree"] >= 0.8, oracle
+
+    assert replay.score_actions(model, tok, out) == 1.0
