@@ -746,6 +746,35 @@ def model_from_weights(args, weights, quantization=None, device="cuda", switch_m
     return Model(args, model, lin("lm_head"))
 
 
+def load(path, device="cuda"):
+    """(model, tokenizer) from an MLX-format checkpoint directory (what mlx-lm's ``load``
+    reads for this architecture, laguna.py:196-241): ``config.json`` with its
+    "quantization" entry and the ``*.safetensors`` shards. Per-expert (unstacked) weights
+    and the experts' router bias are rearranged by ``Model.sanitize``. The tokenizer is the
+    directory's Hugging Face tokenizer when it has one, else None."""
+    import json
+    from pathlib import Path
+
+    from safetensors.torch import load_file
+
+    path = Path(path)
+    config = json.loads((path / "config.json").read_text())
+    args = ModelArgs.from_dict(config)
+    shards = sorted(path.glob("*.safetensors"))
+    if not shards:
+        raise FileNotFoundError(f"{path}: no *.safetensors weights")
+    weights = {}
+    for f in shards:
+        weights.update(load_file(str(f)))
+    weights = Model.sanitize(Model(args, None, None), weights)
+    model = model_from_weights(args, weights, config.get("quantization"), device)
+    tok = None
+    if (path / "tokenizer.json").exists() or (path / "tokenizer_config.json").exists():
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(str(path))
+    return model, tok
+
+
 class DecodeGraph:
     """Greedy bs1 decoding one CUDA-graph replay per token. The token id and the cache
     position live on the device: each step embeds ``tok``, runs every layer at position

@@ -135,6 +135,19 @@ def model_config(args, group_size=64, bits=4):
     return c
 
 
+def save_checkpoint(model, out_dir, group_size=64, bits=4):
+    """Write ``model`` as an MLX-format checkpoint directory (``config.json`` +
+    ``model.safetensors``, packed words as uint32), the layout ``laguna.load`` reads."""
+    from safetensors.torch import save_file
+    out = Path(out_dir)
+    out.mkdir(parents=True, exist_ok=True)
+    w = {k: (t.view(torch.uint32) if t.dtype == torch.int32 else t)
+         for k, t in model_weights(model).items()}
+    save_file(w, str(out / "model.safetensors"))
+    (out / "config.json").write_text(json.dumps(model_config(model.args, group_size, bits),
+                                                indent=1))
+
+
 def pack_model(model, out_dir, group_size=64, bits=4):
     """Write ``model`` in the pack format (same byte layout as scripts/pack_experts.py)."""
     from safetensors.torch import save_file

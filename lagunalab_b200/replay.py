@@ -174,8 +174,10 @@ def score_actions(model, tokenizer, ref_path, max_new=None):
 
 
 def main(argv=None):
-    """CLI of replay.py:127-164; ``--model`` is an expert pack directory (``load_streaming``,
-    every expert resident)."""
+    """CLI of replay.py:127-164; ``--model`` is an MLX-format checkpoint directory
+    (``laguna.load``) or an expert pack directory (``load_streaming``, every expert
+    resident)."""
+    from .laguna import load
     from .streaming import load_streaming
 
     p = argparse.ArgumentParser()
@@ -187,7 +189,10 @@ def main(argv=None):
     p.add_argument("--max-tokens", type=int, default=65536)
     p.add_argument("--actions", action="store_true")
     a = p.parse_args(argv)
-    model, tok = load_streaming(a.model, slots=0)
+    if (Path(a.model) / "layout.json").exists():
+        model, tok = load_streaming(a.model, slots=0)
+    else:
+        model, tok = load(a.model)
     refs = Path(a.refs)
     if a.cmd == "build-ref":
         refs.mkdir(exist_ok=True)

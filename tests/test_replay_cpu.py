@@ -148,3 +148,13 @@ def test_forward_contract_and_position_check(tmp_path):
     np.savez(tmp_path / "bad.npz", **ref)
     with pytest.raises(AssertionError, match="position mismatch"):
         replay.score(m, tmp_path / "bad.npz")
+
+
+def test_load_needs_weight_shards(tmp_path):
+    from lagunalab_b200 import laguna, pack, synth
+    args = synth.decoder_args(vocab=512, hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128,
+                              experts=8, top_k=2, moe_inter=128, shared_inter=128,
+                              dense_inter=256)
+    (tmp_path / "config.json").write_text(json.dumps(pack.model_config(args)))
+    with pytest.raises(FileNotFoundError, match="safetensors"):
+        laguna.load(tmp_path)

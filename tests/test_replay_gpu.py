@@ -43,3 +43,18 @@ def test_replay_scores_on_b200(tmp_path):
     assert oracle["kl_top64_mean"] < 1e-2 and oracle["top1_agree"] >= 0.8, oracle
 
     assert replay.score_actions(model, tok, out) == 1.0
+
+
+def test_checkpoint_round_trip_scores_like_the_original(tmp_path):
+    """``pack.save_checkpoint`` -> ``laguna.load`` (MLX checkpoint directory) gives a model
+    that scores against the original's replay reference within bf16 noise."""
+    from lagunalab_b200 import laguna, pack, replay
+    args, model, W, oargs = _tiny()
+    out = tmp_path / "s.npz"
+    replay.build_ref(model, CharTokenizer(vocab=512), write_capture(tmp_path / "s.jsonl"), out,
+                     n_actions=0)
+    pack.save_checkpoint(model, tmp_path / "ckpt")
+    loaded, tok = laguna.load(tmp_path / "ckpt")
+    assert tok is None
+    got = replay.score(loaded, out)
+    assert got["kl_top64_mean"] < 1e-4 and got["top1_agree"] >= 0.95, got
