@@ -75,4 +75,5 @@ def test_checkpoint_round_trip_scores_like_the_original(tmp_path):
     assert tok is None
     got = replay.score(loaded, out)
     assert got["kl_top64_mean"] < 1e-4, got
+    ref = np.load(out)
     _agrees_off_ties(ref, replay.assistant_logprobs(loaded, ref["ids"], ref["mask"]))
