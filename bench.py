@@ -525,27 +525,14 @@ def cpu_moe(wl, steps, warmup, sample_tokens=256):
     from oracle import moe_ref
     from lagunalab_b200 import synth
     T, E, k, H, I, I_sh = (wl[n] for n in ("T", "E", "k", "H", "I", "I_sh"))
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    if dev == "cuda":
-        blk, x = synth.moe_block(T, E, k, H, I, I_sh, seed=0, zipf=wl["zipf"],
-                                 routed_scaling_factor=wl["scale"])
-        deq = lambda m: moe_ref.dequantize(*(t.cpu() for t in m.mat), 64, 4)
-        wg, wu, wd = (deq(m) for m in (blk.switch_mlp.gate_proj, blk.switch_mlp.up_proj,
-                                       blk.switch_mlp.down_proj))
-        sh = tuple(deq(m) for m in (blk.shared_expert.gate_proj, blk.shared_expert.up_proj,
-                                    blk.shared_expert.down_proj))
-        router, bias = blk.gate.cpu(), blk.e_score_correction_bias.cpu()
-        xs = x[:sample_tokens].cpu()
-        del blk, x
-        torch.cuda.empty_cache()
-    else:  # a CPU-only host: same shapes, weights drawn here
-        g = torch.Generator().manual_seed(0)
-        r = lambda *s: torch.randn(*s, generator=g) * 0.02
-        wg, wu, wd = r(E, I, H), r(E, I, H), r(E, H, I)
-        sh = (r(I_sh, H), r(I_sh, H), r(H, I_sh))
-        router = r(E, H)
-        bias = synth.zipf_bias(E, 0, device="cpu") if wl["zipf"] else torch.zeros(E)
-        xs = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16)
+    # weights drawn and kept on the CPU (the library is never loaded on this leg)
+    g = torch.Generator().manual_seed(0)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.02
+    wg, wu, wd = r(E, I, H), r(E, I, H), r(E, H, I)
+    sh = (r(I_sh, H), r(I_sh, H), r(H, I_sh))
+    router = r(E, H)
+    bias = synth.zipf_bias(E, 0, device="cpu") if wl["zipf"] else torch.zeros(E)
+    xs = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16)
     nt = cpu_threads()
     torch.set_num_threads(nt)
 
@@ -571,22 +558,18 @@ def cpu_q8(wl, steps, warmup, sample_layers=1):
     from oracle import attn_ref
     from lagunalab_b200 import synth
     n, B, Hq, Hkv = (wl[k] for k in ("n", "B", "Hq", "Hkv"))
-    if torch.cuda.is_available():
-        layers = synth.q8_layers(sample_layers, n, B, Hq, Hkv, seed=0)
-        layers = [(q.cpu(), tuple(t.cpu() for t in kt), tuple(t.cpu() for t in vt))
-                  for q, kt, vt in layers]
-    else:
-        layers = []
-        for _ in range(sample_layers):
-            g = torch.Generator().manual_seed(0)
-            mk = lambda: tuple(
-                torch.from_numpy(a.view("int32") if a.dtype.kind == "u" and a.itemsize == 4
-                                 else a.view("int16")) for a in
-                attn_ref.quantize_rows(torch.randn(B, Hkv, n, 128, generator=g).numpy(), 64, 8))
-            kt, vt = mk(), mk()
-            kt = (kt[0], kt[1].view(torch.bfloat16), kt[2].view(torch.bfloat16))
-            vt = (vt[0], vt[1].view(torch.bfloat16), vt[2].view(torch.bfloat16))
-            layers.append((torch.randn(B, Hq, 1, 128, generator=g).to(torch.bfloat16), kt, vt))
+    # cache rows quantized on the CPU (the library is never loaded on this leg)
+    layers = []
+    for _ in range(sample_layers):
+        g = torch.Generator().manual_seed(0)
+        mk = lambda: tuple(
+            torch.from_numpy(a.view("int32") if a.dtype.kind == "u" and a.itemsize == 4
+                             else a.view("int16")) for a in
+            attn_ref.quantize_rows(torch.randn(B, Hkv, n, 128, generator=g).numpy(), 64, 8))
+        kt, vt = mk(), mk()
+        kt = (kt[0], kt[1].view(torch.bfloat16), kt[2].view(torch.bfloat16))
+        vt = (vt[0], vt[1].view(torch.bfloat16), vt[2].view(torch.bfloat16))
+        layers.append((torch.randn(B, Hq, 1, 128, generator=g).to(torch.bfloat16), kt, vt))
     nt = cpu_threads()
     torch.set_num_threads(nt)
 
@@ -608,66 +591,109 @@ def cpu_q8(wl, steps, warmup, sample_layers=1):
                        f"(oracle restatement: dequantize + fp32 softmax)")
 
 
-def cpu_decode(wl, steps, warmup):
-    """The oracle's decode step on a bounded sample: one MoE layer (attention over the
-    prefill's context + MoE block) and the lm_head, on the config-3 weights, scaled to the
-    whole model: seconds/token = layers x t(layer) + t(lm_head)."""
-    from oracle import model_ref, moe_ref
+def _oracle_quantize(t, bits):
+    """The oracle's quantizer in threads over row blocks -> torch (int32, bf16, bf16)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import attn_ref
+    x = t.reshape(-1, t.shape[-1]).numpy()
+    blocks = [r for r in np.array_split(np.arange(x.shape[0]), cpu_threads()) if len(r)]
+    with ThreadPoolExecutor(len(blocks)) as ex:
+        parts = list(ex.map(lambda r: attn_ref.quantize_rows(x[r[0]:r[-1] + 1], 64, bits),
+                            blocks))
+    cat = lambda j: np.concatenate([q[j] for q in parts]).reshape(*t.shape[:-1], -1)
+    return (torch.from_numpy(cat(0).view(np.int32)),
+            torch.from_numpy(cat(1).view(np.int16)).view(torch.bfloat16),
+            torch.from_numpy(cat(2).view(np.int16)).view(torch.bfloat16))
+
+
+class _PackedKV:
+    """The 8-bit (or bf16) KV cache as the reference's CPU path keeps it: preallocated packed
+    rows; an append quantizes the new rows into place, and a step attends over all rows
+    dequantized to bf16 (DequantKVCache without the fused Metal kernel, which the CPU backend
+    cannot run: laguna_mlx/cache.py:89-100). One buffer serves every layer (each layer costs
+    the same; the rows' values do not change the work)."""
+
+    def __init__(self, kv, rows, cap, Hkv, D):
+        from oracle import attn_ref, moe_ref
+        self.kv, self.offset = kv, rows
+        from lagunalab_b200 import synth
+        k, v = synth.kv_rows(0, cap, Hkv, D, seed=0, device="cpu")
+        if kv == "q8":
+            self.k = _oracle_quantize(k.float(), 8)
+            self.v = _oracle_quantize(v.float(), 8)
+        else:
+            self.k, self.v = k, v
+        self._attn_ref, self._moe_ref = attn_ref, moe_ref
+
+    def _rows(self, t, n):
+        if self.kv != "q8":
+            return t[:, :n].float()
+        q, s, b = t
+        return self._moe_ref.dequantize(q[:, :n], s[:, :n], b[:, :n], 64, 8).to(
+            torch.bfloat16).float()
+
+    def update(self, i, k, v):
+        T = k.shape[1]
+        n0 = self.offset
+        if self.kv == "q8":
+            for dst, x in ((self.k, k), (self.v, v)):
+                q, s_, b_ = _oracle_quantize(x.contiguous(), 8)
+                dst[0][:, n0:n0 + T], dst[1][:, n0:n0 + T], dst[2][:, n0:n0 + T] = q, s_, b_
+        else:
+            self.k[:, n0:n0 + T] = k.to(torch.bfloat16)
+            self.v[:, n0:n0 + T] = v.to(torch.bfloat16)
+        return self._rows(self.k, n0 + T), self._rows(self.v, n0 + T)
+
+
+def cpu_decode(wl, steps, warmup, budget_s=60.0):
+    """One greedy decode token of the workload's model through the oracle's restatement of the
+    reference's CPU path (laguna_mlx/laguna.py:75-206 with the KV cache of cache.py:89-100),
+    on the host cores, with weights built on the CPU (the counter-based generator and the
+    oracle's quantizer: the library is never loaded). A token runs all layers — the dense
+    layer 0, then the MoE layer weights for every one of the other layers (one MoE layer is
+    built and reused: each costs the same) — and the lm_head, at the workload's context over a
+    preallocated cache in the workload's KV format. As many whole tokens are timed as fit in
+    ``budget_s`` (at least one, at most ``steps``), after ``warmup`` untimed MoE layers."""
+    from oracle import model_ref
     from lagunalab_b200 import synth
     nt = cpu_threads()
     torch.set_num_threads(nt)
-    a = synth.decoder_args(vocab=wl["vocab"], hidden=wl["hidden"], layers=2, heads=wl["heads"],
-                           kv_heads=wl["kv_heads"], head_dim=wl["head_dim"],
+    a = synth.decoder_args(vocab=wl["vocab"], hidden=wl["hidden"], layers=wl["layers"],
+                           heads=wl["heads"], kv_heads=wl["kv_heads"], head_dim=wl["head_dim"],
                            experts=wl["experts"], top_k=wl["top_k"], moe_inter=wl["moe_inter"],
                            shared_inter=wl["shared_inter"], dense_inter=wl["dense_inter"],
                            rope_theta=wl["rope_theta"])
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    model = synth.decoder(a, seed=wl["seed"], device=dev)
-    W = synth.oracle_weights(model)
+    keep = ("model.embed_tokens", "model.norm", "lm_head", "model.layers.0.", "model.layers.1.")
+    items = synth.decoder_tensors(a, seed=wl["seed"], device="cpu",
+                                  want=lambda n: n.startswith(keep))
+    W = model_ref.weights_from_named(items, 2, _oracle_quantize)
+    W["layers"] = [W["layers"][0]] + [W["layers"][1]] * (a.num_hidden_layers - 1)
     oa = synth.oracle_args(a)
-    L = W["layers"][1]  # a MoE layer
     ctx = wl["prefill"]
-    g = torch.Generator().manual_seed(0)
-    kc = torch.randn(a.num_key_value_heads, ctx, a.head_dim, generator=g).to(torch.bfloat16).float()
-    vc = torch.randn(a.num_key_value_heads, ctx, a.head_dim, generator=g).to(torch.bfloat16).float()
-    x = torch.randn(1, a.hidden_size, generator=g).to(torch.bfloat16).float()
-    del model
-
-    class _C:  # a cache already holding ctx rows
-        offset = ctx
-        k = [None, kc]
-        v = [None, vc]
-
-        def update(self, i, k, v):
-            return torch.cat([self.k[i], k], 1), torch.cat([self.v[i], v], 1)
-
-    def layer():
-        hn = model_ref.rmsnorm(x, L["in_norm"], oa["eps"])
-        a_ = model_ref._attention(L, hn, _C(), 1, oa, ctx, model_ref._qlin)
-        h = (x + a_).to(torch.bfloat16).float()
-        m = L["mlp"][1]
-        y, _, _ = moe_ref.moe_block(model_ref.rmsnorm(h, L["post_norm"], oa["eps"]), m["gate"],
-                                    m["bias"], m["experts"], m["shared"], oa["k"],
-                                    oa["routed_scale"], oa["norm_topk_prob"])
-        return y
-
-    def head():
-        return moe_ref.qlinear(model_ref.rmsnorm(x, W["norm"], oa["eps"]), W["lm_head"])
-
-    for _ in range(warmup):
-        layer()
-    tl = []
-    for _ in range(steps):
+    cap = ctx + steps + warmup + 2
+    cache = _PackedKV(wl.get("kv", "bf16"), ctx, cap, a.num_key_value_heads, a.head_dim)
+    tok = [7]
+    one = dict(W, layers=W["layers"][1:2])
+    for _ in range(warmup):  # untimed: one MoE layer
+        model_ref.forward(one, oa, tok, cache)
+        cache.offset -= 1
+    times = []
+    t_all = time.perf_counter()
+    while len(times) < max(1, steps):
         t0 = time.perf_counter()
-        layer()
-        tl.append(time.perf_counter() - t0)
-    t0 = time.perf_counter()
-    head()
-    th = time.perf_counter() - t0
-    sec = wl["layers"] * statistics.median(tl) + th
+        logits = model_ref.forward(W, oa, tok, cache)
+        tok = [int(torch.argmax(logits[-1]))]
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    sec = statistics.median(times)
     return dict(value=1.0 / sec, unit="tokens/s", cores=nt, kind="port",
-                sample=f"1 MoE layer at {ctx} keys ({steps} timed) + the lm_head once, "
-                       f"scaled to {wl['layers']} layers (oracle restatement)")
+                sample=f"{len(times)} whole decode tokens timed ({a.num_hidden_layers} layers + "
+                       f"lm_head each; median) at context {ctx} with a {wl.get('kv', 'bf16')} "
+                       f"KV cache (oracle restatement of the reference's CPU path; one MoE "
+                       f"layer's weights serve all MoE layers and one cache serves all layers)")
 
 
 # ----------------------------------------------------------------------------------------
@@ -688,31 +714,35 @@ def main():
     wl = dict(WORKLOADS[args.workload])
     if args.layers and args.workload == "q8_decode":
         wl["L"] = args.layers
-    ws, rank, local = dist_setup()
-
     if args.impl == "reference":
-        if rank == 0:
-            if args.workload == "q8_decode":
-                ref = cpu_q8(wl, args.steps, args.warmup)
-            elif args.workload in DECODE_WORKLOADS:
-                ref = cpu_decode(wl, min(args.steps, 5), 1)
-            else:
-                ref = cpu_moe(wl, args.steps, args.warmup)
-            metric, unit = metric_unit(args.workload)
-            print(json.dumps({
-                "impl": "reference", "metric": metric, "value": ref["value"], "unit": unit,
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-                "config": config(args, wl, ws),
-                "cpu_baseline": {"value": ref["value"], "unit": unit, "cores": ref["cores"],
-                                 "kind": ref["kind"], "sample": ref["sample"]},
-                "e2e": {"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0},
-            }), flush=True)
-        finish(ws)
+        # the reference arm runs on rank 0's host cores alone: other ranks exit at once (no
+        # process group, nothing spinning on a core), and rank 0 never loads the library
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        if args.workload == "q8_decode":
+            ref = cpu_q8(wl, args.steps, args.warmup)
+        elif args.workload in DECODE_WORKLOADS:
+            ref = cpu_decode(wl, args.steps, 1)
+        else:
+            ref = cpu_moe(wl, args.steps, args.warmup)
+        metric, unit = metric_unit(args.workload)
+        print(json.dumps({
+            "impl": "reference", "metric": metric, "value": ref["value"], "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+            "config": config(args, wl, ws),
+            "cpu_baseline": {"value": ref["value"], "unit": unit, "cores": ref["cores"],
+                             "kind": ref["kind"], "sample": ref["sample"]},
+            "e2e": {"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
 
+    ws, rank, local = dist_setup()
+
     pk, pk_kind = peaks()
+    decode_info = None
     if args.workload in DECODE_WORKLOADS:
         r = run_decode(args, wl, ws, rank)
         value = ws * 1000.0 / r["ms"]  # every replica decodes one token per step
@@ -737,7 +767,7 @@ def main():
                                         f"step, top-k experts, {wl['kv']} K/V at mean context "
                                         f"{sum(r['ctx']) / 2:.0f})",
                          "duration": "graph step time (one replay per token)"}}
-        wl = dict(wl, prefill_ms=r["prefill_ms"], context=list(r["ctx"]))
+        decode_info = {"prefill_ms": r["prefill_ms"], "context": list(r["ctx"])}
         dtype = "bf16"
     elif args.workload == "q8_decode":
         r = run_q8(args, wl, ws, rank)
@@ -785,9 +815,11 @@ def main():
         "gpu_launches": r["launches"] * (ws if args.workload in DECODE_WORKLOADS else 1),
         "clocks": r["clocks"].result(),
     }
+    if decode_info:
+        line["decode"] = decode_info
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else
-              cpu_decode(wl, 3, 1) if args.workload in DECODE_WORKLOADS else cpu_moe(wl, 5, 1))
+              cpu_decode(wl, 2, 1, budget_s=45.0) if args.workload in DECODE_WORKLOADS else cpu_moe(wl, 5, 1))
         line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -208,9 +208,10 @@ int lg_q8_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
 /*
  * lg_q8_decode_attention_noalloc: no counterpart in the reference.  The same fused q8 decode
  * attention as lg_q8_decode_attention, for callers that cannot allocate device memory at the
- * moment they call (a plugin host that only hands over input and output pointers, code running
- * where CUDA forbids allocation calls such as a host function enqueued on a stream, or a
+ * moment they call (a plugin host that only hands over input and output pointers, or a
  * latency-critical path that cannot afford cudaMalloc's implicit device synchronisation).
+ * It issues a memset and a kernel launch on `stream`, so it must not be called from a stream
+ * callback (cudaLaunchHostFunc), where CUDA forbids every CUDA API call.
  * It allocates nothing: its scratch (split partials and completion counters) lives in a fixed
  * 1 MiB array inside this library, which every GPU that loads the library holds until the
  * process exits (lg_q8_decode_fixed_scratch_bytes() returns the size).  A call whose scratch

@@ -1,7 +1,8 @@
 // MoE block orchestration: routing plan -> expert products -> combine, behind the C ABI.
 //
-// lg_moe_experts:  laguna_mlx/laguna.py:147-150 after route(); SwitchGLU + weighted sum +
-//                  routed scale + shared expert, accumulated in fp32, one bf16 rounding.
+// lg_moe_experts:  laguna_mlx/laguna.py:147-150 after route(); SwitchGLU per pick, then the
+//                  weighted sum, routed scale and shared expert with the MLX graph's bf16
+//                  rounding points, summed in a fixed order (deterministic).
 // lg_switch_glu:   SwitchGLU(x, indices) per-pick outputs (mlx-lm switch_layers surface).
 // lg_qmlp:         dense quantized SwiGLU MLP (laguna.py:114-122): the shared-expert machinery
 //                  with no routed experts.
@@ -9,7 +10,7 @@
 
 namespace lg {
 
-int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cudaStream_t s);
+int launch_tc(const GemvArgs& a, int max_groups, void* tc_ws, cudaStream_t s);
 size_t tc_workspace_bytes(int T, int H, int I, int I_sh, int E, int k);
 bool tc_supported(int H, int I, int I_sh, int E);
 int tc_status(const void* tc_ws, int T, int H, int I, int I_sh, int E, int k, int* status);
@@ -20,7 +21,7 @@ struct MoeWs {
   int32_t* active;
   int32_t* perm;
   __nv_bfloat16* h;
-  float* out_acc;
+  __nv_bfloat16* yrows;  // [P + T, H] per-pick down outputs (combine mode)
   void* tc;
 };
 
@@ -34,26 +35,81 @@ static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh,
   t.active = c.take<int32_t>(E + 3);
   t.perm = c.take<int32_t>((size_t)P + T);
   t.h = c.take<__nv_bfloat16>(((size_t)P + T) * Imax);
-  t.out_acc = c.take<float>((size_t)T * H);
+  t.yrows = c.take<__nv_bfloat16>(((size_t)P + T) * H);
   t.tc = c.take<char>(tc_workspace_bytes(T, H, I, I_sh, E, k));
   if (w) *w = t;
   return align_up(c.used, 256);
 }
 
-__global__ void finalize_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out,
-                                     size_t n4) {
+__device__ __forceinline__ void bf16x8(uint4 v, float* f) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = __uint_as_float(u[j] << 16);
+    f[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+  }
+}
+
+// laguna.py:149-150 with the MLX graph's bf16 materialisation points: per pick
+// bf16(y * w), their fp32 sum in pick order rounded to bf16, times the routed scale (bf16),
+// plus the shared expert's row (bf16). One thread per 8 columns of a token; the order of
+// every sum is fixed, so the result does not depend on scheduling.
+__global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ y,
+                                    const int32_t* __restrict__ inds,
+                                    const __nv_bfloat16* __restrict__ w, int T, int k, int E,
+                                    int H, float scale, int has_shared,
+                                    __nv_bfloat16* __restrict__ out) {
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+  const int H8 = H / 8;
+  const size_t total = (size_t)T * H8, P = (size_t)T * k;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
-    float4 v = reinterpret_cast<const float4*>(acc)[i];
-    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t*>(&lo);
-    o.y = *reinterpret_cast<uint32_t*>(&hi);
-    reinterpret_cast<uint2*>(out)[i] = o;
+    const size_t t = i / H8;
+    const int c = (int)(i % H8) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const size_t p = t * k + j;
+      const int e = inds[p];
+      if (e < 0 || e >= E) continue;
+      const float wj = bf2f(w[p]);
+      float v[8];
+      bf16x8(*reinterpret_cast<const uint4*>(y + p * H + c), v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += round_bf16(v[q] * wj);
+    }
+    float sh[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (has_shared) bf16x8(*reinterpret_cast<const uint4*>(y + (P + t) * H + c), sh);
+    float r[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float s_ = round_bf16(round_bf16(acc[q]) * scale);
+      r[q] = has_shared ? s_ + sh[q] : s_;
+    }
+    uint4 o;
+    __nv_bfloat162 b0 = __floats2bfloat162_rn(r[0], r[1]), b1 = __floats2bfloat162_rn(r[2], r[3]);
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(r[4], r[5]), b3 = __floats2bfloat162_rn(r[6], r[7]);
+    o.x = *reinterpret_cast<uint32_t*>(&b0);
+    o.y = *reinterpret_cast<uint32_t*>(&b1);
+    o.z = *reinterpret_cast<uint32_t*>(&b2);
+    o.w = *reinterpret_cast<uint32_t*>(&b3);
+    *reinterpret_cast<uint4*>(out + t * H + c) = o;
   }
+}
+
+int launch_combine(const __nv_bfloat16* yrows, const int32_t* inds, const __nv_bfloat16* w,
+                   int T, int k, int E, int H, float routed_scale, int has_shared,
+                   __nv_bfloat16* out, cudaStream_t st) {
+  if (T <= 0) return LG_OK;
+  const size_t n = (size_t)T * (H / 8);
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  prof_begin("combine", st);
+  LG_CUDA_TRY(launch_k(combine_rows_kernel, dim3(blocks), dim3(256), 0, st, yrows, inds, w, T, k,
+                       E, H, routed_scale, has_shared, out));
+  prof_end("combine", st);
+  LG_LAUNCH_CHECK("combine_rows");
+  return LG_OK;
 }
 
 static int check_qmat(const void* q, const void* s, const void* b, const char* name) {
@@ -106,7 +162,6 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   carve_moe(workspace, T, H, Ie, E, k, I_sh, &w);
   const int P = T * (E > 0 ? k : 0);
   const bool with_sh = I_sh > 0;
-  if (mode == 0) LG_CUDA_TRY(cudaMemsetAsync(w.out_acc, 0, sizeof(float) * (size_t)T * H, st));
   if (mode == 1) LG_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(uint16_t) * (size_t)P * H, st));
   int rc = launch_plan(inds, T, E > 0 ? k : 0, E, with_sh ? 1 : 0, w.counts, w.offsets, w.perm,
                        w.active, st);
@@ -143,10 +198,9 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   a.sd_b = static_cast<const __nv_bfloat16*>(sb[2]);
   a.h = w.h;
   a.h_stride = Ie > I_sh ? Ie : I_sh;
-  a.w = static_cast<const __nv_bfloat16*>(weights);
-  a.routed_scale = routed_scale;
-  a.out_acc = w.out_acc;
-  a.ypick = static_cast<__nv_bfloat16*>(out);
+  // combine mode: every pick row and shared row goes to the workspace, then one fixed-order
+  // pass combines them; per-pick mode: the routed rows go straight to the caller's output
+  a.ypick = mode == 0 ? w.yrows : static_cast<__nv_bfloat16*>(out);
   int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
   // Tensor-core grouped GEMM when there are enough rows per expert to fill 128-row tiles;
   // the split-K GEMV otherwise (decode), or when the shapes do not tile.
@@ -154,21 +208,13 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   const bool use_tc = (path == LG_PATH_TENSOR) ||
                       (path == LG_PATH_AUTO && tiles_ok && P + (with_sh ? T : 0) > 512);
   if (use_tc)
-    rc = launch_tc(a, max_groups, mode == 0, w.tc, st);
+    rc = launch_tc(a, max_groups, w.tc, st);
   else
-    rc = launch_gemv(a, max_groups, mode == 0, st);
+    rc = launch_gemv(a, max_groups, st);
   if (rc) return rc;
-  if (mode == 0) {
-    size_t n4 = (size_t)T * H / 4;
-    int blocks = (int)((n4 + 255) / 256);
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    prof_begin("finalize", st);
-    LG_CUDA_TRY(launch_k(finalize_bf16_kernel, dim3(blocks), dim3(256), 0, st,
-                         static_cast<const float*>(w.out_acc), static_cast<__nv_bfloat16*>(out),
-                         n4));
-    prof_end("finalize", st);
-    LG_LAUNCH_CHECK("finalize_bf16");
-  }
+  if (mode == 0)
+    return launch_combine(w.yrows, inds, static_cast<const __nv_bfloat16*>(weights), T, a.k, E, H,
+                          routed_scale, with_sh ? 1 : 0, static_cast<__nv_bfloat16*>(out), st);
   return LG_OK;
 }
 

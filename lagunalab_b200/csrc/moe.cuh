@@ -20,14 +20,17 @@ struct GemvArgs {
   const __nv_bfloat16 *sg_s, *sg_b, *su_s, *su_b, *sd_s, *sd_b;
   __nv_bfloat16* h;        // [P + T, h_stride] intermediate (SwiGLU output), bf16
   int h_stride;
-  const __nv_bfloat16* w;  // [T, k] routing weights
-  float routed_scale;
-  float* out_acc;          // [T, H] fp32 combine accumulator (scatter mode)
-  __nv_bfloat16* ypick;    // [T, k, H] per-pick outputs (SwitchGLU mode)
+  __nv_bfloat16* ypick;    // [P (+ T with the shared expert), H] per-pick down outputs
 };
 
 int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32_t* counts,
                 int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s);
-int launch_gemv(const GemvArgs& a, int max_groups, bool scatter, cudaStream_t s);
+int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s);
+// out[t] = bf16(bf16(bf16(sum_j bf16(y[t*k+j] * w[t*k+j])) * scale) + y[P + t]) per token, the
+// picks summed in order j = 0..k-1 (picks whose expert id is outside [0, E) skipped), the shared
+// row added when has_shared.
+int launch_combine(const __nv_bfloat16* yrows, const int32_t* inds, const __nv_bfloat16* w,
+                   int T, int k, int E, int H, float routed_scale, int has_shared,
+                   __nv_bfloat16* out, cudaStream_t s);
 
 }  // namespace lg

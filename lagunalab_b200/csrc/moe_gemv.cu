@@ -16,10 +16,9 @@
 //   the bf16 rounding points of the MLX graph (laguna.py:122): g, u -> bf16; silu = g*sigmoid(g)
 //   with each op rounded to bf16; h = bf16(silu * u).
 // down kernel: one CTA = one 16-row tile of the hidden dimension for one expert group, split-K
-//   over 4 warps; the epilogue rounds y to bf16 (gather_qmm output) and either adds
-//   w * routed_scale * y into an fp32 [T, H] accumulator with red.global.add (the combine of
-//   laguna.py:149-150; the shared group adds with weight 1), or stores y per pick (the
-//   SwitchGLU call surface).
+//   over 4 warps; the epilogue rounds y to bf16 (gather_qmm output) and stores it per pick
+//   row (routed picks, then the shared expert's rows); the weighted combine of
+//   laguna.py:149-150 is a separate fixed-order pass over those rows.
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "moe.cuh"
@@ -126,7 +125,6 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
   }
 }
 
-template <bool SCATTER>
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a) {
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
@@ -190,13 +188,8 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
         const int n = (j < 2) ? ra : rb;
         if (col < cnt) {
           const int p = a.perm[row0 + col];
-          const float y = round_bf16(v);  // gather_qmm output is bf16
-          if (SCATTER) {
-            const float wt = (p < a.P) ? bf2f(a.w[p]) * a.routed_scale : 1.0f;
-            red_add_f32(a.out_acc + (size_t)row_token(p, a.P, a.k) * H + n, wt * y);
-          } else if (p < a.P) {
-            a.ypick[(size_t)p * H + n] = __float2bfloat16_rn(y);
-          }
+          // gather_qmm's bf16 output per pick row (shared rows follow the routed ones)
+          a.ypick[(size_t)p * H + n] = __float2bfloat16_rn(v);
         }
       }
     }
@@ -204,7 +197,7 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
   }
 }
 
-int launch_gemv(const GemvArgs& a, int max_groups, bool scatter, cudaStream_t s) {
+int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s) {
   if (max_groups <= 0) return LG_OK;
   const int Imax = a.I > a.I_sh ? a.I : a.I_sh;
   dim3 g1((Imax + 15) / 16, max_groups);
@@ -214,10 +207,7 @@ int launch_gemv(const GemvArgs& a, int max_groups, bool scatter, cudaStream_t s)
   LG_LAUNCH_CHECK("moe_gemv_gateup");
   dim3 g2((a.H + 15) / 16, max_groups);
   prof_begin("experts_down", s);
-  if (scatter)
-    LG_CUDA_TRY(launch_k(moe_gemv_down_kernel<true>, g2, dim3(GV_WARPS * 32), 0, s, a));
-  else
-    LG_CUDA_TRY(launch_k(moe_gemv_down_kernel<false>, g2, dim3(GV_WARPS * 32), 0, s, a));
+  LG_CUDA_TRY(launch_k(moe_gemv_down_kernel, g2, dim3(GV_WARPS * 32), 0, s, a));
   prof_end("experts_down", s);
   LG_LAUNCH_CHECK("moe_gemv_down");
   return LG_OK;

@@ -15,9 +15,9 @@
 //   warp 1      one thread issues tcgen05.mma (M 128, N 256, K 16, bf16 -> fp32) into one of
 //               two TMEM accumulators (2 x 256 columns) and commits stage / tile barriers
 //   warps 12-15 epilogue: tcgen05.ld of the accumulator; gate/up: SwiGLU with the MLX bf16
-//               rounding points (laguna.py:122) -> h; down: y -> bf16, times the routing weight
-//               and routed scale, red.global.add.v4.f32 into the fp32 [T, H] combine
-//               accumulator (laguna.py:149-150), or per-pick stores (SwitchGLU surface)
+//               rounding points (laguna.py:122) -> h; down: y -> bf16 stored per pick row
+//               (routed picks, then the shared expert's rows); the weighted combine
+//               (laguna.py:149-150) is a separate fixed-order pass over those rows
 // The two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next.
 //
 // K order: inside every aligned 8-wide K chunk the operands are stored in the order
@@ -71,11 +71,7 @@ struct TcArgs {
   const __nv_bfloat16 *s0, *b0, *s1, *b1, *ss0, *sb0, *ss1, *sb1;
   __nv_bfloat16* h;
   int h_stride;
-  const __nv_bfloat16* w;
-  float routed_scale;
-  float* out_acc;
-  __nv_bfloat16* ypick;
-  int scatter;
+  __nv_bfloat16* ypick;  // [rows, H] per-pick down outputs (pick id order)
   int* err;
 };
 
@@ -407,14 +403,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       } else {
-        int p = 0, tok = 0;
-        float wt = 0.f;
-        if (valid) {
-          p = a.perm[R];
-          tok = p < a.P ? p / a.k : p - a.P;
-          // routing weights exist only in combine mode (the per-pick surface passes none)
-          wt = (a.scatter && p < a.P) ? bf2f(a.w[p]) * a.routed_scale : 1.0f;
-        }
+        const int p = valid ? a.perm[R] : 0;
         const int n0 = nt * 256;
 #pragma unroll 1
         for (int c = 0; c < 256; c += 16) {
@@ -422,22 +411,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tmem_ld16(taddr + c, yv);
           tmem_ld_wait(yv);
           if (valid) {
+            // gather_qmm's bf16 output, stored per pick (shared rows after the P routed
+            // ones); the combine sums each token's rows in a fixed order afterwards
             float y[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) y[j] = round_bf16(__uint_as_float(yv[j]));
-            if (a.scatter) {
-              float* o = a.out_acc + (size_t)tok * H + n0 + c;
-#pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                red_add_v4_f32(o + j, wt * y[j], wt * y[j + 1], wt * y[j + 2], wt * y[j + 3]);
-            } else if (p < a.P) {
-              __nv_bfloat16* o = a.ypick + (size_t)p * H + n0 + c;
-              *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]),
-                                                        pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
-              *reinterpret_cast<uint4*>(o + 8) =
-                  make_uint4(pack_bf2(y[8], y[9]), pack_bf2(y[10], y[11]), pack_bf2(y[12], y[13]),
-                             pack_bf2(y[14], y[15]));
-            }
+            for (int j = 0; j < 16; ++j) y[j] = __uint_as_float(yv[j]);
+            __nv_bfloat16* o = a.ypick + (size_t)p * H + n0 + c;
+            *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]),
+                                                      pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
+            *reinterpret_cast<uint4*>(o + 8) =
+                make_uint4(pack_bf2(y[8], y[9]), pack_bf2(y[10], y[11]), pack_bf2(y[12], y[13]),
+                           pack_bf2(y[14], y[15]));
           }
         }
       }
@@ -603,7 +587,7 @@ static int sm_count() {
   return n;
 }
 
-int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cudaStream_t st) {
+int launch_tc(const GemvArgs& a, int max_groups, void* tc_ws, cudaStream_t st) {
   if (!tc_supported(a.H, a.I, a.I_sh, a.E))
     return fail(LG_ERR_UNSUPPORTED,
                 "tensor-core path needs hidden %% 256 == 0 and intermediate %% 128 == 0 "
@@ -671,11 +655,7 @@ int launch_tc(const GemvArgs& a, int max_groups, bool scatter, void* tc_ws, cuda
   t.I_sh = a.I_sh;
   t.h = a.h;
   t.h_stride = a.h_stride;
-  t.w = a.w;
-  t.routed_scale = a.routed_scale;
-  t.out_acc = a.out_acc;
   t.ypick = a.ypick;
-  t.scatter = scatter ? 1 : 0;
   t.err = w.counts + 2;
 
   const int grid_gu = (int)(gu < (size_t)sm_count() ? gu : (size_t)sm_count());

@@ -793,6 +793,7 @@ class DecodeGraph:
         self.cap = c0.q.keys[0].shape[2] if getattr(c0, "q", None) is not None else c0.keys.shape[2]
         self.steps = 0
         self._body()  # one real step, eagerly
+        self.first_logits = self.logits.clone()  # that step's logits (the capture reuses names)
         self.steps = 1
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
@@ -809,6 +810,8 @@ class DecodeGraph:
     def _body(self):
         logits = self.model.last_logits(self.tok.view(1, 1), self.cache, pos_dev=self.pos)
         ops.argmax(logits.view(1, -1), ids=self.tok, pos=self.pos, inc=1)
+        # the captured step's logits buffer (graph memory): valid after each replay
+        self.logits = logits.view(-1)
 
     def step(self):
         """One token (asynchronous); ``tok`` holds it afterwards."""

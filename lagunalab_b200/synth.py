@@ -1,8 +1,11 @@
 """Seeded synthetic inputs with the BASELINE shapes (no datasets or checkpoints are used).
 
-Weights are drawn N(0, std) on the GPU from a seeded generator and quantized to the MLX
-4-bit affine group-64 layout (bf16 scales/biases) by this library's quantizer; the same
-packed tensors feed the kernels and, in tests, the CPU oracle.
+MoE-block weights are drawn N(0, std) on the GPU from a seeded generator and quantized to
+the MLX 4-bit affine group-64 layout (bf16 scales/biases) by this library's quantizer; the
+same packed tensors feed the kernels and, in tests, the CPU oracle. Full decoders (BASELINE
+config 3) draw their weights from ``hash_normal``, a counter-based generator that gives the
+same bits on the CPU and the GPU, so a CPU checker can rebuild the exact model a GPU run
+used without copying 1.8 GB of packed weights.
 
 Skewed routing (Zipf(1.1) expert popularity): the router's selection-only
 bias ``e_score_correction_bias`` (laguna_mlx/laguna.py:133, :140) is set to
@@ -117,44 +120,178 @@ def decoder_args(vocab=100352, hidden=2048, layers=40, heads=32, kv_heads=4, hea
         mlp_only_layers=[0], moe_routed_scaling_factor=routed_scale, gating=gating)
 
 
-def decoder(args, seed=0, std=0.02, norm_noise=0.0, router_bias_std=0.0, device="cuda"):
-    """A random-init Laguna ``Model``: every linear and the embedding 4-bit g64, the router
-    8-bit g64 (laguna.py:236-238), bf16 norms (ones, plus ``norm_noise`` N(0,1) noise)."""
-    dev = torch.device(device)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(seed)
-    H, D = args.hidden_size, args.head_dim
-    ql = lambda shape, bits=4: laguna.QuantizedLinear(
-        *ops.quantize(_randn(shape, std, gen, dev), 64, bits), 64, bits)
-    qs = lambda shape: laguna.SwitchLinear(*ops.quantize(_randn(shape, std, gen, dev), 64, 4))
+_M32 = 0xFFFFFFFF
+# Irwin-Hall(4) over bytes: the sum of four uniform bytes has mean 510 and standard deviation
+# sqrt(4 * (256^2 - 1) / 12)
+_IH_MEAN = 510.0
+_IH_SD = (4 * (256 ** 2 - 1) / 12) ** 0.5
+
+
+def _mix32(x):
+    """A 32-bit integer hash (xor-shift / multiply rounds) on an int64 tensor holding values in
+    [0, 2^32). The multipliers are odd and below 2^31, so every product stays below 2^63 and
+    CPU and CUDA compute the same bits."""
+    x = x ^ (x >> 16)
+    x = (x * 0x7FEB352D) & _M32
+    x = x ^ (x >> 15)
+    x = (x * 0x2C1B3C6D) & _M32
+    return x ^ (x >> 16)
+
+
+def _mix32_int(v):
+    return int(_mix32(torch.tensor([v & _M32], dtype=torch.int64))[0])
+
+
+def hash_normal(shape, seed, stream, std=1.0, device="cuda", chunk=1 << 24):
+    """Seeded approximately-normal fp32 values (mean 0, standard deviation ``std``, |x| <=
+    3.45 std) that are bit-identical on the CPU and on the GPU: element i of (seed, stream) is
+    the Irwin-Hall sum of the four bytes of a two-round integer hash of i, centred and scaled
+    by one fp32 multiply. Used wherever a CPU checker must rebuild the exact weights or
+    inputs a GPU run used (torch's CPU and CUDA generators draw different numbers)."""
+    shape = tuple(int(d) for d in (shape if isinstance(shape, (tuple, list)) else (shape,)))
+    n = 1
+    for d in shape:
+        n *= d
+    if n >= 1 << 32:
+        raise ValueError("hash_normal: at most 2^32 values per stream")
+    k1 = _mix32_int(seed * 0x9E3779B1 + 0x632BE5AB)
+    k2 = _mix32_int(stream * 0x85EBCA77 + k1)
+    c = torch.tensor(std / _IH_SD, dtype=torch.float32, device=device)
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    for a in range(0, n, chunk):
+        b = min(n, a + chunk)
+        x = torch.arange(a, b, dtype=torch.int64, device=device)
+        x = _mix32(_mix32(x ^ k1) ^ k2)
+        s = (x & 255) + ((x >> 8) & 255) + ((x >> 16) & 255) + (x >> 24)
+        out[a:b] = (s.to(torch.float32) - _IH_MEAN) * c
+    return out.view(shape)
+
+
+def decoder_tensors(args, seed=0, std=0.02, norm_noise=0.0, router_bias_std=0.0, device="cuda",
+                    want=None):
+    """Every parameter of a random-init Laguna decoder, lazily, in one fixed order:
+    (MLX parameter name, kind, fp32 tensor) with kind "q4" (a linear, the embedding or a
+    stacked expert tensor, to be quantized 4-bit g64), "q8" (the router, 8-bit g64,
+    laguna.py:236-238), "norm" (an RMSNorm weight: ones, plus ``norm_noise`` noise) or "bias"
+    (the router's fp32 ``e_score_correction_bias``). Values come from ``hash_normal`` with one
+    stream per tensor, so a CPU checker rebuilds the GPU model bit for bit. ``want(name)``
+    (optional) selects the tensors to produce; the others are skipped without being drawn
+    (their streams are still consumed, so the selected ones keep their values)."""
+    for name, kind, make in _decoder_thunks(args, seed, std, norm_noise, router_bias_std,
+                                            device):
+        if want is None or want(name):
+            yield name, kind, make()
+
+
+def _decoder_thunks(args, seed, std, norm_noise, router_bias_std, device):
+    """(name, kind, thunk) per decoder parameter; each thunk owns its stream id."""
+    H, D, V = args.hidden_size, args.head_dim, args.vocab_size
+    stream = iter(range(1 << 30))
+
+    def normal(shape, s=std):
+        sid = next(stream)
+        return lambda: hash_normal(shape, seed, sid, s, device)
 
     def norm(n):
-        w = torch.ones(n, device=dev)
-        if norm_noise:
-            w = w + norm_noise * torch.randn(n, generator=gen, device=dev)
-        return laguna.RMSNorm(n, args.rms_norm_eps, w.to(torch.bfloat16))
+        sid = next(stream)
 
-    emb = ql((args.vocab_size, H))
-    embed = laguna.QuantizedEmbedding(emb.weight, emb.scales, emb.biases)
-    layers = []
+        def make():
+            w = torch.ones(n, dtype=torch.float32, device=device)
+            if norm_noise:
+                w = w + hash_normal(n, seed, sid, norm_noise, device)
+            return w
+        return make
+
+    yield "model.embed_tokens", "q4", normal((V, H))
     for i in range(args.num_hidden_layers):
+        p = f"model.layers.{i}"
         Hq, Hkv = args.num_attention_heads_per_layer[i], args.num_key_value_heads
         G = Hq if args.gating == "per-head" else Hq * D
-        attn = laguna.Attention(args, i, ql((Hq * D, H)), ql((Hkv * D, H)), ql((Hkv * D, H)),
-                                ql((H, Hq * D)), ql((G, H)), norm(D), norm(D))
+        for n, shape in (("q_proj", (Hq * D, H)), ("k_proj", (Hkv * D, H)),
+                         ("v_proj", (Hkv * D, H)), ("o_proj", (H, Hq * D)), ("g_proj", (G, H))):
+            yield f"{p}.self_attn.{n}", "q4", normal(shape)
+        yield f"{p}.self_attn.q_norm", "norm", norm(D)
+        yield f"{p}.self_attn.k_norm", "norm", norm(D)
         if i in args.mlp_only_layers:
             I = args.intermediate_size
-            mlp = laguna.MLP(H, I, ql((I, H)), ql((I, H)), ql((H, I)))
+            yield f"{p}.mlp.gate_proj", "q4", normal((I, H))
+            yield f"{p}.mlp.up_proj", "q4", normal((I, H))
+            yield f"{p}.mlp.down_proj", "q4", normal((H, I))
         else:
-            E, I, Ish = args.num_experts, args.moe_intermediate_size, args.shared_expert_intermediate_size
-            sw = laguna.SwitchGLU(H, I, E, qs((E, I, H)), qs((E, I, H)), qs((E, H, I)))
-            sh = laguna.MLP(H, Ish, ql((Ish, H)), ql((Ish, H)), ql((H, Ish))) if Ish else None
-            bias = (router_bias_std * torch.randn(E, generator=gen, device=dev)
-                    if router_bias_std else torch.zeros(E, device=dev))
-            mlp = laguna.SparseMoeBlock(args, ql((E, H), bits=8), bias, sw, sh)
-        layers.append(laguna.DecoderLayer(args, i, attn, mlp, norm(H), norm(H)))
-    model = laguna.LagunaModel(args, embed, layers, norm(H))
-    return laguna.Model(args, model, ql((args.vocab_size, H)))
+            E, I = args.num_experts, args.moe_intermediate_size
+            Ish = args.shared_expert_intermediate_size
+            yield f"{p}.mlp.switch_mlp.gate_proj", "q4", normal((E, I, H))
+            yield f"{p}.mlp.switch_mlp.up_proj", "q4", normal((E, I, H))
+            yield f"{p}.mlp.switch_mlp.down_proj", "q4", normal((E, H, I))
+            if Ish:
+                yield f"{p}.mlp.shared_expert.gate_proj", "q4", normal((Ish, H))
+                yield f"{p}.mlp.shared_expert.up_proj", "q4", normal((Ish, H))
+                yield f"{p}.mlp.shared_expert.down_proj", "q4", normal((H, Ish))
+            sid = next(stream)
+            bias = ((lambda sid=sid: hash_normal(E, seed, sid, router_bias_std, device))
+                    if router_bias_std
+                    else (lambda: torch.zeros(E, dtype=torch.float32, device=device)))
+            yield f"{p}.mlp.e_score_correction_bias", "bias", bias
+            yield f"{p}.mlp.gate", "q8", normal((E, H))
+        yield f"{p}.input_layernorm", "norm", norm(H)
+        yield f"{p}.post_attention_layernorm", "norm", norm(H)
+    yield "model.norm", "norm", norm(H)
+    yield "lm_head", "q4", normal((V, H))
+
+
+def decoder_quantization(args):
+    """The "quantization" config entry of these models: 4-bit g64, the routers 8-bit g64."""
+    q = {"group_size": 64, "bits": 4}
+    for i in range(args.num_hidden_layers):
+        if i not in args.mlp_only_layers:
+            q[f"model.layers.{i}.mlp.gate"] = {"group_size": 64, "bits": 8}
+    return q
+
+
+def decoder(args, seed=0, std=0.02, norm_noise=0.0, router_bias_std=0.0, device="cuda"):
+    """A random-init Laguna ``Model``: every linear and the embedding 4-bit g64, the router
+    8-bit g64 (laguna.py:236-238), bf16 norms; the tensors of ``decoder_tensors`` quantized on
+    the GPU by the library's quantizer (bit-exact with the CPU checker's) and loaded through
+    the MLX-name loader ``laguna.model_from_weights``."""
+    weights = {}
+    for name, kind, t in decoder_tensors(args, seed, std, norm_noise, router_bias_std, device):
+        if kind in ("q4", "q8"):
+            q, s, b = ops.quantize(t, 64, 4 if kind == "q4" else 8)
+            weights[name + ".weight"], weights[name + ".scales"], weights[name + ".biases"] = q, s, b
+        elif kind == "norm":
+            weights[name + ".weight"] = t.to(torch.bfloat16)
+        else:
+            weights[name] = t
+        del t
+    return laguna.model_from_weights(args, weights, decoder_quantization(args), device)
+
+
+KV_SEED_OFFSET = 7777
+
+
+def kv_rows(layer, n, Hkv=4, D=128, seed=0, device="cuda"):
+    """Synthetic K and V rows of one layer's cache, bf16 [Hkv, n, D] each: hash_normal N(0, 1)
+    values (streams 2 * layer and 2 * layer + 1 of ``seed + KV_SEED_OFFSET``), the same bits on
+    the CPU and the GPU. A decode that starts from such a cache state exercises attention at
+    a long context without a prefill of that length (the CPU checker cannot run one)."""
+    s = seed + KV_SEED_OFFSET
+    k = hash_normal((Hkv, n, D), s, 2 * layer, 1.0, device).to(torch.bfloat16)
+    v = hash_normal((Hkv, n, D), s, 2 * layer + 1, 1.0, device).to(torch.bfloat16)
+    return k, v
+
+
+def fill_q8_cache(cache, n, seed=0):
+    """Fill rows [0, n) of every layer of a ``make_quantized_cache`` list with ``kv_rows``
+    quantized 8-bit g64 by the library's quantizer, and set each layer's offset to n."""
+    for i, c in enumerate(cache):
+        qc = c.q
+        k, v = kv_rows(i, n, seed=seed)
+        Hkv, _, D = k.shape
+        qc.reserve(1, Hkv, D, n, k.device)
+        ops.quantize_into(k[None], qc.keys, 0, qc.group_size, qc.bits)
+        ops.quantize_into(v[None], qc.values, 0, qc.group_size, qc.bits)
+        qc.offset = n
+        del k, v
 
 
 def oracle_weights(model):
