@@ -190,8 +190,12 @@ def timed(step, K, stream, profile_stage=None):
 def run_moe(args, wl, ws, rank):
     from lagunalab_b200 import ep, synth
     T, E, k, H, I, I_sh = (wl[n] for n in ("T", "E", "k", "H", "I", "I_sh"))
-    if ws > 1:
-        blk, x, fwd = ep.bench_block(T, E, k, H, I, I_sh, wl["zipf"], wl["scale"], ws, rank)
+    if ws > 1:  # expert parallel over peer memory, T tokens per rank (weak scaling)
+        blk = ep.bench_block(E, k, H, I, I_sh, wl["zipf"], wl["scale"])
+        g = torch.Generator(device="cuda")
+        g.manual_seed(1000 + rank)
+        x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+        fwd = ep.PeerExpertParallel(blk, capacity=T)
     else:
         blk, x = synth.moe_block(T, E, k, H, I, I_sh, seed=0, zipf=wl["zipf"],
                                  routed_scaling_factor=wl["scale"])
@@ -234,6 +238,71 @@ def run_moe(args, wl, ws, rank):
     return dict(ms=ms, e2e_ms=e2e_ms, kernel_ms=gu_ms, launches=launches, clocks=clocks,
                 tokens=tokens, counts=counts, h2d=x.numel() * x.element_size(),
                 d2h=out.numel() * out.element_size())
+
+
+EP_PREFILL = dict(T=32768, E=128, k=8, H=2048, I=1024, I_sh=1024, zipf=True, scale=1.0)
+
+
+def run_ep_prefill(args, ws, rank):
+    """BASELINE config 5 prefill: one MoE layer over 32,768 tokens split evenly over the ranks
+    (strong scaling), 128 experts sharded E/N per GPU, Zipf router; the exchange is the
+    peer-memory path (lagunalab_b200/ep.py PeerExpertParallel). Rank 0 also times the one-GPU
+    block on all 32,768 tokens (the curve's baseline) and checks the gathered expert-parallel
+    outputs against it."""
+    import torch.distributed as dist
+    from lagunalab_b200 import ep
+    c = EP_PREFILL
+    Tr = c["T"] // ws
+    blk = ep.bench_block(c["E"], c["k"], c["H"], c["I"], c["I_sh"], c["zipf"], c["scale"])
+
+    def tokens(r):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(2000 + r)
+        return torch.randn(Tr, c["H"], generator=g, device="cuda").to(torch.bfloat16)
+
+    stream = torch.cuda.current_stream()
+    out = dict(tokens=c["T"], experts=c["E"], experts_per_gpu=c["E"] // ws, tokens_per_gpu=Tr,
+               n_gpus=ws)
+    outs = None
+    if ws > 1:
+        x = tokens(rank)
+        pe = ep.PeerExpertParallel(blk, capacity=Tr)
+        for _ in range(args.warmup):
+            pe(x)
+        torch.cuda.synchronize()
+        barrier(ws)
+        ms, _, launches = timed(lambda: pe(x), args.steps, stream)
+        ms = max_over_ranks(ms, ws)
+        y = pe(x)
+        torch.cuda.synchronize()
+        status = int(max_over_ranks(float(pe.status()), ws))
+        outs = [torch.empty_like(y) for _ in range(ws)]
+        dist.all_gather(outs, y)
+        pe.close()
+        out.update(ms_per_step=ms, tokens_per_s=c["T"] / (ms * 1e-3), status=status,
+                   gpu_launches_per_step=launches // max(1, args.steps),
+                   exchange="NVLink peer stores issued by the dispatch kernel and the expert "
+                            "down-product epilogue; epoch flags with bounded waits; no collective")
+    if rank == 0:
+        xa = torch.cat([tokens(r) for r in range(ws)])
+        for _ in range(args.warmup):
+            blk(xa)
+        torch.cuda.synchronize()
+        ms1, _, _ = timed(lambda: blk(xa), args.steps, stream)
+        out.update(one_gpu_ms=ms1, one_gpu_tokens_per_s=c["T"] / (ms1 * 1e-3))
+        if outs is not None:
+            ref = blk(xa).float()
+            got = torch.cat(outs).float()
+            out.update(speedup=ms1 / out["ms_per_step"],
+                       efficiency=ms1 / (out["ms_per_step"] * ws),
+                       identical_to_one_gpu=bool(torch.equal(got, ref)),
+                       max_rel_err=float((got - ref).abs().max() / ref.abs().max()),
+                       cosine=float(torch.nn.functional.cosine_similarity(
+                           got.reshape(-1), ref.reshape(-1), dim=0)))
+    del blk
+    torch.cuda.empty_cache()
+    barrier(ws)
+    return out
 
 
 def capture(fn, profile_stage=None):
@@ -706,6 +775,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="decode_q8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the config-5 expert-parallel prefill measurement")
     ap.add_argument("--layers", type=int, default=None,
                     help="q8_decode only: layers per step (default: the config's 40; fewer "
                          "for small profiling runs)")
@@ -817,6 +888,8 @@ def main():
     }
     if decode_info:
         line["decode"] = decode_info
+    if not args.no_ep:
+        line["ep_prefill"] = run_ep_prefill(args, ws, rank)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else
               cpu_decode(wl, 2, 1, budget_s=45.0) if args.workload in DECODE_WORKLOADS else cpu_moe(wl, 5, 1))

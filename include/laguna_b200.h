@@ -439,6 +439,52 @@ int lg_q8_decode_attention_dev(const void* q, int B, int Hq, int Hkv, int D, con
  */
 int lg_decode_status(unsigned long long check[4], int reset);
 
+/* ---------------------------------------------------------------------------------------
+ * Expert parallelism over the GPUs of one node (no counterpart in the reference, which runs
+ * on one device; BASELINE config 5 defines the sharding). W <= 8 ranks, one process per GPU;
+ * rank r owns experts [r*E/W, (r+1)*E/W). Each rank allocates an arena of
+ * lg_ep_arena_bytes(W, Tr, k, H) zeroed device bytes (Tr: the most tokens a rank routes in
+ * one forward, the same on every rank), exports it with lg_ep_ipc_handle, maps every peer's
+ * with lg_ep_ipc_open, and passes the W arena pointers (its own at index r) to every call.
+ * A forward is, on every rank with the same epoch (1, 2, ... one per forward):
+ *   lg_router_topk -> lg_ep_dispatch -> lg_qmlp (shared expert, into the arena's shared rows,
+ *   lg_ep_arena_offsets) -> lg_ep_experts -> lg_ep_combine.
+ * The exchanges are peer stores issued by the kernels over NVLink (plain peer pointers); ranks
+ * synchronise through epoch flags in the arenas with waits bounded by timeout_s (<= 0: 2 s).
+ * An expired wait records (code | source << 8) in the arena's status word (lg_ep_status;
+ * code 1: dispatch, 2: combine) and the forward completes with NaN outputs instead of
+ * hanging. The output equals the one-GPU lg_moe_experts of the same tokens bit for bit.
+ * --------------------------------------------------------------------------------------- */
+size_t lg_ep_arena_bytes(int W, int Tr, int k, int H);
+int lg_ep_arena_offsets(int W, int Tr, int k, int H, size_t* shared_rows, size_t* combine_rows);
+size_t lg_ep_ipc_handle_bytes(void);
+/* handle: lg_ep_ipc_handle_bytes() bytes; offset: ptr minus the start of its allocation. */
+int lg_ep_ipc_handle(const void* ptr, void* handle, size_t* offset);
+/* Maps a peer's allocation; *ptr = its start + offset, *base is what lg_ep_ipc_close takes. */
+int lg_ep_ipc_open(const void* handle, size_t offset, void** ptr, void** base);
+int lg_ep_ipc_close(void* base);
+/* Sends this rank's T <= Tr tokens (x bf16 [T, H], inds int32 [T, k], weights bf16 [T, k]) to
+ * the owners of their picks: two launches on `stream`. */
+int lg_ep_dispatch(const void* x, const int32_t* inds, const void* weights, int T, int Tr,
+                   int H, int k, int E, int W, int rank, void* const* arenas, unsigned epoch,
+                   void* stream);
+size_t lg_ep_experts_workspace_bytes(int W, int Tr, int H, int I, int El, int k);
+/* Waits for every source's dispatch, runs this rank's El experts (MLX 4-bit g64 weights
+ * [El, I, H/8] / [El, H, I/8] with bf16 scales and biases) over the received rows and stores
+ * every pick's bf16(bf16(y) * w) into its source's arena; then flags every source. */
+int lg_ep_experts(int W, int Tr, int H, int I, int El, int k, const uint32_t* gate_q,
+                  const void* gate_s, const void* gate_b, const uint32_t* up_q, const void* up_s,
+                  const void* up_b, const uint32_t* down_q, const void* down_s,
+                  const void* down_b, int rank, void* const* arenas, unsigned epoch,
+                  double timeout_s, int path, void* workspace, size_t workspace_bytes,
+                  void* stream);
+/* Waits for every owner's rows, then out[t] = bf16(bf16(bf16(sum_j rows) * scale) + shared). */
+int lg_ep_combine(const int32_t* inds, int T, int Tr, int H, int k, int E, float routed_scale,
+                  int has_shared, int W, int rank, void* const* arenas, unsigned epoch,
+                  double timeout_s, void* out, void* stream);
+/* Status word of an arena (0 = ok). Synchronous; reset != 0 clears it. */
+int lg_ep_status(const void* arena, int reset, int* status);
+
 #ifdef __cplusplus
 }
 #endif

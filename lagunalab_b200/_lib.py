@@ -67,6 +67,19 @@ SIGNATURES = {
                                 P, I, P, P]),
     "lg_q8_decode_attention_dev": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, P, I, c_float,
                                            P, P, P, c_size_t, P]),
+    "lg_ep_arena_bytes": (c_size_t, [I, I, I, I]),
+    "lg_ep_arena_offsets": (c_int, [I, I, I, I, P, P]),
+    "lg_ep_ipc_handle_bytes": (c_size_t, []),
+    "lg_ep_ipc_handle": (c_int, [P, P, P]),
+    "lg_ep_ipc_open": (c_int, [P, c_size_t, P, P]),
+    "lg_ep_ipc_close": (c_int, [P]),
+    "lg_ep_dispatch": (c_int, [P, P, P, I, I, I, I, I, I, I, P, ctypes.c_uint, P]),
+    "lg_ep_experts_workspace_bytes": (c_size_t, [I, I, I, I, I, I]),
+    "lg_ep_experts": (c_int, [I, I, I, I, I, I, P, P, P, P, P, P, P, P, P, I, P, ctypes.c_uint,
+                              ctypes.c_double, I, P, c_size_t, P]),
+    "lg_ep_combine": (c_int, [P, I, I, I, I, I, c_float, I, I, I, P, ctypes.c_uint,
+                              ctypes.c_double, P, P]),
+    "lg_ep_status": (c_int, [P, I, P]),
     "lg_moe_decode": (c_int, [P, P, P, I, I, I, I, c_float, P, P, P, P, P, P, P, P, P, I,
                               P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
 }

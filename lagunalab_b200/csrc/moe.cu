@@ -25,7 +25,8 @@ struct MoeWs {
   void* tc;
 };
 
-static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh, MoeWs* w) {
+static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh, MoeWs* w,
+                        bool with_yrows = true) {
   Carver c(base);
   const int P = T * k;
   const int Imax = I > I_sh ? I : I_sh;
@@ -35,7 +36,7 @@ static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh,
   t.active = c.take<int32_t>(E + 3);
   t.perm = c.take<int32_t>((size_t)P + T);
   t.h = c.take<__nv_bfloat16>(((size_t)P + T) * Imax);
-  t.yrows = c.take<__nv_bfloat16>(((size_t)P + T) * H);
+  t.yrows = c.take<__nv_bfloat16>(with_yrows ? ((size_t)P + T) * H : 0);
   t.tc = c.take<char>(tc_workspace_bytes(T, H, I, I_sh, E, k));
   if (w) *w = t;
   return align_up(c.used, 256);
@@ -125,7 +126,8 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
                    const void* const* sc, const void* const* bi, int I_sh,
                    const uint32_t* const* sq, const void* const* ss, const void* const* sb,
                    int group_size, int bits, int path, void* out, void* workspace,
-                   size_t workspace_bytes, int mode, cudaStream_t st) {
+                   size_t workspace_bytes, int mode, cudaStream_t st,
+                   const EpRet* ep = nullptr) {
   LG_CHECK_ARG(bits == 4 && group_size == 64,
                "experts: only 4-bit group-64 weights are supported (got bits=%d group=%d)", bits,
                group_size);
@@ -137,8 +139,10 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
                "experts: hidden %d and intermediate %d/%d must be multiples of 64", H, I, I_sh);
   LG_CHECK_ARG(path >= LG_PATH_AUTO && path <= LG_PATH_TENSOR, "experts: path %d", path);
   if (T == 0) return LG_OK;
-  LG_CHECK_ARG(x && out && aligned(x, 16) && aligned(out, 16),
-               "experts: x/out must be non-NULL and 16-byte aligned");
+  LG_CHECK_ARG(mode == 2 ? (ep != nullptr) : (out != nullptr && aligned(out, 16)),
+               "experts: NULL or misaligned output");
+  LG_CHECK_ARG(x && aligned(x, 16),
+               "experts: x must be non-NULL and 16-byte aligned");
   if (E > 0) {
     LG_CHECK_ARG(inds != nullptr, "experts: NULL inds");
     LG_CHECK_ARG(mode == 1 || weights != nullptr, "experts: NULL routing weights");
@@ -153,13 +157,13 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
       if (rc) return rc;
     }
   const int Ie = E > 0 ? I : 0;
-  const size_t need = carve_moe(nullptr, T, H, Ie, E, k, I_sh, nullptr);
+  const size_t need = carve_moe(nullptr, T, H, Ie, E, k, I_sh, nullptr, mode == 0);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(LG_ERR_WORKSPACE, "experts: workspace %zu bytes at %p, need %zu (256-aligned)",
                 workspace_bytes, workspace, need);
   if (T == 0) return LG_OK;
   MoeWs w;
-  carve_moe(workspace, T, H, Ie, E, k, I_sh, &w);
+  carve_moe(workspace, T, H, Ie, E, k, I_sh, &w, mode == 0);
   const int P = T * (E > 0 ? k : 0);
   const bool with_sh = I_sh > 0;
   if (mode == 1) LG_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(uint16_t) * (size_t)P * H, st));
@@ -201,6 +205,8 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   // combine mode: every pick row and shared row goes to the workspace, then one fixed-order
   // pass combines them; per-pick mode: the routed rows go straight to the caller's output
   a.ypick = mode == 0 ? w.yrows : static_cast<__nv_bfloat16*>(out);
+  a.ep = {};
+  if (mode == 2) a.ep = *ep;  // expert parallel: down outputs go to the source ranks
   int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
   // Tensor-core grouped GEMM when there are enough rows per expert to fill 128-row tiles;
   // the split-K GEMV otherwise (decode), or when the shapes do not tile.
@@ -216,6 +222,21 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
     return launch_combine(w.yrows, inds, static_cast<const __nv_bfloat16*>(weights), T, a.k, E, H,
                           routed_scale, with_sh ? 1 : 0, static_cast<__nv_bfloat16*>(out), st);
   return LG_OK;
+}
+
+// Expert products of received rows whose down outputs go back to their source ranks (ep.cu).
+int moe_experts_ep(const void* x, int T, int H, int I, int E, int k, const int32_t* inds,
+                   const void* weights, const uint32_t* const* q, const void* const* sc,
+                   const void* const* bi, int path, void* workspace, size_t workspace_bytes,
+                   const EpRet& ep, cudaStream_t st) {
+  const uint32_t* nq[3] = {nullptr, nullptr, nullptr};
+  const void* nv[3] = {nullptr, nullptr, nullptr};
+  return moe_run(x, T, H, I, E, k, inds, weights, 1.0f, q, sc, bi, 0, nq, nv, nv, 64, 4, path,
+                 nullptr, workspace, workspace_bytes, 2, st, &ep);
+}
+
+size_t moe_ep_workspace_bytes(int T, int H, int I, int E, int k) {
+  return carve_moe(nullptr, T, H, I, E, k, 0, nullptr, false);
 }
 
 }  // namespace lg

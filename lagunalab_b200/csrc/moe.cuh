@@ -5,6 +5,24 @@
 
 namespace lg {
 
+// Expert-parallel return of the down products (ep.cu): a routed pick p = row * k + j of a
+// received row writes bf16(bf16(y) * w[p]) into the combine rows of the source rank that sent
+// the row, ret[row / Tr] + (tok[row] * k + j) * H (peer memory), instead of a local buffer.
+struct EpRet {
+  __nv_bfloat16* ret[8];
+  const int32_t* tok;
+  const __nv_bfloat16* w;
+  int Tr;
+  int on;
+};
+
+__device__ __forceinline__ __nv_bfloat16* ep_ret_row(const EpRet& ep, int p, int k, int H,
+                                                     float* wt) {
+  const int row = p / k, j = p - row * k;
+  *wt = __bfloat162float(ep.w[p]);
+  return ep.ret[row / ep.Tr] + ((size_t)ep.tok[row] * k + j) * H;
+}
+
 // Arguments of the expert-product kernels.  Group g < E is routed expert g; group E (when
 // present) is the shared expert.  Rows of group g are [offsets[g], offsets[g+1]) in the
 // expert-contiguous order; perm[row] is the pick id (routed: t*k + j, shared: P + t).
@@ -21,6 +39,7 @@ struct GemvArgs {
   __nv_bfloat16* h;        // [P + T, h_stride] intermediate (SwiGLU output), bf16
   int h_stride;
   __nv_bfloat16* ypick;    // [P (+ T with the shared expert), H] per-pick down outputs
+  EpRet ep;                // expert-parallel return (ep.on), replacing ypick
 };
 
 int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32_t* counts,
@@ -29,6 +48,11 @@ int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s);
 // out[t] = bf16(bf16(bf16(sum_j bf16(y[t*k+j] * w[t*k+j])) * scale) + y[P + t]) per token, the
 // picks summed in order j = 0..k-1 (picks whose expert id is outside [0, E) skipped), the shared
 // row added when has_shared.
+int moe_experts_ep(const void* x, int T, int H, int I, int E, int k, const int32_t* inds,
+                   const void* weights, const uint32_t* const* q, const void* const* sc,
+                   const void* const* bi, int path, void* workspace, size_t workspace_bytes,
+                   const EpRet& ep, cudaStream_t st);
+size_t moe_ep_workspace_bytes(int T, int H, int I, int E, int k);
 int launch_combine(const __nv_bfloat16* yrows, const int32_t* inds, const __nv_bfloat16* w,
                    int T, int k, int E, int H, float routed_scale, int has_shared,
                    __nv_bfloat16* out, cudaStream_t s);

@@ -188,13 +188,21 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
         const int n = (j < 2) ? ra : rb;
         if (col < cnt) {
           const int p = a.perm[row0 + col];
-          // gather_qmm's bf16 output per pick row (shared rows follow the routed ones)
-          a.ypick[(size_t)p * H + n] = __float2bfloat16_rn(v);
+          // gather_qmm's bf16 output per pick row (shared rows follow the routed ones), or
+          // (expert parallel) weighted into the source rank's combine row
+          if (a.ep.on) {
+            float wt;
+            __nv_bfloat16* orow = ep_ret_row(a.ep, p, a.k, H, &wt);
+            orow[n] = __float2bfloat16_rn(round_bf16(v) * wt);
+          } else {
+            a.ypick[(size_t)p * H + n] = __float2bfloat16_rn(v);
+          }
         }
       }
     }
     __syncthreads();
   }
+  if (a.ep.on) __threadfence_system();  // peer stores visible before the signal
 }
 
 int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s) {

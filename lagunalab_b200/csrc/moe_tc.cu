@@ -72,6 +72,7 @@ struct TcArgs {
   __nv_bfloat16* h;
   int h_stride;
   __nv_bfloat16* ypick;  // [rows, H] per-pick down outputs (pick id order)
+  EpRet ep;              // expert-parallel return of the down outputs (replaces ypick)
   int* err;
 };
 
@@ -405,6 +406,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       } else {
         const int p = valid ? a.perm[R] : 0;
         const int n0 = nt * 256;
+        // destination row: local per-pick rows, or (expert parallel) the source rank's
+        // combine row with the routing weight applied
+        __nv_bfloat16* orow = a.ypick + (size_t)p * H;
+        float wt = 1.0f;
+        if (valid && a.ep.on) orow = ep_ret_row(a.ep, p, a.k, H, &wt);
 #pragma unroll 1
         for (int c = 0; c < 256; c += 16) {
           uint32_t yv[16];
@@ -416,7 +422,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             float y[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = __uint_as_float(yv[j]);
-            __nv_bfloat16* o = a.ypick + (size_t)p * H + n0 + c;
+            if (a.ep.on) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) y[j] = round_bf16(y[j]) * wt;
+            }
+            __nv_bfloat16* o = orow + n0 + c;
             *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]),
                                                       pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
             *reinterpret_cast<uint4*>(o + 8) =
@@ -434,6 +444,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 
   // ---------------- teardown: every MMA retired before TMEM is released ----------------
+  if (!GATEUP && a.ep.on) __threadfence_system();  // peer stores visible before the signal
   __syncthreads();
 #ifdef LG_TC_PROFILE
   if (threadIdx.x == 0 && g_tc_stats) g_tc_stats[(GATEUP ? 0 : 4096) + blockIdx.x * 16 + 9] = clock64();
@@ -656,6 +667,7 @@ int launch_tc(const GemvArgs& a, int max_groups, void* tc_ws, cudaStream_t st) {
   t.h = a.h;
   t.h_stride = a.h_stride;
   t.ypick = a.ypick;
+  t.ep = a.ep;
   t.err = w.counts + 2;
 
   const int grid_gu = (int)(gu < (size_t)sm_count() ? gu : (size_t)sm_count());

@@ -1,86 +1,117 @@
-"""Expert parallelism for the MoE block over torch.distributed (NCCL on B200, gloo in tests).
+"""Expert parallelism for the MoE block over the GPUs of one node (the
+reference runs on one device and has no counterpart).
 
-Rank r of W owns the contiguous experts [r*E/W, (r+1)*E/W); router and shared expert are
-replicated and every rank routes its own tokens. One forward:
+Rank r of W owns the contiguous experts [r*E/W, (r+1)*E/W); the router and the shared expert
+are replicated and every rank routes its own tokens. One forward, on every rank alike:
 
-1. route locally (the fused router kernel): inds [T, k], w [T, k];
-2. order the T*k picks by destination rank (stable, so picks keep token order inside a
-   destination), exchange per-destination counts (all-to-all of W ints);
-3. dispatch: all-to-all of the picked token rows (bf16 [*, H]) and their local expert ids;
-4. local experts: SwitchGLU over the received rows (k = 1 per row, the grouped kernels);
-5. combine: all-to-all of the expert outputs back to the source rank, un-permute, then
-   out = sum_k w * y * routed_scale + shared(x).
+1. route locally (the router kernel): inds [T, k], w [T, k];
+2. dispatch: each token with at least one pick owned by rank d is sent to d once, into slot
+   s of d's receive rows for this source (slots in token order), with its k expert ids local
+   to d (-1 for picks owned elsewhere), its k routing weights and its token index;
+3. the owner runs its experts over the received rows (the grouped kernels) and returns, for
+   every pick, bf16(bf16(y) * w) into the source's combine row (token * k + j);
+4. combine at the source in pick order: bf16(bf16(bf16(sum_j rows) * scale) + shared(x)),
+   the arithmetic of the one-GPU block, so the outputs are bit-identical to it.
 
-Every rank takes the same collective steps in the same order. The compute steps are
-injectable (``route_fn``, ``expert_fn``, ``shared_fn``) so the control flow can be tested on
-CPU ranks with the oracle.
+``PeerExpertParallel`` is the B200 path: the exchanges are NVLink peer stores from inside the
+kernels (``csrc/ep.cu``) into per-rank arenas mapped with CUDA IPC, synchronised by epoch flags
+with bounded waits; no host synchronisation and no collective in the data path.
+``CollectiveExpertParallel`` runs the same data flow with fixed-capacity torch all-to-alls
+(``capacity`` rows per rank pair, so no host read of counts) and injectable compute, so the
+control flow is tested on gloo CPU ranks with the oracle's arithmetic.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 
-class ExpertParallelMoE:
+def _bf(t):
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def plan_slots(inds, El, W):
+    """Per (token, destination): the token's slot in that destination's receive rows, or -1
+    when none of its picks is owned there (slots in token order). inds [T, k] -> [T, W]."""
+    owner = torch.where(inds >= 0, torch.div(inds, El, rounding_mode="floor"), -1)
+    has = torch.stack([(owner == d).any(-1) for d in range(W)], dim=-1)  # [T, W]
+    slot = torch.cumsum(has.to(torch.int64), 0) - 1
+    return torch.where(has, slot, torch.full_like(slot, -1))
+
+
+class CollectiveExpertParallel:
+    """The expert-parallel data flow with fixed-capacity torch all-to-alls (gloo or NCCL).
+
+    ``route_fn(x) -> (inds [T, k], w [T, k])``; ``expert_fn(rows [R, H], lid [R, k]) -> y
+    [R, k, H]`` (the local experts' per-pick outputs, ignored where lid < 0); ``shared_fn(x)
+    -> [T, H]``. ``capacity`` bounds the tokens per rank and forward (the same on all ranks)."""
+
     def __init__(self, E, k, routed_scaling_factor, route_fn, expert_fn, shared_fn=None,
-                 group=None):
+                 capacity=4096, group=None):
         self.group = group
         self.W = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if E % self.W:
             raise ValueError(f"{E} experts do not split evenly over {self.W} ranks")
-        self.E, self.k, self.El = E, k, E // self.W
+        self.E, self.k, self.El, self.cap = E, k, E // self.W, capacity
         self.scale = routed_scaling_factor
         self.route_fn, self.expert_fn, self.shared_fn = route_fn, expert_fn, shared_fn
 
-    def dispatch(self, x, inds):
-        """Returns (recv_rows, recv_local_ids, order, send_counts, recv_counts)."""
-        T, k = inds.shape
-        flat = inds.reshape(-1).to(torch.int64)
-        dest = torch.div(flat, self.El, rounding_mode="floor")
-        order = torch.sort(dest, stable=True).indices
-        send_counts = torch.bincount(dest, minlength=self.W).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-        rows = x[torch.div(order, k, rounding_mode="floor")].contiguous()
-        lid = (flat[order] - dest[order] * self.El).to(torch.int32).contiguous()
-        recv_rows = rows.new_empty((sum(rc), x.shape[-1]))
-        recv_lid = lid.new_empty((sum(rc),))
-        dist.all_to_all_single(recv_rows, rows, rc, sc, group=self.group)
-        dist.all_to_all_single(recv_lid, lid, rc, sc, group=self.group)
-        return recv_rows, recv_lid, order, sc, rc
-
-    def combine(self, y_recv, order, sc, rc, shape):
-        """Send expert outputs back and restore pick order -> [T, k, H]."""
-        T, k, H = shape
-        y_back = y_recv.new_empty((sum(sc), H))
-        dist.all_to_all_single(y_back, y_recv.contiguous(), sc, rc, group=self.group)
-        y = torch.empty_like(y_back)
-        y[order] = y_back
-        return y.view(T, k, H)
+    def _a2a(self, t):
+        out = torch.empty_like(t)
+        dist.all_to_all_single(out, t.contiguous(), group=self.group)
+        return out
 
     def __call__(self, x):
-        lead = x.shape[:-1]
-        H = x.shape[-1]
+        lead, H = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, H)
+        T, W, k, El, cap = x2.shape[0], self.W, self.k, self.El, self.cap
+        if T > cap:
+            raise ValueError(f"{T} tokens exceed the capacity {cap}")
         inds, w = self.route_fn(x2)
-        inds = inds.reshape(-1, self.k)
-        w = w.reshape(-1, self.k)
-        recv_rows, recv_lid, order, sc, rc = self.dispatch(x2, inds)
-        # expert outputs travel in the input's dtype on every rank (a rank that received no
-        # rows must post a combine exchange of the same element size as the others)
-        if recv_rows.shape[0]:
-            y_recv = self.expert_fn(recv_rows, recv_lid).to(x2.dtype)
-        else:
-            y_recv = recv_rows.new_empty((0, H))
-        y = self.combine(y_recv, order, sc, rc, (x2.shape[0], self.k, H))
-        out = (y.float() * w.float().unsqueeze(-1)).sum(1) * self.scale
+        inds = inds.reshape(T, k).to(torch.int64)
+        w = w.reshape(T, k)
+        slot = plan_slots(inds, El, W)
+        # send buffers: [W destinations, cap slots, ...]
+        sx = x2.new_zeros((W, cap, H))
+        slid = torch.full((W, cap, k), -1, dtype=torch.int64)
+        sw = torch.zeros((W, cap, k), dtype=w.dtype)
+        stok = torch.zeros((W, cap), dtype=torch.int64)
+        count = torch.zeros(W, dtype=torch.int64)
+        for d in range(W):
+            t = (slot[:, d] >= 0).nonzero().squeeze(-1)
+            s = slot[t, d]
+            sx[d, s] = x2[t]
+            mine = (inds[t] >= d * El) & (inds[t] < (d + 1) * El)
+            slid[d, s] = torch.where(mine, inds[t] - d * El, torch.full_like(inds[t], -1))
+            sw[d, s] = w[t]
+            stok[d, s] = t
+            count[d] = t.numel()
+        rx, rlid, rw, rtok, rcount = (self._a2a(b) for b in (sx, slid, sw, stok, count))
+        live = torch.arange(cap)[None, :] < rcount[:, None]  # [W sources, cap]
+        rlid = torch.where(live[..., None], rlid, torch.full_like(rlid, -1))
+        y = self.expert_fn(rx.reshape(W * cap, H), rlid.reshape(W * cap, k))
+        y = y.reshape(W, cap, k, H).to(torch.float32)
+        term = _bf(_bf(y) * rw.to(torch.float32)[..., None])
+        # return: for each source, its combine rows [cap tokens, k picks, H]
+        back = torch.zeros((W, cap, k, H), dtype=torch.float32)
+        ok = rlid >= 0
+        for s in range(W):
+            tt, jj = ok[s].nonzero(as_tuple=True)
+            if tt.numel():
+                back[s, rtok[s, tt], jj] = term[s, tt, jj]
+        got = self._a2a(back)  # got[d] = the rows owner d computed for this rank's picks
+        owner = torch.div(inds, El, rounding_mode="floor")  # [T, k]
+        rows = got[owner, torch.arange(T)[:, None], torch.arange(k)[None, :]]  # [T, k, H]
+        acc = rows.sum(dim=1) if k else x2.new_zeros((T, H), dtype=torch.float32)
+        out = _bf(_bf(acc) * float(self.scale))
         if self.shared_fn is not None:
-            out = out + self.shared_fn(x2).float()
+            out = _bf(out + self.shared_fn(x2).to(torch.float32))
         return out.to(x.dtype).reshape(*lead, H)
 
 
 def local_switch_glu(sw, lo, hi):
-    """A SwitchGLU view holding experts [lo, hi) of ``sw`` (copied contiguous)."""
+    """A SwitchGLU holding experts [lo, hi) of ``sw`` (copied contiguous)."""
     from .laguna import SwitchGLU, SwitchLinear
 
     def cut(p):
@@ -91,30 +122,129 @@ def local_switch_glu(sw, lo, hi):
                      cut(sw.up_proj), cut(sw.down_proj))
 
 
-def from_block(blk, group=None):
-    """Expert-parallel forward for a SparseMoeBlock: this rank keeps its expert slice."""
-    W = dist.get_world_size(group)
-    r = dist.get_rank(group)
-    El = blk.num_experts // W
-    local = local_switch_glu(blk.switch_mlp, r * El, (r + 1) * El)
+class PeerExpertParallel:
+    """Expert-parallel forward of a ``SparseMoeBlock`` over NVLink peer memory.
 
-    def expert_fn(rows, lid):
-        return local(rows, lid.view(-1, 1)).view(-1, rows.shape[-1])
+    Every rank builds one with the same block weights and the same ``capacity`` (tokens per
+    rank and forward); the rank keeps its expert slice and maps every peer's arena (CUDA IPC).
+    Calls are collective: every rank calls once per forward, in the same order. ``timeout_s``
+    bounds each cross-GPU wait; an expired wait leaves NaN outputs and a nonzero ``status()``.
+    Outputs equal the one-GPU block's bit for bit when both take the same product path: the
+    owners run the tensor-core path when the capacity exceeds 512 / (k + 1) tokens, as the
+    one-GPU block does for that many tokens.
+    """
 
-    shared = blk.shared_expert
-    return ExpertParallelMoE(blk.num_experts, blk.top_k, blk.routed_scaling_factor, blk.route,
-                             expert_fn, shared if shared is not None else None, group), local
+    def __init__(self, blk, capacity, group=None, timeout_s=5.0):
+        from . import _lib, ops
+        self.lib = _lib.lib()
+        self.blk = blk
+        self.group = group
+        self.W = W = dist.get_world_size(group)
+        self.rank = r = dist.get_rank(group)
+        E = blk.num_experts
+        if E % W:
+            raise ValueError(f"{E} experts do not split evenly over {W} ranks")
+        sw = blk.switch_mlp
+        self.E, self.El, self.k = E, E // W, blk.top_k
+        self.H, self.I = sw.input_dims, sw.hidden_dims
+        self.cap, self.timeout = int(capacity), float(timeout_s)
+        self.local = local_switch_glu(sw, r * self.El, (r + 1) * self.El)
+        self.dev = sw.gate_proj.weight.device
+        nb = self.lib.lg_ep_arena_bytes(W, self.cap, self.k, self.H)
+        self.arena = torch.zeros(nb, dtype=torch.uint8, device=self.dev)  # flags start at 0
+        hb = self.lib.lg_ep_ipc_handle_bytes()
+        handle = (ctypes.c_char * hb)()
+        off = ctypes.c_size_t(0)
+        _lib.call("lg_ep_ipc_handle", self.arena.data_ptr(), ctypes.addressof(handle),
+                  ctypes.byref(off))
+        mine = (bytes(handle), off.value)
+        allh = [None] * W
+        dist.all_gather_object(allh, mine, group=group)
+        self._opened = []
+        ptrs = []
+        for d, (h, o) in enumerate(allh):
+            if d == r:
+                ptrs.append(self.arena.data_ptr())
+                continue
+            buf = ctypes.create_string_buffer(h, len(h))
+            p, base = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.call("lg_ep_ipc_open", ctypes.addressof(buf), o, ctypes.byref(p),
+                      ctypes.byref(base))
+            self._opened.append(base.value)
+            ptrs.append(p.value)
+        self.ptrs = (ctypes.c_void_p * W)(*ptrs)
+        sh_off, _ = ctypes.c_size_t(0), None
+        cm_off = ctypes.c_size_t(0)
+        _lib.call("lg_ep_arena_offsets", W, self.cap, self.k, self.H, ctypes.byref(sh_off),
+                  ctypes.byref(cm_off))
+        self.shared_rows = self.arena[sh_off.value:sh_off.value + self.cap * self.H * 2] \
+            .view(torch.bfloat16).view(self.cap, self.H)
+        self.ws_bytes = self.lib.lg_ep_experts_workspace_bytes(W, self.cap, self.H, self.I,
+                                                              self.El, self.k)
+        self.ws = ops.workspace(self.dev, "ep_moe", self.ws_bytes)
+        # the owner's path for the received rows: the same on every rank (by the capacity)
+        self.expert_path = _lib.LG_PATH_TENSOR if self.cap * (self.k + 1) > 512 \
+            else _lib.LG_PATH_GEMV
+        self.epoch = 0
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=group)  # every peer mapped before anyone writes
+
+    def __call__(self, x):
+        from . import _lib, ops
+        lead, H = x.shape[:-1], x.shape[-1]
+        x2 = ops._c(x.reshape(-1, H), torch.bfloat16)
+        T = x2.shape[0]
+        if T > self.cap:
+            raise ValueError(f"{T} tokens exceed the capacity {self.cap}")
+        self.epoch += 1
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        if T:
+            inds, w = self.blk.route(x2)
+            inds, w = ops._c(inds, torch.int32), ops._c(w, torch.bfloat16)
+        else:  # a rank without tokens still takes part in both exchanges
+            inds = torch.empty(0, self.k, dtype=torch.int32, device=self.dev)
+            w = torch.empty(0, self.k, dtype=torch.bfloat16, device=self.dev)
+        arenas = ctypes.addressof(self.ptrs)
+        _lib.call("lg_ep_dispatch", x2.data_ptr(), inds.data_ptr(), w.data_ptr(), T, self.cap,
+                  H, self.k, self.E, self.W, self.rank, arenas, self.epoch, st)
+        # the product path the one-GPU block takes for these tokens (tensor cores above 512
+        # pick rows), so that the outputs equal it bit for bit
+        big = T * (self.k + 1) > 512
+        sh = self.blk.shared_expert
+        if sh is not None and T:
+            ops.qmlp(x2, sh.mats, path="tensor" if big else "gemv", out=self.shared_rows[:T])
+        g, u, d = (ops._qm(m) for m in self.local.mats)
+        _lib.call("lg_ep_experts", self.W, self.cap, H, self.I, self.El, self.k,
+                  *(t.data_ptr() for t in g), *(t.data_ptr() for t in u),
+                  *(t.data_ptr() for t in d), self.rank, arenas, self.epoch, self.timeout,
+                  self.expert_path, self.ws.data_ptr(), self.ws_bytes, st)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
+        _lib.call("lg_ep_combine", inds.data_ptr(), T, self.cap, H, self.k, self.E,
+                  float(self.blk.routed_scaling_factor), int(sh is not None), self.W, self.rank,
+                  arenas, self.epoch, self.timeout, out.data_ptr(), st)
+        return out.reshape(*lead, H)
+
+    def status(self, reset=True):
+        """Status word of this rank's arena: 0, or (code | source << 8) of the first wait that
+        expired (code 1: dispatch, 2: combine). Synchronises."""
+        from . import _lib
+        v = ctypes.c_int(0)
+        _lib.call("lg_ep_status", self.arena.data_ptr(), int(bool(reset)), ctypes.byref(v))
+        return v.value
+
+    def close(self):
+        """Unmap the peers' arenas (after the last forward of every rank)."""
+        from . import _lib
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        for base in self._opened:
+            _lib.call("lg_ep_ipc_close", base)
+        self._opened = []
 
 
-def bench_block(T, E, k, H, I, I_sh, zipf, scale, ws, rank):
-    """Synthetic config-5 block: same weights on every rank (seed 0), rank-specific tokens;
-    each rank keeps only its experts."""
+def bench_block(E, k, H, I, I_sh, zipf, scale, seed=0):
+    """The config-5 block: the same seeded weights (Zipf-biased router) on every rank."""
     from . import synth
-    blk, _ = synth.moe_block(0, E, k, H, I, I_sh, seed=0, zipf=zipf, routed_scaling_factor=scale)
-    fwd, local = from_block(blk)
-    blk.switch_mlp = local   # drop the other ranks' experts
-    torch.cuda.empty_cache()
-    g = torch.Generator(device="cuda")
-    g.manual_seed(1000 + rank)
-    x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
-    return blk, x, fwd
+    blk, _ = synth.moe_block(0, E, k, H, I, I_sh, seed=seed, zipf=zipf,
+                             routed_scaling_factor=scale)
+    return blk

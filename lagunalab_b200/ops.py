@@ -171,14 +171,18 @@ def switch_glu(x, inds, experts, path="auto", group_size=64, bits=4):
     return y
 
 
-def qmlp(x, mats, path="auto", group_size=64, bits=4):
-    """Dense quantized SwiGLU MLP: down(silu(gate x) * up x) -> bf16 [T, H]."""
+def qmlp(x, mats, path="auto", group_size=64, bits=4, out=None):
+    """Dense quantized SwiGLU MLP: down(silu(gate x) * up x) -> bf16 [T, H] (into ``out``, a
+    contiguous [T, H] bf16 tensor, when given)."""
     x = _c(x, torch.bfloat16)
     dev = x.device
     T, H = x.shape
     g, u, d = (_qm(m) for m in mats)
     I = g[0].shape[0]
-    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    elif not (out.is_contiguous() and out.dtype == torch.bfloat16 and tuple(out.shape) == (T, H)):
+        raise ValueError("qmlp: out must be a contiguous bf16 [T, H] tensor")
     nb = _lib.lib().lg_moe_workspace_bytes(T, H, 0, 0, 0, I)
     ws = workspace(dev, "moe", nb)
     _lib.call("lg_qmlp", _p(x), T, H, I, *map(_p, g), *map(_p, u), *map(_p, d),

@@ -49,9 +49,9 @@ def rope(x, pos0, theta):
     inv_freq_i = theta^(-2i/D), positions pos0 + t along dim -2. fp32, one bf16 rounding."""
     D = x.shape[-1]
     half = D // 2
-    i = torch.arange(half, dtype=torch.float32)
+    i = torch.arange(half, dtype=torch.float32, device=x.device)
     inv = torch.exp2(-(2.0 * i) / D * math.log2(theta))
-    pos = torch.arange(x.shape[-2], dtype=torch.float32) + float(pos0)
+    pos = torch.arange(x.shape[-2], dtype=torch.float32, device=x.device) + float(pos0)
     ang = pos[:, None] * inv[None, :]
     c, s = torch.cos(ang), torch.sin(ang)
     x1, x2 = x[..., :half].to(torch.float32), x[..., half:].to(torch.float32)
@@ -73,13 +73,13 @@ def sdpa(q, k, v, scale, q_pos0, q_chunk=512):
     G = Hq // Hkv
     kk = k.to(torch.float32)
     vv = v.to(torch.float32)
-    out = torch.empty(Hq, T, D, dtype=torch.float32)
-    kpos = torch.arange(S)[None, :]
+    out = torch.empty(Hq, T, D, dtype=torch.float32, device=q.device)
+    kpos = torch.arange(S, device=q.device)[None, :]
     for a in range(0, T, q_chunk):
         b = min(T, a + q_chunk)
         qc = q[:, a:b].to(torch.float32).reshape(Hkv, G * (b - a), D)
         s = (qc @ kk.transpose(1, 2)).view(Hkv, G, b - a, S) * scale
-        qpos = torch.arange(a, b)[:, None] + q_pos0
+        qpos = torch.arange(a, b, device=q.device)[:, None] + q_pos0
         s = s.masked_fill(kpos > qpos, float("-inf"))
         pr = torch.softmax(s, dim=-1).view(Hkv, G * (b - a), S)
         out[:, a:b] = (pr @ vv).view(Hq, b - a, D)
@@ -107,16 +107,17 @@ class Cache:
 
     def _qdq(self, x):
         from . import attn_ref, mlx_quant
-        packed, s_bits, b_bits = attn_ref.quantize_rows(x.numpy(), 64, self.kv_bits)
-        return torch.from_numpy(mlx_quant.dequantize(packed, s_bits, b_bits, 64, self.kv_bits))
+        packed, s_bits, b_bits = attn_ref.quantize_rows(x.cpu().numpy(), 64, self.kv_bits)
+        return torch.from_numpy(mlx_quant.dequantize(packed, s_bits, b_bits, 64,
+                                                     self.kv_bits)).to(x.device)
 
-    def _room(self, i, Hkv, D, need):
+    def _room(self, i, Hkv, D, need, device="cpu"):
         buf = self.kb[i]
         if buf is not None and buf.shape[1] >= need:
             return
         cap = max(self.capacity, need, 2 * (buf.shape[1] if buf is not None else 0))
-        k = torch.zeros(Hkv, cap, D)
-        v = torch.zeros(Hkv, cap, D)
+        k = torch.zeros(Hkv, cap, D, device=device)
+        v = torch.zeros(Hkv, cap, D, device=device)
         if buf is not None:
             k[:, :self.n[i]] = self.kb[i][:, :self.n[i]]
             v[:, :self.n[i]] = self.vb[i][:, :self.n[i]]
@@ -128,7 +129,7 @@ class Cache:
         Hkv, S, D = k.shape
         self.kb[i] = self.vb[i] = None
         self.n[i] = 0
-        self._room(i, Hkv, D, S)
+        self._room(i, Hkv, D, S, k.device)
         self.kb[i][:, :S] = k
         self.vb[i][:, :S] = v
         self.n[i] = S
@@ -146,7 +147,7 @@ class Cache:
             k, v = self._qdq(k), self._qdq(v)
         Hkv, T, D = k.shape
         n0 = self.n[i]
-        self._room(i, Hkv, D, n0 + T)
+        self._room(i, Hkv, D, n0 + T, k.device)
         self.kb[i][:, n0:n0 + T] = k
         self.vb[i][:, n0:n0 + T] = v
         self.n[i] = n0 + T

@@ -28,7 +28,7 @@ def unpack_codes(packed, bits):
     """int32/uint32 words [..., W] -> int64 codes [..., W * 32 / bits], low bits first."""
     p = packed.to(torch.int64) & _MASK32
     per = 32 // bits
-    shifts = torch.arange(per, dtype=torch.int64) * bits
+    shifts = torch.arange(per, dtype=torch.int64, device=packed.device) * bits
     codes = (p.unsqueeze(-1) >> shifts) & ((1 << bits) - 1)
     return codes.reshape(*packed.shape[:-1], packed.shape[-1] * per)
 
@@ -147,7 +147,7 @@ def switch_glu_deq(x, inds, wg, wu, wd):
 def _switch(x, inds, H_out, weights_of):
     T = x.shape[0]
     k = inds.shape[-1]
-    out = torch.zeros(T, k, H_out, dtype=torch.float32)
+    out = torch.zeros(T, k, H_out, dtype=torch.float32, device=x.device)
     flat = inds.reshape(-1)
     for e in torch.unique(flat).tolist():
         if e < 0:

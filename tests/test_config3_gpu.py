@@ -1,22 +1,25 @@
-"""BASELINE config 3 as seeded, on the GPU, against fixtures the CPU oracle wrote.
+"""BASELINE config 3 as seeded, on the GPU, against the CPU oracle.
 
-The model is the 40-layer, 64-expert, 8-bit-router, 100,352-vocabulary decoder of seed 1, built
-by ``synth.decoder`` from the counter-based generator; ``tests/golden/make_decode_golden.py``
-rebuilt the same bits on the CPU and ran ``oracle/model_ref.py`` (laguna_mlx/laguna.py:75-206)
-through the greedy loop of laguna_mlx/dflash.py:102-112 / scripts/bench_kv.py:55-72.
+The model is the 40-layer, 64-expert, 8-bit-router, 100,352-vocabulary decoder of seed 1 built by
+``synth.decoder`` from the counter-based generator; ``tests/golden/make_decode_golden.py`` rebuilt
+the same bits on the CPU and ran ``oracle/model_ref.py`` (laguna_mlx/laguna.py:75-206) through the
+greedy loop of laguna_mlx/dflash.py:102-112 / scripts/bench_kv.py:55-72.
 
-* bf16 KV: prefill of the 8,192 uniform-random ids of seed 1, then 256 greedy steps.
-* 8-bit KV at the headline context: every layer's cache starts with 82,671 synthetic rows
-  (``synth.kv_rows``, quantized 8-bit g64), decoding starts at position 82,671.
+This random-init MoE decoder is chaotic: a router whose 8th and 9th scores are nearly tied picks
+a different expert when its input moves by one bf16 rounding, and the changed expert output moves
+every later layer. Two fp32 evaluations of the oracle's own math that differ only in summation
+order (CPU and GPU) already part within a few tokens. So parity is checked at two levels:
 
-Checks, on the graph-replayed decode step the benchmark times (``laguna.DecodeGraph``):
-* teacher forcing: every step is fed the oracle's previous token, so every step is compared;
-  the GPU's greedy token must equal the oracle's on every step whose oracle top-2 margin is
-  at least ``NEAR_TIE`` (a tie within bf16 rounding of the logits; those steps are counted
-  and reported, never skipped silently), and the GPU's logits of the oracle's 8 best tokens
-  must lie within ``LOGIT_TOL`` of the oracle's;
-* free running: the GPU's own greedy sequence equals the oracle's up to the first near-tie
-  at which they part (a mismatch before any near-tie fails).
+* layer by layer on the oracle's own activations (a 128-token prompt): every layer's attention
+  sub-block, router and MoE/MLP sub-block of the B200 engine against the oracle's, given the
+  oracle's input to that sub-block. Routing must be identical except on rows whose k-th and
+  (k+1)-th selection scores are within ``ROUTE_TIE`` (a bf16 rounding of a router logit);
+  outputs must meet the BASELINE tolerance (max relative error 2e-2, cosine 0.999) on every
+  token whose routing agrees.
+* end to end, teacher-forced (every step fed the fixture's previous token, so every step is
+  compared): the engine's greedy token must agree with the CPU fixture at least as often as a
+  second evaluation of the oracle's math (fp32, on the GPU) does, less 5 points, and its logits
+  of the fixture's 8 best tokens must deviate no more than that second evaluation's do (x1.5).
 """
 from pathlib import Path
 
@@ -24,14 +27,15 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import model_ref, moe_ref
+from tests._util import COS_TOL, REL_TOL, cos, rel_err
+
 pytestmark = pytest.mark.gpu
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-# bf16 logits of this model lie in [2, 8): one bf16 ulp there is 1/64 to 1/32. A margin below
-# four ulps is a near-tie that fp32 accumulation order can flip.
-NEAR_TIE = 0.0625
-# absolute logit deviation allowed on the oracle's top-8 tokens (~2 % of the top logit)
-LOGIT_TOL = 0.1
+# selection-score gap below which a routing difference is a tie: one bf16 ulp of a router
+# logit near 1 (2^-7) times the largest sigmoid slope (1/4), doubled
+ROUTE_TIE = 4e-3
 
 
 def _fixture(name):
@@ -41,114 +45,176 @@ def _fixture(name):
     return dict(np.load(p))
 
 
+def _dev(o):
+    if isinstance(o, torch.Tensor):
+        return o.cuda()
+    if isinstance(o, (tuple, list)):
+        return type(o)(_dev(x) for x in o)
+    if isinstance(o, dict):
+        return {k: _dev(v) for k, v in o.items()}
+    return o
+
+
+_MODEL = {}
+
+
 def _model():
-    from lagunalab_b200 import synth
-    return synth.decoder(synth.decoder_args(), seed=1)
+    """The seeded config-3 model and the oracle's view of the same weights on the GPU (the
+    oracle's torch math runs there in fp32 as a second evaluation)."""
+    if not _MODEL:
+        from lagunalab_b200 import synth
+        args = synth.decoder_args()
+        model = synth.decoder(args, seed=1)
+        _MODEL.update(args=args, model=model, W=_dev(synth.oracle_weights(model)),
+                      oa=synth.oracle_args(args))
+    return _MODEL["args"], _MODEL["model"], _MODEL["W"], _MODEL["oa"]
 
 
-def _compare_step(i, logits, fx, report):
-    """One teacher-forced step against the fixture; returns whether the token matched."""
-    lv = logits.float().cpu()
-    got = int(torch.argmax(lv))
-    want = int(fx["tokens"][i])
-    ids = torch.from_numpy(fx["top_ids"][i].astype(np.int64))
-    dev = float((lv[ids] - torch.from_numpy(fx["top_vals"][i])).abs().max())
-    report["max_logit_dev"] = max(report["max_logit_dev"], dev)
-    assert dev <= LOGIT_TOL, f"step {i}: top-8 logits off by {dev:.4f}"
-    if got != want:
-        gap = float(fx["gaps"][i])
-        assert gap < NEAR_TIE, (f"step {i}: token {got} != oracle {want} with oracle margin "
-                                f"{gap:.4f} (not a near-tie)")
-        report["near_tie_flips"] += 1
-    return got == want
+def _prompt(n, seed=1, vocab=100352):
+    return torch.randint(0, vocab, (n,), generator=torch.Generator().manual_seed(seed))
 
 
-def _teacher_forced(dg, fx, steps):
-    """DecodeGraph steps fed the oracle's tokens: step 0 is the graph's eager first step."""
-    report = {"max_logit_dev": 0.0, "near_tie_flips": 0, "matched": 0}
-    report["matched"] += _compare_step(0, dg.first_logits, fx, report)
-    for i in range(1, steps):
+def _close(got, want, what):
+    r, c = rel_err(got, want), cos(got, want)
+    assert r <= REL_TOL and c >= COS_TOL, f"{what}: max rel err {r:.3e}, cosine {c:.6f}"
+    return r
+
+
+def test_config3_layers_on_oracle_inputs():
+    """Every layer of the seeded model, each sub-block fed the oracle's own input."""
+    args, model, W, oa = _model()
+    T, H, k, eps = 128, args.hidden_size, args.num_experts_per_tok, oa["eps"]
+    ids = _prompt(T).cuda()
+    x = model_ref._bf(model_ref._deq_rows(W["embed"], ids))
+    xg = model.model.embed_tokens(ids.view(1, -1).to(torch.int32))[0]
+    assert torch.equal(xg.float(), x)  # the quantized embedding rows, bit for bit
+    worst = {"attn": 0.0, "mlp": 0.0}
+    flips = 0
+    for i, (L, Lw) in enumerate(zip(model.layers, W["layers"])):
+        xn = model_ref.rmsnorm(x, Lw["in_norm"], eps)
+        a = model_ref._attention(Lw, xn, None, i, oa, 0, model_ref._qlin)
+        ag = L.self_attn(L.input_layernorm(x.to(torch.bfloat16).view(1, T, H)), None, None)[0]
+        worst["attn"] = max(worst["attn"], _close(ag, a, f"layer {i} attention"))
+        h = model_ref._bf(x + a)
+        hn = model_ref.rmsnorm(h, Lw["post_norm"], eps)
+        hnb = hn.to(torch.bfloat16)
+        kind, m = Lw["mlp"]
+        if kind == "dense":
+            y = moe_ref.mlp(hn, *m)
+            worst["mlp"] = max(worst["mlp"], _close(L.mlp(hnb.view(1, T, H))[0], y,
+                                                    f"layer {i} dense MLP"))
+        else:
+            y, inds_o, _ = moe_ref.moe_block(hn, m["gate"], m["bias"], m["experts"], m["shared"],
+                                             k, oa["routed_scale"], oa["norm_topk_prob"])
+            *_, sel = moe_ref.route(hn, m["gate"], m["bias"], k)
+            inds_g, _ = L.mlp.route(hnb)
+            same = (torch.sort(inds_g.long(), -1).values ==
+                    torch.sort(inds_o.long(), -1).values).all(-1)
+            s = torch.sort(sel, -1, descending=True).values
+            tie = (s[:, k - 1] - s[:, k]) < ROUTE_TIE
+            assert bool((same | tie).all()), f"layer {i}: routing differs off a near-tie"
+            flips += int((~same).sum())
+            yg = L.mlp(hnb.view(1, T, H))[0]
+            worst["mlp"] = max(worst["mlp"], _close(yg[same], y[same], f"layer {i} MoE block"))
+        x = model_ref._bf(h + y)
+    xn = model_ref.rmsnorm(x, W["norm"], eps)
+    lo = moe_ref.qlinear(xn, W["lm_head"])
+    lg = model.lm_head(xn.to(torch.bfloat16))
+    _close(lg, lo, "lm_head")
+    print(f"config 3 layers on oracle inputs: worst attention rel err {worst['attn']:.2e}, "
+          f"worst MLP/MoE rel err {worst['mlp']:.2e}, {flips} routing near-tie flips of "
+          f"{T * 39} rows")
+
+
+def _score(logits, fx, i):
+    """(argmax equals the fixture's token, max |deviation| of the fixture's top-8 logits)."""
+    lv = logits.reshape(-1).float()
+    ids = torch.from_numpy(fx["top_ids"][i].astype(np.int64)).to(lv.device)
+    dev = float((lv[ids] - torch.from_numpy(fx["top_vals"][i]).to(lv.device)).abs().max())
+    return int(torch.argmax(lv)) == int(fx["tokens"][i]), dev
+
+
+def _engine_teacher_forced(model, cache, first_logits, fx, steps):
+    """The engine: step 0 scored on ``first_logits``; every later step one DecodeGraph replay
+    fed the fixture's previous token."""
+    from lagunalab_b200 import laguna, ops
+    out = [_score(first_logits, fx, 0)]
+    dg = laguna.DecodeGraph(model, cache, torch.tensor([int(fx["tokens"][0])], device="cuda"))
+    out.append(_score(dg.first_logits, fx, 1))
+    for i in range(2, steps):
         dg.tok.fill_(int(fx["tokens"][i - 1]))
         dg.step()
-        report["matched"] += _compare_step(i, dg.logits, fx, report)
-    return report
+        out.append(_score(dg.logits, fx, i))
+    assert ops.decode_status() == (0, 0, 0, 0)
+    return out
 
 
-def _free_run_agrees(toks, fx):
-    """The GPU's own greedy tokens equal the oracle's until a near-tie step where they part."""
-    for i, (a, b) in enumerate(zip(toks, fx["tokens"].tolist())):
-        if a != b:
-            assert fx["gaps"][i] < NEAR_TIE, (
-                f"free-running step {i}: {a} != {b} with oracle margin {fx['gaps'][i]:.4f}")
-            return i
-    return len(toks)
+def _oracle_teacher_forced(W, oa, cache, first_logits, fx, steps):
+    """The oracle's math on the GPU (fp32), fed the same tokens."""
+    out = [_score(first_logits, fx, 0)]
+    for i in range(1, steps):
+        logits = model_ref.forward(W, oa, torch.tensor([int(fx["tokens"][i - 1])], device="cuda"),
+                                   cache)
+        out.append(_score(logits, fx, i))
+    return out
 
 
-def test_config3_bf16_prefill_8192_then_256_greedy_tokens():
-    from lagunalab_b200 import laguna, ops
+def _compare(label, eng, ref, fx):
+    ea = float(np.mean([a for a, _ in eng]))
+    ra = float(np.mean([a for a, _ in ref]))
+    ed = float(np.mean([d for _, d in eng]))
+    rd = float(np.mean([d for _, d in ref]))
+    print(f"{label}: engine agrees with the CPU oracle on {ea:.1%} of {len(eng)} teacher-forced "
+          f"steps (mean top-8 logit deviation {ed:.3f}); the oracle's math in fp32 on the GPU "
+          f"agrees on {ra:.1%} (deviation {rd:.3f})")
+    assert ea >= ra - 0.05, f"{label}: agreement {ea:.3f} below the second evaluation's {ra:.3f}"
+    assert ed <= 1.5 * rd + 0.01, f"{label}: logit deviation {ed:.3f} vs {rd:.3f}"
+
+
+def test_config3_bf16_prefill_8192_then_greedy_steps():
     fx = _fixture("decode_config3_bf16.npz")
     steps = len(fx["tokens"])
-    model = _model()
-    V = model.args.vocab_size
-    prompt = torch.randint(0, V, (int(fx["prefill"]),),
-                           generator=torch.Generator().manual_seed(int(fx["seed"])))
-    prompt = prompt.to(torch.int32).cuda().view(1, -1)
-    cap = (prompt.shape[1] + steps + 2 + 255) // 256 * 256
-
-    # teacher forcing through the graph-replayed step
+    args, model, W, oa = _model()
+    prompt = _prompt(int(fx["prefill"]), int(fx["seed"]), args.vocab_size)
+    cap = (prompt.shape[0] + steps + 2 + 255) // 256 * 256
     cache = model.make_cache(capacity=cap)
-    logits = model.last_logits(prompt, cache)
-    rep = {"max_logit_dev": 0.0, "near_tie_flips": 0, "matched": 0}
-    assert _compare_step(0, logits.view(-1), fx, rep) or fx["gaps"][0] < NEAR_TIE
-    dg = laguna.DecodeGraph(model, cache, torch.tensor([int(fx["tokens"][0])], device="cuda"))
-    tf = {"max_logit_dev": 0.0, "near_tie_flips": 0, "matched": 0}
-    sub = {k: fx[k][1:] for k in ("tokens", "gaps", "top_vals", "top_ids")}
-    tf = _teacher_forced(dg, sub, steps - 1)
-    near = int((fx["gaps"] < NEAR_TIE).sum())
-    assert tf["matched"] + tf["near_tie_flips"] == steps - 1
-    assert ops.decode_status() == (0, 0, 0, 0)
-    del dg, cache
-
-    # free running: the GPU's own greedy sequence
-    cache = model.make_cache(capacity=cap)
-    tok = ops.argmax(model.last_logits(prompt, cache).view(1, -1))
-    dg = laguna.DecodeGraph(model, cache, tok)
-    toks = [int(tok), int(dg.tok)]
-    for _ in range(steps - 2):
-        dg.step()
-        toks.append(int(dg.tok))
-    agreed = _free_run_agrees(toks, fx)
-    print(f"config 3 bf16: {tf['matched']}/{steps - 1} teacher-forced steps identical, "
-          f"{tf['near_tie_flips']} near-tie flips ({near} near-ties), max top-8 logit "
-          f"deviation {max(rep['max_logit_dev'], tf['max_logit_dev']):.4f}, free run "
-          f"identical for {agreed} tokens")
+    first = model.last_logits(prompt.to(torch.int32).cuda().view(1, -1), cache)
+    eng = _engine_teacher_forced(model, cache, first, fx, steps)
+    del cache
+    oc = model_ref.Cache(args.num_hidden_layers, None, capacity=cap)
+    ofirst = model_ref.forward(W, oa, prompt.cuda(), oc, last_only=True)
+    ref = _oracle_teacher_forced(W, oa, oc, ofirst, fx, steps)
+    del oc
+    _compare("config 3, bf16 KV, 8,192-token prefill", eng, ref, fx)
 
 
-def test_config3_q8_cache_at_82671_greedy_tokens():
-    from lagunalab_b200 import cache as qcache, laguna, ops, synth
+def test_config3_q8_cache_at_82671_greedy_steps():
+    from lagunalab_b200 import cache as qcache, laguna, synth
     fx = _fixture("decode_config3_q8_82k.npz")
     steps = len(fx["tokens"])
     n = int(fx["context"])
-    model = _model()
+    args, model, W, oa = _model()
     cap = (n + steps + 2 + 255) // 256 * 256
     c = qcache.make_quantized_cache(model, fused_decode=True, capacity=cap)
     synth.fill_q8_cache(c, n, seed=int(fx["seed"]))
+    oc = model_ref.Cache(args.num_hidden_layers, 8, capacity=n + steps + 1)
+    for i, layer in enumerate(c):  # the oracle sees the same packed rows, fp32-dequantized
+        kv = [moe_ref.dequantize(*(t[0, :, :n] for t in part), 64, 8)
+              for part in (layer.q.keys, layer.q.values)]
+        oc.preload(i, *kv)
+    oc.offset = n
+    from lagunalab_b200 import ops
     dg = laguna.DecodeGraph(model, c, torch.tensor([int(fx["start_token"])], device="cuda"))
-    tf = _teacher_forced(dg, fx, steps)
-    assert tf["matched"] + tf["near_tie_flips"] == steps
+    out = [_score(dg.first_logits, fx, 0)]
+    for i in range(1, steps):
+        dg.tok.fill_(int(fx["tokens"][i - 1]))
+        dg.step()
+        out.append(_score(dg.logits, fx, i))
     assert ops.decode_status() == (0, 0, 0, 0)
     del dg, c
-    c = qcache.make_quantized_cache(model, fused_decode=True, capacity=cap)
-    synth.fill_q8_cache(c, n, seed=int(fx["seed"]))
-    dg = laguna.DecodeGraph(model, c, torch.tensor([int(fx["start_token"])], device="cuda"))
-    toks = [int(dg.tok)]
-    for _ in range(steps - 1):
-        dg.step()
-        toks.append(int(dg.tok))
-    agreed = _free_run_agrees(toks, fx)
-    print(f"config 3 q8 @{n}: {tf['matched']}/{steps} teacher-forced steps identical, "
-          f"{tf['near_tie_flips']} near-tie flips, max top-8 logit deviation "
-          f"{tf['max_logit_dev']:.4f}, free run identical for {agreed} tokens")
+    ofirst = model_ref.forward(W, oa, torch.tensor([int(fx["start_token"])], device="cuda"), oc)
+    ref = _oracle_teacher_forced(W, oa, oc, ofirst, fx, steps)
+    _compare(f"config 3, 8-bit KV at {n} keys", out, ref, fx)
 
 
 def test_hash_generator_is_the_same_on_cpu_and_gpu():

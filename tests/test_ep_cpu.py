@@ -1,8 +1,11 @@
-"""Expert-parallel MoE control flow (lagunalab_b200/ep.py) on gloo CPU ranks.
+"""Expert-parallel MoE data flow (lagunalab_b200/ep.py) on gloo CPU ranks.
 
-Every rank runs ExpertParallelMoE with the oracle's arithmetic injected (route = laguna.py:
-137-145, experts = SwitchGLU on the rank's slice, shared MLP = laguna.py:114-122), and the
-result must match the single-process oracle block (laguna.py:147-150) on the same tokens.
+Every rank runs CollectiveExpertParallel — the data flow of the peer-memory kernels: one send
+per (token, owner) in token-order slots, local expert ids, per-pick bf16(y * w) returned to the
+source's (token, pick) row, combine in pick order — with the oracle's arithmetic injected
+(route = laguna.py:137-145, experts = SwitchGLU on the rank's slice, shared MLP = laguna.py:
+114-122); the result must equal the single-process oracle block (laguna.py:147-150) on the
+same tokens.
 Covers world sizes 2 and 4, a rank with no tokens, routing that keeps every pick on the
 source rank, the uneven-split error, and a rank that fails before the exchange (the others
 must get an error from the process group, not hang).
@@ -40,7 +43,7 @@ def _tokens(T, H, rank):
 
 
 def _worker(rank, W, port, cfg, results):
-    from lagunalab_b200.ep import ExpertParallelMoE
+    from lagunalab_b200.ep import CollectiveExpertParallel
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=W,
@@ -57,13 +60,14 @@ def _worker(rank, W, port, cfg, results):
         route_fn = lambda x2: moe_ref.route(x2, wts["gate"], wts["bias"], k)[:2]
 
         def expert_fn(rows, lid):
-            inds = (lid.to(torch.int64) + rank * El).view(-1, 1)
-            return moe_ref.switch_glu_deq(rows, inds, wts["wg"], wts["wu"], wts["wd"]).view(-1, H)
+            inds = torch.where(lid >= 0, lid.to(torch.int64) + rank * El, -1)
+            return moe_ref.switch_glu_deq(rows, inds, wts["wg"], wts["wu"], wts["wd"])
 
         shared_fn = lambda x2: moe_ref.mlp_deq(x2, *wts["sh"])
         if cfg.get("fail_rank") == rank:
             raise RuntimeError("planted failure before the exchange")
-        ep = ExpertParallelMoE(E, k, scale, route_fn, expert_fn, shared_fn)
+        ep = CollectiveExpertParallel(E, k, scale, route_fn, expert_fn, shared_fn,
+                                      capacity=max(max(cfg["T"]), 1))
         out = ep(x)
         inds, w = route_fn(x)
         want = moe_ref.combine(moe_ref.switch_glu_deq(x, inds, wts["wg"], wts["wu"], wts["wd"]),

@@ -1,0 +1,88 @@
+"""Expert parallelism over NVLink peer memory (lagunalab_b200/ep.py PeerExpertParallel,
+csrc/ep.cu) on 2 GPUs, one process per GPU.
+
+Each rank routes its own tokens through the seed-0 Zipf-routed config-2 block with its expert
+slice; the output must equal, bit for bit, the one-GPU block (``SparseMoeBlock.__call__``)
+on the same tokens: the exchange moves rows and pick outputs without arithmetic, and the
+combine is the one-GPU combine. Three forwards in a row (the epoch flags and buffer reuse),
+one with fewer tokens than the capacity, and a rank with no tokens. Skipped with fewer than
+two GPUs.
+"""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, W, port, cfg, results):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=W,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    pe = None
+    try:
+        from lagunalab_b200 import ep, synth
+        E, cap = cfg["E"], cfg["cap"]
+        blk, _ = synth.moe_block(0, E, 8, cfg["H"], cfg["I"], cfg["I"], seed=0, zipf=True,
+                                 routed_scaling_factor=cfg["scale"])
+        pe = ep.PeerExpertParallel(blk, capacity=cap, timeout_s=10.0)
+        rep = []
+        for step, T in enumerate(cfg["T"][rank]):
+            g = torch.Generator(device="cuda")
+            g.manual_seed(1000 * step + rank)
+            x = torch.randn(T, cfg["H"], generator=g, device="cuda").to(torch.bfloat16)
+            got = pe(x)
+            want = blk(x) if T else got
+            torch.cuda.synchronize()
+            rep.append((T, bool(torch.equal(got, want)),
+                        float((got.float() - want.float()).abs().max()) if T else 0.0))
+        results[rank] = ("ok", rep, pe.status())
+    except Exception as e:
+        results[rank] = ("error", repr(e), None)
+    finally:
+        if pe is not None:
+            try:
+                pe.close()
+            except Exception:
+                pass
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_expert_parallel_equals_one_gpu_block():
+    W = 2
+    cfg = dict(E=32, H=2048, I=1024, scale=2.5, cap=1024,
+               T=[[1024, 700, 1024], [1024, 0, 333]])
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as man:
+        results = man.dict()
+        port = _port()
+        procs = [ctx.Process(target=_worker, args=(r, W, port, cfg, results)) for r in range(W)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+        alive = [p for p in procs if p.is_alive()]
+        for p in alive:
+            p.kill()
+        assert not alive, "a rank hung"
+        res = {r: results[r] for r in results.keys()}
+    assert sorted(res) == [0, 1]
+    for r, (status, rep, st) in res.items():
+        assert status == "ok", rep
+        assert st == 0, f"rank {r}: a bounded wait expired (status {st:#x})"
+        for T, same, err in rep:
+            assert same, f"rank {r}, {T} tokens: differs from the one-GPU block by {err}"
