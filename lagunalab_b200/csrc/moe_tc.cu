@@ -46,8 +46,11 @@ constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;  // 32 KB
 constexpr int TC_P_BYTES = TC_BN * TC_BK / 2;  // 8 KB
 constexpr int TC_NBAR = 2 * TC_NA + 2 * TC_NS + 2 * TC_NP + 5;
+// down-epilogue staging: per epilogue warp 32 rows x 64 bf16 columns, rows 144 bytes apart
+constexpr int TC_OUT_PITCH = 144;
+constexpr int TC_OUT_BYTES = 4 * 32 * TC_OUT_PITCH;
 constexpr size_t TC_SMEM = 1024 + TC_NA * TC_A_BYTES + TC_NS * TC_B_BYTES + TC_NP * TC_P_BYTES +
-                           TC_NBAR * 8 + 16;
+                           TC_NBAR * 8 + 16 + 16 + TC_OUT_BYTES;
 
 #ifdef LG_TC_PROFILE
 // Diagnostic build only: cycles each role spends waiting, per CTA (16 counters).
@@ -133,6 +136,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* t_empty = t_full + 2;
   uint64_t* teardown = t_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(teardown + 1);
+  uint8_t* sOut = reinterpret_cast<uint8_t*>(  // 16-byte aligned, within the 32 bytes reserved
+      (reinterpret_cast<uintptr_t>(tmem_slot) + 4 + 15) & ~static_cast<uintptr_t>(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = a.err;
@@ -404,21 +409,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       } else {
-        const int p = valid ? a.perm[R] : 0;
+        // down: gather_qmm's bf16 output per pick row (shared rows after the routed ones), or
+        // (expert parallel) bf16(bf16(y) * w) into the source rank's combine row. 64 columns
+        // at a time go through this warp's shared-memory rows, so that each store instruction
+        // writes whole 128-byte lines (8 lanes per row, 4 rows per instruction) — also to a
+        // peer GPU's memory over NVLink
         const int n0 = nt * 256;
-        // destination row: local per-pick rows, or (expert parallel) the source rank's
-        // combine row with the routing weight applied
-        __nv_bfloat16* orow = a.ypick + (size_t)p * H;
+        __nv_bfloat16* orow = nullptr;
         float wt = 1.0f;
-        if (valid && a.ep.on) orow = ep_ret_row(a.ep, p, a.k, H, &wt);
+        if (valid) {
+          const int p = a.perm[R];
+          orow = a.ep.on ? ep_ret_row(a.ep, p, a.k, H, &wt) : a.ypick + (size_t)p * H;
+        }
+        uint8_t* stg = sOut + q * (32 * TC_OUT_PITCH);
+        uint8_t* mine = stg + lane * TC_OUT_PITCH;
 #pragma unroll 1
-        for (int c = 0; c < 256; c += 16) {
-          uint32_t yv[16];
-          tmem_ld16(taddr + c, yv);
-          tmem_ld_wait(yv);
-          if (valid) {
-            // gather_qmm's bf16 output, stored per pick (shared rows after the P routed
-            // ones); the combine sums each token's rows in a fixed order afterwards
+        for (int c0 = 0; c0 < 256; c0 += 64) {
+#pragma unroll 1
+          for (int cc = 0; cc < 64; cc += 16) {
+            uint32_t yv[16];
+            tmem_ld16(taddr + c0 + cc, yv);
+            tmem_ld_wait(yv);
             float y[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = __uint_as_float(yv[j]);
@@ -426,13 +437,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) y[j] = round_bf16(y[j]) * wt;
             }
-            __nv_bfloat16* o = orow + n0 + c;
-            *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]),
-                                                      pack_bf2(y[4], y[5]), pack_bf2(y[6], y[7]));
-            *reinterpret_cast<uint4*>(o + 8) =
-                make_uint4(pack_bf2(y[8], y[9]), pack_bf2(y[10], y[11]), pack_bf2(y[12], y[13]),
-                           pack_bf2(y[14], y[15]));
+            uint4* s4 = reinterpret_cast<uint4*>(mine + cc * 2);
+            s4[0] = make_uint4(pack_bf2(y[0], y[1]), pack_bf2(y[2], y[3]), pack_bf2(y[4], y[5]),
+                               pack_bf2(y[6], y[7]));
+            s4[1] = make_uint4(pack_bf2(y[8], y[9]), pack_bf2(y[10], y[11]),
+                               pack_bf2(y[12], y[13]), pack_bf2(y[14], y[15]));
           }
+          __syncwarp();
+#pragma unroll
+          for (int w8 = 0; w8 < 8; ++w8) {
+            const int rr = w8 * 4 + (lane >> 3), seg = lane & 7;
+            const unsigned long long dst =
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+            if (dst) {
+              const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * TC_OUT_PITCH + seg * 16);
+              *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + (size_t)(n0 + c0) * 2 +
+                                        seg * 16) = v;
+            }
+          }
+          __syncwarp();
         }
       }
       // every epilogue thread has waited for its TMEM loads; one arrive hands the accumulator
