@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32, 4) moe_dec_gateup_kernel(MdArgs
   group_sums(xs, gpr, gsum);
   const int gpw = (gpr + NW - 1) / NW;
   const int gw0 = warp * gpw, gwn = max(0, min(gpr, gw0 + gpw) - gw0);
-  if (!mbar_wait(bar, 0, berr, 1, 400000000LL)) {
+  if (!__syncthreads_and(mbar_wait(bar, 0, berr, 1, 400000000LL))) {  // CTA-uniform exit
     // the tiles never arrived: record it, let the copies drain (bounded), leave the rows unset
     if (tid == 0 && atomicCAS(&g_stage_check[0], 0ull, 4ull) == 0ull) g_stage_check[3] = 0xB1u;
     for (const long long t0 = clock64(); !mbar_try_wait(bar, 0) && clock64() - t0 < 400000000LL;) {

@@ -291,7 +291,8 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
   for (; j < nw; ++j) {
     const int s = j % QA_STAGES;
     const int t0 = QA_TK * (tile0 + warp + QA_WARPS * j);
-    if (!mbar_wait(&bars[s], (j / QA_STAGES) & 1, s_flag, 1)) break;
+    // the warp leaves together: the loop body issues warp-collective MMAs
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (j / QA_STAGES) & 1, s_flag, 1))) break;
     const uint8_t* Kt = kvw + s * 2 * QA_TILE;
     const uint8_t* Vt = Kt + QA_TILE;
     uint8_t* St = scw + s * 4 * QA_SCS;
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(QA_THREADS, 1)
   } else {
     for (int i = threadIdx.x; i < nsg; i += QA_THREADS) t_ml[i] = __ldcg(gml + i);
   }
-  __syncthreads();
+  ok = __syncthreads_and(ok);  // one verdict for the whole CTA
   // per head (one warp each): max over splits, then the normalised split weights
   for (int h = warp; h < G; h += QA_WARPS) {
     float M = -INFINITY;
