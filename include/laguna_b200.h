@@ -270,13 +270,19 @@ int lg_embed(const int32_t* ids, int T, const uint32_t* w_q, const void* w_s, co
  *   k_cache bf16 [Hkv, cap, D] row p = rope(bf16(rmsnorm(k_h, kn_w)), p)
  *   v_cache bf16 [Hkv, cap, D] row p = v_h
  *   gate_out bf16 [T, Hq or Hq*D]     = bf16(softplus(float(g)))
- * RoPE: non-interleaved pairs (i, i + D/2), inv_freq_i = theta^(-2i/D) (the default rope of
- * laguna.py:69-72).  D % 64 == 0, D <= 256.  Rows p >= cap are not written (size the cache).
+ * RoPE: non-interleaved pairs (i, i + R/2) over the first R dims (laguna.py:62-72). rot_dims 0
+ * (inv_freq NULL, mscale 1): R = D and inv_freq_i = theta^(-2i/D), the default rope.
+ * Otherwise R = rot_dims (a multiple of 64, <= D) with the caller's frequency table
+ * inv_freq fp32 [R/2] (partial rotary, YaRN) and, for mscale != 1 (YaRN's attention factor),
+ * the rotated dims scaled by mscale and rounded to bf16 first; dims past R pass through.
+ * Cache rows: ring > 0 (a sliding window's ring buffer, ring == cap): row = p mod ring;
+ * else row = p - row0.  D % 64 == 0, D <= 256.  Rows outside [0, cap) are not written.
  */
 int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
                  const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
                  int pos_host, int gate_per_head, void* q_out, void* k_cache, void* v_cache,
-                 int cap, void* gate_out, void* stream);
+                 int cap, void* gate_out, const float* inv_freq, int rot_dims, float mscale,
+                 int ring, int row0, void* stream);
 
 /*
  * lg_attn_prep with an 8-bit group-64 KV cache (DequantKVCache, laguna_mlx/cache.py:66-106):
@@ -288,6 +294,7 @@ int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void*
                     const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
                     int pos_host, int gate_per_head, void* q_out, uint32_t* k_q, void* k_s,
                     void* k_b, uint32_t* v_q, void* v_s, void* v_b, int cap, void* gate_out,
+                    const float* inv_freq, int rot_dims, float mscale, int ring, int row0,
                     void* stream);
 
 /*
@@ -302,7 +309,8 @@ int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void*
  * own CTA and the last CTA of each head to finish runs that head's prologue. The workspace
  * (lg_decode_qkv_prep_workspace_bytes) holds one counter per head; it must start zeroed and
  * completed calls leave it so. D % 64 == 0, D <= 256; LG_ERR_UNSUPPORTED when the projection's
- * tiles do not all fit on the GPU at once.
+ * tiles do not all fit on the GPU at once. inv_freq .. row0: RoPE and cache rows as in
+ * lg_attn_prep.
  */
 int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, const void* w_s,
                        const void* w_b, const void* norm_w, float eps, int Hq, int Hkv, int D,
@@ -310,6 +318,7 @@ int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, const void* w_
                        const int32_t* pos_dev, int pos_host, int gate_per_head, void* qkvg_out,
                        void* q_out, void* gate_out, void* k_cache, void* v_cache, uint32_t* k_q,
                        void* k_s, void* k_b, uint32_t* v_q, void* v_s, void* v_b, int cap,
+                       const float* inv_freq, int rot_dims, float mscale, int ring, int row0,
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes of lg_decode_qkv_prep (one counter per head slot). */

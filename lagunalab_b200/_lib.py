@@ -47,14 +47,16 @@ SIGNATURES = {
     "lg_rmsnorm": (c_int, [P, P, P, I, I, c_float, P, P, P]),
     "lg_qlinear": (c_int, [P, I, I, I, P, P, P, I, I, P, P, P]),
     "lg_embed": (c_int, [P, I, P, P, P, I, I, I, I, P, P]),
-    "lg_attn_prep": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, I, P, P]),
+    "lg_attn_prep": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, I, P,
+                             P, I, c_float, I, I, P]),
     "lg_bf16_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
     "lg_bf16_decode_attention": (c_int, [P, I, I, I, I, P, P, I, I, P, I, I, c_float, P, P, P,
                                          c_size_t, P]),
     "lg_argmax": (c_int, [P, I, I, P, P, I, P]),
     "lg_decode_gemv": (c_int, [P, I, I, P, P, P, P, P, P, P, c_float, P, P, P]),
     "lg_decode_qkv_prep": (c_int, [P, I, P, P, P, P, c_float, I, I, I, P, P, c_float, c_float, P,
-                                   I, I, P, P, P, P, P, P, P, P, P, P, P, I, P, c_size_t, P]),
+                                   I, I, P, P, P, P, P, P, P, P, P, P, P, I,
+                                   P, I, c_float, I, I, P, c_size_t, P]),
     "lg_decode_qkv_prep_workspace_bytes": (c_size_t, [I, I]),
     "lg_router_decode": (c_int, [P, P, c_float, I, P, P, P, P, I, I, I, I, P, P, P, P, P,
                                  c_size_t, P]),
@@ -64,7 +66,7 @@ SIGNATURES = {
     "lg_router_decode_supported": (c_int, [I, I]),
     "lg_decode_status": (c_int, [P, I]),
     "lg_attn_prep_q8": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, P, P, P,
-                                P, I, P, P]),
+                                P, I, P, P, I, c_float, I, I, P]),
     "lg_q8_decode_attention_dev": (c_int, [P, I, I, I, I, P, P, P, P, P, P, I, I, P, I, c_float,
                                            P, P, P, c_size_t, P]),
     "lg_ep_arena_bytes": (c_size_t, [I, I, I, I]),

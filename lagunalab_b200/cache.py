@@ -167,15 +167,17 @@ class DequantKVCache:
 def make_quantized_cache(model, bits=8, group_size=64, quantized_decode=False, fused_decode=False,
                          capacity=0):
     """laguna_mlx/cache.py:147-157: quantized K/V on full-attention layers (``capacity``
-    preallocates rows, as one-token steps replayed from a CUDA graph need). Sliding layers
-    are outside this build's scope (every BASELINE config uses full attention)."""
+    preallocates rows, as one-token steps replayed from a CUDA graph need); sliding-window
+    layers keep a bf16 ring of their window."""
     a = model.args
     if a.head_dim % group_size:
         raise ValueError(f"head_dim {a.head_dim} is not a multiple of group_size {group_size}")
+    from .laguna import RotatingKVCache
     caches = []
     for lt in a.layer_types:
-        if lt == "sliding_attention":
-            raise NotImplementedError("sliding-window layers are not part of this build")
+        if lt == "sliding_attention":  # sliding layers keep their bf16 window (cache.py:153)
+            caches.append(RotatingKVCache(a.sliding_window))
+            continue
         caches.append(DequantKVCache(group_size=group_size, bits=bits,
                                      quantized_decode=quantized_decode, fused_decode=fused_decode,
                                      capacity=capacity))

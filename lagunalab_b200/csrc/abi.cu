@@ -100,6 +100,6 @@ extern "C" int lg_event_elapsed_ms(void* ev_start, void* ev_end, float* ms) {
   return LG_OK;
 }
 
-extern "C" int lg_abi_version(void) { return 1; }
+extern "C" int lg_abi_version(void) { return 2; }
 
 extern "C" const char* lg_last_error(void) { return lg::g_err; }

@@ -794,7 +794,8 @@ extern "C" int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, con
                                   int pos_host, int gate_per_head, void* qkvg_out, void* q_out,
                                   void* gate_out, void* k_cache, void* v_cache, uint32_t* k_q,
                                   void* k_s, void* k_b, uint32_t* v_q, void* v_s, void* v_b,
-                                  int cap, void* workspace, size_t workspace_bytes,
+                                  int cap, const float* inv_freq, int rot_dims, float mscale,
+                                  int ring, int row0, void* workspace, size_t workspace_bytes,
                                   void* stream) {
   LG_CHECK_ARG(K > 0 && K % 64 == 0 && K <= 16384, "decode_qkv_prep: hidden %d", K);
   LG_CHECK_ARG(Hq > 0 && Hkv > 0 && D % 64 == 0 && D <= 256,
@@ -810,8 +811,11 @@ extern "C" int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, con
                "decode_qkv_prep: give either the bf16 cache or the 8-bit cache");
   LG_CHECK_ARG(aligned(x, 16) && aligned(norm_w, 16),
                "decode_qkv_prep: x and the norm weight must be 16-byte aligned");
-  LG_CHECK_ARG(pos_dev || (pos_host >= 0 && pos_host < cap),
-               "decode_qkv_prep: position %d beyond the cache capacity %d", pos_host, cap);
+  LG_CHECK_ARG(pos_dev || ring > 0 || (pos_host - row0 >= 0 && pos_host - row0 < cap),
+               "decode_qkv_prep: position %d beyond the cache rows %d..%d", pos_host, row0,
+               row0 + cap - 1);
+  LG_CHECK_ARG(ring == 0 || ring == cap, "decode_qkv_prep: a ring buffer has %d rows, not %d",
+               cap, ring);
   int rc = check_tile_mat(w_q, w_s, w_b, "decode_qkv_prep");
   if (rc) return rc;
   const size_t need = lg_decode_qkv_prep_workspace_bytes(Hq, Hkv);
@@ -830,6 +834,8 @@ extern "C" int lg_decode_qkv_prep(const void* x, int K, const uint32_t* w_q, con
   a.prep = 1;
   a.head_cnt = static_cast<unsigned int*>(workspace);
   PrepArgs p = {};
+  if (int rc2 = prep_extend(&p, D, inv_freq, rot_dims, mscale, ring, row0, "decode_qkv_prep"))
+    return rc2;
   p.qkvg = static_cast<const __nv_bfloat16*>(qkvg_out);
   p.qn_w = static_cast<const __nv_bfloat16*>(qn_w);
   p.kn_w = static_cast<const __nv_bfloat16*>(kn_w);

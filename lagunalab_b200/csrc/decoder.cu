@@ -336,16 +336,20 @@ static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const 
                          const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
                          int pos_host, int gate_per_head, void* q_out, void* k_cache,
                          void* v_cache, const uint32_t* const* q8, const void* const* q8sb,
-                         int cap, void* gate_out, void* stream) {
+                         int cap, void* gate_out, const float* inv_freq, int rot_dims,
+                         float mscale, int ring, int row0, void* stream) {
   LG_CHECK_ARG(D % 64 == 0 && D <= 256 && Hq > 0 && Hkv > 0 && T >= 0,
                "attn_prep: head_dim %d (need a multiple of 64, <= 256)", D);
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(qkvg && qn_w && kn_w && q_out && ((k_cache && v_cache) || q8) && gate_out,
                "attn_prep: NULL pointer");
-  LG_CHECK_ARG(pos_dev || (pos_host >= 0 && pos_host + T <= cap),
-               "attn_prep: positions %d..%d beyond the cache capacity %d", pos_host,
-               pos_host + T - 1, cap);
-  PrepArgs a;
+  LG_CHECK_ARG(pos_dev || ring > 0 || (pos_host - row0 >= 0 && pos_host - row0 + T <= cap),
+               "attn_prep: positions %d..%d beyond the cache rows %d..%d", pos_host,
+               pos_host + T - 1, row0, row0 + cap - 1);
+  LG_CHECK_ARG(ring == 0 || ring == cap, "attn_prep: a ring buffer has %d rows, not %d", cap,
+               ring);
+  PrepArgs a = {};
+  if (int rc = prep_extend(&a, D, inv_freq, rot_dims, mscale, ring, row0, "attn_prep")) return rc;
   a.qkvg = static_cast<const __nv_bfloat16*>(qkvg);
   a.qn_w = static_cast<const __nv_bfloat16*>(qn_w);
   a.kn_w = static_cast<const __nv_bfloat16*>(kn_w);
@@ -379,24 +383,28 @@ static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const 
 extern "C" int lg_attn_prep(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
                             const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
                             int pos_host, int gate_per_head, void* q_out, void* k_cache,
-                            void* v_cache, int cap, void* gate_out, void* stream) {
+                            void* v_cache, int cap, void* gate_out, const float* inv_freq,
+                            int rot_dims, float mscale, int ring, int row0, void* stream) {
   LG_CHECK_ARG(k_cache && v_cache, "attn_prep: NULL cache");
   return attn_prep_run(qkvg, T, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, pos_host,
                        gate_per_head, q_out, k_cache, v_cache, nullptr, nullptr, cap, gate_out,
-                       stream);
+                       inv_freq, rot_dims, mscale, ring, row0, stream);
 }
 
 extern "C" int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void* qn_w,
                                const void* kn_w, float eps, float rope_theta,
                                const int32_t* pos_dev, int pos_host, int gate_per_head,
                                void* q_out, uint32_t* k_q, void* k_s, void* k_b, uint32_t* v_q,
-                               void* v_s, void* v_b, int cap, void* gate_out, void* stream) {
+                               void* v_s, void* v_b, int cap, void* gate_out,
+                               const float* inv_freq, int rot_dims, float mscale, int ring,
+                               int row0, void* stream) {
   LG_CHECK_ARG(k_q && k_s && k_b && v_q && v_s && v_b, "attn_prep_q8: NULL cache");
   LG_CHECK_ARG(D <= 256, "attn_prep_q8: head_dim %d > 256", D);
   const uint32_t* q8[2] = {k_q, v_q};
   const void* sb[4] = {k_s, k_b, v_s, v_b};
   return attn_prep_run(qkvg, T, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, pos_host,
-                       gate_per_head, q_out, nullptr, nullptr, q8, sb, cap, gate_out, stream);
+                       gate_per_head, q_out, nullptr, nullptr, q8, sb, cap, gate_out, inv_freq,
+                       rot_dims, mscale, ring, row0, stream);
 }
 
 extern "C" int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,

@@ -16,8 +16,12 @@ namespace lg {
 //   k = rope(bf16(rmsnorm(k_h, kn_w)), p)  -> k_cache [Hkv, cap, D] row p
 //   v                                       -> v_cache row p
 //   gate = bf16(softplus(float(g)))         -> gate_out [T, Hq or Hq*D]
-// RoPE is the default non-interleaved form (pairs i, i + D/2; mx.fast.rope traditional=False)
-// with inv_freq_i = theta^(-2i/D), computed in fp32 with one bf16 rounding.
+// RoPE is the non-interleaved form (mx.fast.rope traditional=False) on the first R dims: pairs
+// (i, i + R/2), fp32 angles, one bf16 rounding, dims past R unchanged. Default: R = D and
+// inv_freq_i = theta^(-2i/D) computed in the kernel; otherwise (partial rotary, YaRN,
+// laguna.py:62-72) the caller's inv_freq table [R/2] and, when mscale != 1, the rotated dims
+// scaled by mscale and rounded to bf16 first (mlx-lm's YaRN layer).
+// Cache row of position p: p - row0, or p mod ring for a sliding-window ring buffer.
 // ---------------------------------------------------------------------------------------
 struct PrepArgs {
   const __nv_bfloat16* qkvg;
@@ -26,6 +30,11 @@ struct PrepArgs {
   const int* pos_dev;
   int pos_host, T, Hq, Hkv, D, cap, gate_per_head;
   float eps, log2_theta;
+  const float* inv_freq;  // [rot_half] (null: the default theta^(-2i/D), all D dims rotated)
+  int rot_half;           // R / 2: a multiple of 32 (0: D / 2)
+  float mscale;           // YaRN attention factor on the rotated dims (1: none)
+  int ring;               // > 0: cache row = position mod ring (sliding window)
+  int row0;               // linear caches: cache row = position - row0
   __nv_bfloat16* q_out;
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
@@ -37,6 +46,25 @@ struct PrepArgs {
   uint32_t* vq;
   __nv_bfloat16 *vs, *vb;
 };
+
+// Host side: the RoPE and cache-row extension of a prologue (partial rotary / YaRN table,
+// sliding-window ring). rot_dims 0 = all D dims with the default frequencies (inv_freq NULL);
+// otherwise a multiple of 64 up to D with a table of rot_dims / 2 frequencies.
+inline int prep_extend(PrepArgs* a, int D, const float* inv_freq, int rot_dims, float mscale,
+                       int ring, int row0, const char* who) {
+  if (rot_dims == 0) rot_dims = D;
+  LG_CHECK_ARG(rot_dims > 0 && rot_dims <= D && rot_dims % 64 == 0,
+               "%s: rotary dims %d must be a multiple of 64 up to head_dim %d", who, rot_dims, D);
+  LG_CHECK_ARG(inv_freq || (rot_dims == D && mscale == 1.0f),
+               "%s: partial rotary or YaRN needs a frequency table", who);
+  LG_CHECK_ARG(ring >= 0 && row0 >= 0, "%s: ring %d / row0 %d", who, ring, row0);
+  a->inv_freq = inv_freq;
+  a->rot_half = rot_dims / 2;
+  a->mscale = mscale;
+  a->ring = ring;
+  a->row0 = row0;
+  return LG_OK;
+}
 
 // Quantize the row that one warp holds (lane l: elements l + 32 k, k < 2P, so element k's group
 // of 64 is k / 2) into cache row `row` of an 8-bit g64 packed cache; the arithmetic of
@@ -76,6 +104,24 @@ __device__ __forceinline__ __nv_bfloat16 prep_gate(float g) {
   return __float2bfloat16_rn(fmaxf(g, 0.f) + log1pf(expf(-fabsf(g))));
 }
 
+// RoPE on the first 64 PR dims from the caller's frequency table: lane chunks j and j + PR
+// (elements l + 32 j and l + 32 (j + PR)) are the pair (i, i + 32 PR).
+template <int P, int PR>
+__device__ __forceinline__ void rope_table(float (&x)[2 * P], const PrepArgs& a, int pos, int l) {
+#pragma unroll
+  for (int j = 0; j < PR; ++j) {
+    float sn, cs;
+    sincosf((float)pos * a.inv_freq[l + 32 * j], &sn, &cs);
+    float n0 = x[j], n1 = x[j + PR];
+    if (a.mscale != 1.0f) {
+      n0 = round_bf16(n0 * a.mscale);
+      n1 = round_bf16(n1 * a.mscale);
+    }
+    x[j] = n0 * cs - n1 * sn;
+    x[j + PR] = n0 * sn + n1 * cs;
+  }
+}
+
 // One (token t, head slot) of the prologue, by one warp: slots [0, Hq) q heads, [Hq, Hq+Hkv)
 // k heads, [Hq+Hkv, Hq+2Hkv) v heads; D = 64 P. Lane l holds elements l + 32 k (k < 2P), so the
 // rotary pairs (i, i + D/2) are its own slots (k, k + P) and no barrier is needed. write_gate: a
@@ -87,19 +133,20 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
   constexpr int D = 64 * P;
   const int l = threadIdx.x & 31;
   const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
+  const int crow = a.ring > 0 ? pos % a.ring : pos - a.row0;  // the position's cache row
   const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
   const __nv_bfloat16* row = a.qkvg + (size_t)t * row_stride;
   float x[2 * P];
   if (slot >= a.Hq + a.Hkv) {  // v: into the cache as it is
     const int h = slot - a.Hq - a.Hkv;
     const __nv_bfloat16* src = row + (a.Hq + a.Hkv + h) * D;
-    if (pos >= a.cap) return;
+    if (crow < 0 || crow >= a.cap) return;
     if (a.vq) {
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) x[k] = bf2f(__ldcg(src + l + 32 * k));
-      quantize_row8_warp<P>(x, (size_t)h * a.cap + pos, a.vq, a.vs, a.vb, sb);
+      quantize_row8_warp<P>(x, (size_t)h * a.cap + crow, a.vq, a.vs, a.vb, sb);
     } else {
-      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + pos) * D;
+      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + crow) * D;
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __ldcg(src + l + 32 * k);
     }
@@ -119,15 +166,22 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
   const float rn = 1.0f / sqrtf(ss / (float)D + a.eps);
 #pragma unroll
   for (int k = 0; k < 2 * P; ++k) x[k] = round_bf16(round_bf16(x[k] * rn) * bf2f(nw[l + 32 * k]));
+  if (!a.inv_freq) {  // default RoPE over all D dims
 #pragma unroll
-  for (int j = 0; j < P; ++j) {
-    const int i = l + 32 * j;
-    const float inv_freq = exp2f(-(float)(2 * i) / (float)D * a.log2_theta);
-    float sn, cs;
-    sincosf((float)pos * inv_freq, &sn, &cs);
-    const float n0 = x[j], n1 = x[j + P];
-    x[j] = n0 * cs - n1 * sn;
-    x[j + P] = n0 * sn + n1 * cs;
+    for (int j = 0; j < P; ++j) {
+      const int i = l + 32 * j;
+      const float inv_freq = exp2f(-(float)(2 * i) / (float)D * a.log2_theta);
+      float sn, cs;
+      sincosf((float)pos * inv_freq, &sn, &cs);
+      const float n0 = x[j], n1 = x[j + P];
+      x[j] = n0 * cs - n1 * sn;
+      x[j + P] = n0 * sn + n1 * cs;
+    }
+  } else {  // the first 2 * rot_half dims with table frequencies
+    const int Pr = a.rot_half / 32;
+    if (Pr == 1) rope_table<P, 1>(x, a, pos, l);
+    if constexpr (P >= 2) if (Pr == 2) rope_table<P, 2>(x, a, pos, l);
+    if constexpr (P >= 4) if (Pr == 4) rope_table<P, 4>(x, a, pos, l);
   }
   if (is_q) {
     __nv_bfloat16* dst = a.q_out + ((size_t)h * a.T + t) * D;
@@ -144,13 +198,13 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
           go[l + 32 * k] = prep_gate(bf2f(__ldcg(g + h * D + l + 32 * k)));
       }
     }
-  } else if (pos < a.cap) {
+  } else if (crow >= 0 && crow < a.cap) {
     if (a.kq) {
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) x[k] = round_bf16(x[k]);
-      quantize_row8_warp<P>(x, (size_t)h * a.cap + pos, a.kq, a.ks, a.kb, sb);
+      quantize_row8_warp<P>(x, (size_t)h * a.cap + crow, a.kq, a.ks, a.kb, sb);
     } else {
-      __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + pos) * D;
+      __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + crow) * D;
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __float2bfloat16_rn(x[k]);
     }

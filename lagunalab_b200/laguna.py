@@ -361,6 +361,97 @@ class KVCache:
         return 0 if self.keys is None else 2 * self.keys.numel() * self.keys.element_size()
 
 
+def rope_setup(p, head_dim, device):
+    """A layer type's RoPE for the prologue kernels (laguna.py:62-72): None for the default
+    rope over every head dim (the kernel computes theta^(-2i/D) itself), else (inv_freq fp32
+    [R/2] on ``device``, R, mscale) for partial rotary (R = head_dim * partial_rotary_factor)
+    and/or YaRN scaling. YaRN (Peng et al., "YaRN: Efficient Context Window Extension of Large
+    Language Models", 2023): frequencies whose wavelength exceeds the original context
+    (below ``beta_slow`` rotations over it) are divided by ``factor``, those above
+    ``beta_fast`` rotations are kept, a linear ramp in between; the rotated dims are scaled by
+    ``attention_factor`` (default 0.1 ln(factor) + 1)."""
+    R = int(head_dim * p.get("partial_rotary_factor", 1.0))
+    kind = p.get("rope_type", "default")
+    if kind == "default" and R == head_dim:
+        return None
+    if R % 64 or R <= 0:
+        raise NotImplementedError(f"rotary dims {R}: the prologue kernels rotate multiples of 64")
+    theta = float(p["rope_theta"])
+    exps = [2.0 * i / R for i in range(R // 2)]
+    base_freq = [theta ** -e for e in exps]
+    mscale = 1.0
+    if kind == "yarn":
+        factor = float(p["factor"])
+        ctx = float(p.get("original_max_position_embeddings", 4096))
+        fast, slow = float(p.get("beta_fast", 32.0)), float(p.get("beta_slow", 1.0))
+
+        def dim_of(rotations):  # the dim whose wavelength fits `rotations` times into ctx
+            return R * math.log(ctx / (2 * math.pi * rotations)) / (2 * math.log(theta))
+
+        lo, hi = max(math.floor(dim_of(fast)), 0), min(math.ceil(dim_of(slow)), R - 1)
+        width = (hi - lo) if hi != lo else 0.001
+        freqs = []
+        for i, f in enumerate(base_freq):
+            keep = 1.0 - min(max((i - lo) / width, 0.0), 1.0)  # 1: original, 0: interpolated
+            freqs.append(f * keep + (f / factor) * (1.0 - keep))
+        base_freq = freqs
+        ms = p.get("attention_factor")
+        mscale = float(ms) if ms is not None else (0.1 * math.log(factor) + 1.0 if factor > 1
+                                                   else 1.0)
+    elif kind != "default":
+        raise NotImplementedError(f"rope_type {kind!r}")
+    inv = torch.tensor(base_freq, dtype=torch.float64).to(torch.float32).to(device)
+    return inv, R, mscale
+
+
+class RotatingKVCache:
+    """mlx-lm RotatingKVCache surface for sliding-window layers (laguna.py:209-214): the last
+    ``max_size`` keys/values in a bf16 ring buffer [B, Hkv, max_size, D] (row = position mod
+    max_size); ``offset`` counts every token seen. Attention over the ring is order-free
+    (each key carries its own rotary position), so decode attends the filled rows as they
+    lie."""
+
+    def __init__(self, max_size, keep=0):
+        if keep:
+            raise NotImplementedError("keep > 0 (attention sinks) is not supported")
+        self.max_size = int(max_size)
+        self.keys = self.values = None
+        self.offset = 0
+
+    def reserve(self, B, Hkv, D, device):
+        if self.keys is None:
+            self.keys = torch.zeros(B, Hkv, self.max_size, D, dtype=torch.bfloat16, device=device)
+            self.values = torch.zeros_like(self.keys)
+
+    def window_rows(self):
+        """Ring rows of the last min(offset, max_size) positions, oldest first."""
+        n = min(self.offset, self.max_size)
+        pos = torch.arange(self.offset - n, self.offset, device=self.keys.device)
+        return pos % self.max_size
+
+    @property
+    def state(self):
+        if self.keys is None:
+            return None, None
+        r = self.window_rows()
+        return self.keys[:, :, r], self.values[:, :, r]
+
+    def is_trimmable(self):
+        return self.offset < self.max_size
+
+    def trim(self, n):
+        n = min(self.offset, n) if self.offset < self.max_size else 0
+        self.offset -= n
+        return n
+
+    def empty(self):
+        return self.keys is None
+
+    @property
+    def nbytes(self):
+        return 0 if self.keys is None else 2 * self.keys.numel() * self.keys.element_size()
+
+
 def _concat_rows(mats):
     """Row-concatenate MLX-layout matrices (words, scales, biases) with the same K."""
     return tuple(torch.cat([m[i] for m in mats], dim=0).contiguous() for i in range(3))
@@ -380,14 +471,14 @@ class Attention:
         self.scale = hd ** -0.5
         self.per_head_gate = args.gating == "per-head"
         lt = args.layer_types[layer_idx]
-        if lt != "full_attention":
-            raise NotImplementedError("sliding-window layers are not supported on this path")
+        self.window = args.sliding_window if lt == "sliding_attention" else None
+        if lt == "sliding_attention" and not self.window:
+            raise ValueError("a sliding-window layer needs args.sliding_window")
         rp = args.rope_for(lt)
-        if rp.get("rope_type", "default") != "default" or rp.get("partial_rotary_factor", 1.0) != 1.0:
-            raise NotImplementedError("only the default full-rotary RoPE is supported")
         self.rope_theta = float(rp["rope_theta"])
         self.eps = args.rms_norm_eps
         dev = q_proj.weight.device
+        self.rope = rope_setup(rp, hd, dev)  # None: the default rope over every head dim
         self.q_norm = q_norm or RMSNorm(hd, args.rms_norm_eps, device=dev)
         self.k_norm = k_norm or RMSNorm(hd, args.rms_norm_eps, device=dev)
         mats = [q_proj.mat, k_proj.mat, v_proj.mat, g_proj.mat]
@@ -423,7 +514,11 @@ class Attention:
         else:
             qkvg = self._qkvg(in_norm(x).reshape(L, H))
         if cache is None:
-            cache = KVCache()
+            cache = RotatingKVCache(self.window) if self.window else KVCache()
+        if isinstance(cache, RotatingKVCache):
+            o = self._window_attention(qkvg, L, cache, pos_dev, x.device)
+            out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
+            return out.reshape(B, L, H)
         if getattr(cache, "q", None) is not None:  # 8-bit quantized cache (DequantKVCache)
             o = self._q8_attention(qkvg, L, cache, pos_dev, x.device)
             out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
@@ -433,7 +528,8 @@ class Attention:
                 raise ValueError("device-position steps are single-token steps on a sized cache")
             q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
                                     self.eps, self.rope_theta, cache.keys[0], cache.values[0],
-                                    pos_dev=pos_dev, gate_per_head=self.per_head_gate)
+                                    pos_dev=pos_dev, gate_per_head=self.per_head_gate,
+                                    rope=self.rope)
             o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, 0,
                                           self.scale, gate=gate if self.per_head_gate else None,
                                           n_dev=pos_dev, n_add=1)
@@ -446,7 +542,7 @@ class Attention:
         pos = cache.offset
         q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
                                 self.eps, self.rope_theta, cache.keys[0], cache.values[0],
-                                pos=pos, gate_per_head=self.per_head_gate)
+                                pos=pos, gate_per_head=self.per_head_gate, rope=self.rope)
         cache.offset += L
         if L == 1:
             o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, pos + 1,
@@ -484,14 +580,17 @@ class Attention:
             qc.reserve(1, Hkv, D, 1, x.device)
             ck, cv = qc.keys, qc.values
         else:
+            if isinstance(cache, RotatingKVCache):
+                cache.reserve(1, Hkv, D, x.device)
             if cache.keys is None:
                 return None
             ck, cv = cache.keys[0], cache.values[0]
+        ring = cache.max_size if isinstance(cache, RotatingKVCache) else 0
         try:
             _, q, gate = ops.decode_qkv_prep(x, self._qkvg.mat, (in_norm.weight, in_norm.eps),
                                              Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
                                              self.eps, self.rope_theta, ck, cv, pos_dev=pos_dev,
-                                             gate_per_head=per_head)
+                                             gate_per_head=per_head, rope=self.rope, ring=ring)
         except _lib.LagunaError as e:
             if e.code != _lib.LG_ERR_UNSUPPORTED:
                 raise
@@ -509,6 +608,58 @@ class Attention:
             o = o * gate.view(1, Hq * D)
         return self.o_proj(o, residual=None if residual is None else residual.reshape(1, -1))
 
+    def _window_attention(self, qkvg, L, cache, pos_dev, device):
+        """Sliding-window attention over a RotatingKVCache (laguna.py:183-186, :209-214): a
+        query at position p sees the keys of positions p - W < j <= p. Single-token steps write
+        the new row into the ring (row = p mod W) and attend its filled rows; multi-token steps
+        attend over the window's previous rows and the new ones with a window mask, then keep
+        the last W rows in the ring."""
+        Hq, Hkv, D, W = self.n_heads, self.n_kv_heads, self.head_dim, cache.max_size
+        per_head = self.per_head_gate
+        cache.reserve(1, Hkv, D, device)
+        kr, vr = cache.keys[0], cache.values[0]
+        if L == 1:
+            pos = cache.offset
+            q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                    self.eps, self.rope_theta, kr, vr, pos=pos, pos_dev=pos_dev,
+                                    gate_per_head=per_head, rope=self.rope, ring=W)
+            g = gate if per_head else None
+            if pos_dev is not None:  # the valid rows min(p + 1, W): the kernel clamps to cap
+                o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values, 0,
+                                              self.scale, gate=g, n_dev=pos_dev, n_add=1)
+            else:
+                cache.offset += 1
+                o = ops.bf16_decode_attention(q.view(1, Hq, D), cache.keys, cache.values,
+                                              min(pos + 1, W), self.scale, gate=g)
+            o = o.view(1, Hq * D)
+            return o if per_head else o * gate.view(1, Hq * D)
+        if pos_dev is not None:
+            raise ValueError("device-position steps are single-token steps")
+        pos = cache.offset
+        n_prev = min(pos, W)
+        kt = torch.empty(Hkv, n_prev + L, D, dtype=torch.bfloat16, device=device)
+        vt = torch.empty_like(kt)
+        if n_prev:
+            rows = cache.window_rows()
+            kt[:, :n_prev] = kr[:, rows]
+            vt[:, :n_prev] = vr[:, rows]
+        q, gate = ops.attn_prep(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                self.eps, self.rope_theta, kt, vt, pos=pos,
+                                gate_per_head=per_head, rope=self.rope, row0=pos - n_prev)
+        qi = torch.arange(L, device=device)[:, None] + n_prev
+        kj = torch.arange(n_prev + L, device=device)[None, :]
+        mask = (kj <= qi) & (kj > qi - W)
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q.unsqueeze(0), kt.unsqueeze(0), vt.unsqueeze(0), attn_mask=mask, scale=self.scale,
+            enable_gqa=True)[0].transpose(0, 1)  # [L, Hq, D]
+        keep = min(W, n_prev + L)
+        newpos = torch.arange(pos + L - keep, pos + L, device=device)
+        kr[:, newpos % W] = kt[:, n_prev + L - keep:]
+        vr[:, newpos % W] = vt[:, n_prev + L - keep:]
+        cache.offset = pos + L
+        g = gate[..., None] if per_head else gate.view(L, Hq, D)
+        return (o * g).reshape(L, Hq * D)
+
     def _q8_attention(self, qkvg, L, cache, pos_dev, device):
         """Attention over an 8-bit group-64 DequantKVCache (laguna_mlx/cache.py:89-106): the new
         k, v rows are quantized into the packed cache; single-token steps with ``fused_decode``
@@ -523,7 +674,7 @@ class Attention:
                 raise ValueError("device-position steps are fused single-token steps")
             q, gate = ops.attn_prep_q8(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
                                        self.eps, self.rope_theta, qc.keys, qc.values,
-                                       pos_dev=pos_dev, gate_per_head=per_head)
+                                       pos_dev=pos_dev, gate_per_head=per_head, rope=self.rope)
             o = ops.q8_decode_attention_dev(q.view(1, Hq, D), qc.keys, qc.values, cap, pos_dev,
                                             1, self.scale, gate=gate if per_head else None)
             o = o.view(1, Hq * D)
@@ -531,7 +682,7 @@ class Attention:
         pos = qc.offset
         q, gate = ops.attn_prep_q8(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
                                    self.eps, self.rope_theta, qc.keys, qc.values, pos=pos,
-                                   gate_per_head=per_head)
+                                   gate_per_head=per_head, rope=self.rope)
         qc.offset += L
         n = pos + L
         cache.fused_step = cache.fused_decode and L == 1
@@ -648,10 +799,10 @@ class Model:
         return self.model.layers
 
     def make_cache(self, capacity=0):
-        for lt in self.args.layer_types:
-            if lt == "sliding_attention":
-                raise NotImplementedError("sliding-window layers are not supported on this path")
-        return [KVCache(capacity) for _ in self.args.layer_types]
+        """laguna.py:209-214: a ring of the window for sliding-window layers, a growing cache
+        (``capacity`` rows preallocated) for full-attention layers."""
+        return [RotatingKVCache(self.args.sliding_window) if lt == "sliding_attention"
+                else KVCache(capacity) for lt in self.args.layer_types]
 
     def sanitize(self, weights):
         """laguna.py:216-228 on a dict of tensors: per-expert weights stacked into
@@ -789,8 +940,13 @@ class DecodeGraph:
         self.model, self.cache = model, cache
         self.tok = tok.reshape(1).to(torch.int32).clone()
         self.pos = torch.tensor([cache[0].offset], dtype=torch.int32, device=self.tok.device)
-        c0 = cache[0]
-        self.cap = c0.q.keys[0].shape[2] if getattr(c0, "q", None) is not None else c0.keys.shape[2]
+        full = [c for c in cache if not isinstance(c, RotatingKVCache)]
+        if full:
+            c0 = full[0]
+            self.cap = (c0.q.keys[0].shape[2] if getattr(c0, "q", None) is not None
+                        else c0.keys.shape[2])
+        else:  # only sliding windows: rings never fill up
+            self.cap = 1 << 30
         self.steps = 0
         self._body()  # one real step, eagerly
         self.first_logits = self.logits.clone()  # that step's logits (the capture reuses names)

@@ -356,7 +356,7 @@ def decode_gemv(x, mat, norm=None, residual=None, up=None, out=None, group_size=
 
 
 def decode_qkv_prep(x, mat, norm, Hq, Hkv, D, qn_w, kn_w, qk_eps, theta, cache_k, cache_v,
-                    pos=0, pos_dev=None, gate_per_head=True):
+                    pos=0, pos_dev=None, gate_per_head=True, rope=None, ring=0, row0=0):
     """One token's q/k/v/g projection (input RMSNorm ``norm=(weight, eps)`` fused in) and its
     attention prologue in one launch; returns (qkvg [1, N], q [Hq, 1, D], gate). ``cache_k`` /
     ``cache_v``: the bf16 cache [Hkv, cap, D] tensors, or the 8-bit cache's (words, scales,
@@ -387,7 +387,8 @@ def decode_qkv_prep(x, mat, norm, Hq, Hkv, D, qn_w, kn_w, qk_eps, theta, cache_k
               _p(_c(norm[0], torch.bfloat16)), float(norm[1]), Hq, Hkv, D, _p(_c(qn_w)),
               _p(_c(kn_w)), float(qk_eps), float(theta), _p(pos_dev), int(pos),
               int(bool(gate_per_head)), _p(qkvg), _p(q), _p(gate), _p(kc), _p(vc), _p(kq),
-              _p(ks), _p(kb), _p(vq), _p(vs), _p(vb), cap, _p(ws), ws.numel(), _stream(dev))
+              _p(ks), _p(kb), _p(vq), _p(vs), _p(vb), cap, *_rope_args(rope, ring, row0),
+              _p(ws), ws.numel(), _stream(dev))
     return qkvg, q, gate
 
 
@@ -476,10 +477,23 @@ def embed(ids, mat, group_size=64, bits=4):
     return out
 
 
+def _rope_args(rope, ring, row0):
+    """(inv_freq pointer, rotated dims, mscale, ring, row0) for the prologue entry points.
+    ``rope``: None (default RoPE over all dims) or (inv_freq fp32 CUDA tensor [R/2], R,
+    mscale)."""
+    if rope is None:
+        return None, 0, 1.0, int(ring), int(row0)
+    inv, R, ms = rope
+    return _p(_c(inv, torch.float32)), int(R), float(ms), int(ring), int(row0)
+
+
 def attn_prep(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos=0, pos_dev=None,
-              gate_per_head=True):
+              gate_per_head=True, rope=None, ring=0, row0=0):
     """From fused q|k|v|g projections [T, .] write k, v rows into the caches [Hkv, cap, D] at
-    positions pos + t and return (q [Hq, T, D] normed + roped, gate [T, Hq or Hq*D])."""
+    positions pos + t and return (q [Hq, T, D] normed + roped, gate [T, Hq or Hq*D]).
+    ``rope``: (inv_freq, rotated dims, mscale) for partial rotary / YaRN (laguna.py:62-72);
+    ``ring`` > 0: the caches are a sliding window's ring (row = position mod ring); else row =
+    position - ``row0``."""
     qkvg = _c(qkvg, torch.bfloat16)
     T = qkvg.shape[0]
     cap = k_cache.shape[-2]
@@ -487,12 +501,12 @@ def attn_prep(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos=0,
     gate = torch.empty(T, Hq if gate_per_head else Hq * D, dtype=torch.bfloat16, device=qkvg.device)
     _lib.call("lg_attn_prep", _p(qkvg), T, Hq, Hkv, D, _p(_c(qn_w)), _p(_c(kn_w)), float(eps),
               float(theta), _p(pos_dev), int(pos), int(bool(gate_per_head)), _p(q), _p(k_cache),
-              _p(v_cache), cap, _p(gate), _stream(qkvg.device))
+              _p(v_cache), cap, _p(gate), *_rope_args(rope, ring, row0), _stream(qkvg.device))
     return q, gate
 
 
 def attn_prep_q8(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, keys, values, pos=0, pos_dev=None,
-                 gate_per_head=True):
+                 gate_per_head=True, rope=None, ring=0, row0=0):
     """attn_prep with an 8-bit group-64 cache: the new k, v rows are quantized into rows
     pos + t of the packed caches keys/values = (words [B=1, Hkv, cap, D/4], scales, biases)."""
     qkvg = _c(qkvg, torch.bfloat16)
@@ -505,7 +519,7 @@ def attn_prep_q8(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, keys, values, pos=0, 
     _lib.call("lg_attn_prep_q8", _p(qkvg), T, Hq, Hkv, D, _p(_c(qn_w)), _p(_c(kn_w)), float(eps),
               float(theta), _p(pos_dev), int(pos), int(bool(gate_per_head)), _p(q),
               _p(kq), _p(ks), _p(kb), _p(vq), _p(vs), _p(vb), cap, _p(gate),
-              _stream(qkvg.device))
+              *_rope_args(rope, ring, row0), _stream(qkvg.device))
     return q, gate
 
 

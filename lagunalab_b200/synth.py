@@ -106,7 +106,8 @@ def gateup_flops(T, k, H, I, I_sh):
 
 def decoder_args(vocab=100352, hidden=2048, layers=40, heads=32, kv_heads=4, head_dim=128,
                  experts=64, top_k=8, moe_inter=1024, shared_inter=1024, dense_inter=8192,
-                 rope_theta=1e6, routed_scale=2.5, gating="per-head"):
+                 rope_theta=1e6, routed_scale=2.5, gating="per-head", layer_types=None,
+                 sliding_window=None, rope_parameters=None, heads_per_layer=None):
     """ModelArgs of a Laguna decoder; the defaults are BASELINE config 3 (the 50%-pruned
     model: 64 experts per layer, top-8, 40 layers, hidden 2048, GQA 32/4, head_dim 128,
     layer 0 dense with intermediate 8192, vocabulary 100,352, RoPE theta 1e6)."""
@@ -116,8 +117,10 @@ def decoder_args(vocab=100352, hidden=2048, layers=40, heads=32, kv_heads=4, hea
         num_key_value_heads=kv_heads, head_dim=head_dim, rms_norm_eps=1e-6, num_experts=experts,
         num_experts_per_tok=top_k, moe_intermediate_size=moe_inter,
         shared_expert_intermediate_size=shared_inter,
-        rope_parameters={"rope_type": "default", "rope_theta": rope_theta},
-        mlp_only_layers=[0], moe_routed_scaling_factor=routed_scale, gating=gating)
+        rope_parameters=rope_parameters or {"rope_type": "default", "rope_theta": rope_theta},
+        mlp_only_layers=[0], moe_routed_scaling_factor=routed_scale, gating=gating,
+        layer_types=layer_types, sliding_window=sliding_window,
+        num_attention_heads_per_layer=heads_per_layer)
 
 
 _M32 = 0xFFFFFFFF
@@ -322,9 +325,18 @@ def oracle_weights(model):
 
 
 def oracle_args(args):
+    """The CPU oracle's model arguments: per layer the RoPE parameters (None where the default
+    rope rotates every head dim), their theta and the sliding window (None on full layers)."""
+    rps = [args.rope_for(lt) for lt in args.layer_types]
+    plain = lambda p: (p.get("rope_type", "default") == "default"
+                       and p.get("partial_rotary_factor", 1.0) == 1.0)
     return dict(head_dim=args.head_dim, heads=list(args.num_attention_heads_per_layer),
                 kv_heads=args.num_key_value_heads, eps=args.rms_norm_eps,
                 rope_theta=float(args.rope_for("full_attention")["rope_theta"]),
+                rope_thetas=[float(p["rope_theta"]) for p in rps],
+                rope=[None if plain(p) else dict(p) for p in rps],
+                window=[args.sliding_window if lt == "sliding_attention" else None
+                        for lt in args.layer_types],
                 gating="per-head" if args.gating == "per-head" else "element",
                 k=args.num_experts_per_tok, routed_scale=args.moe_routed_scaling_factor,
                 norm_topk_prob=args.norm_topk_prob)

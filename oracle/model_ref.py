@@ -44,18 +44,68 @@ def rmsnorm(x, w, eps):
     return _bf(_bf(xf * r) * w.to(torch.float32))
 
 
-def rope(x, pos0, theta):
-    """Default RoPE (laguna.py:69-72; mx.fast.rope, traditional=False): pairs (i, i + D/2),
-    inv_freq_i = theta^(-2i/D), positions pos0 + t along dim -2. fp32, one bf16 rounding."""
+def rope_params(p, head_dim):
+    """(rotated dims R, inv_freq fp32 [R/2], mscale) of one layer type's RoPE parameters.
+
+    default (laguna.py:69-72 -> mx.fast.rope): inv_freq_i = theta^(-2i/R).
+    yarn (YaRN, Peng et al. 2023, as transformers 5.5's ``_compute_yarn_parameters`` computes
+    it for the vendored PyTorch model): per frequency, a linear ramp between the
+    ``factor``-interpolated and the original frequency over the dims whose wavelength falls
+    between ``beta_fast`` and ``beta_slow`` rotations of ``original_max_position_embeddings``;
+    mscale = ``attention_factor`` (default 0.1 ln(factor) + 1).
+    ``partial_rotary_factor`` f rotates the first R = int(head_dim * f) dims only."""
+    R = int(head_dim * p.get("partial_rotary_factor", 1.0))
+    base = float(p["rope_theta"])
+    idx = torch.arange(0, R, 2, dtype=torch.float64)
+    if p.get("rope_type", "default") == "default":
+        return R, (base ** (-idx / R)).to(torch.float32), 1.0
+    if p["rope_type"] != "yarn":
+        raise NotImplementedError(p["rope_type"])
+    factor = float(p["factor"])
+    orig = float(p.get("original_max_position_embeddings", 4096))
+    fast, slow = float(p.get("beta_fast", 32.0)), float(p.get("beta_slow", 1.0))
+    mscale = p.get("attention_factor")
+    if mscale is None:
+        mscale = 0.1 * math.log(factor) + 1.0 if factor > 1 else 1.0
+
+    def corr_dim(rot):
+        return R * math.log(orig / (rot * 2 * math.pi)) / (2 * math.log(base))
+
+    lo = max(math.floor(corr_dim(fast)), 0)
+    hi = min(math.ceil(corr_dim(slow)), R - 1)
+    if lo == hi:
+        hi += 0.001
+    ramp = ((torch.arange(R // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0, 1)
+    extra = 1 - ramp  # weight of the original (extrapolated) frequency
+    pos_freq = base ** (idx / R)
+    inv = (1 / (factor * pos_freq)) * (1 - extra) + (1 / pos_freq) * extra
+    return R, inv.to(torch.float32), float(mscale)
+
+
+def rope(x, pos0, theta, R=None, inv=None, mscale=1.0):
+    """RoPE of the mlx-lm layer (laguna.py:62-72, 99-100; mx.fast.rope, traditional=False):
+    pairs (i, i + R/2) of the first R dims, positions pos0 + t along dim -2, fp32 angles and
+    one bf16 rounding; dims past R pass through. Default: R = D, inv_freq_i = theta^(-2i/D).
+    mscale != 1 (YaRN) scales the rotated dims first, rounded to the input's bf16 as
+    mlx-lm's YaRN layer does before its fast rope."""
     D = x.shape[-1]
-    half = D // 2
-    i = torch.arange(half, dtype=torch.float32, device=x.device)
-    inv = torch.exp2(-(2.0 * i) / D * math.log2(theta))
+    R = D if R is None else R
+    half = R // 2
+    if inv is None:
+        i = torch.arange(half, dtype=torch.float32, device=x.device)
+        inv = torch.exp2(-(2.0 * i) / R * math.log2(theta))
+    inv = inv.to(device=x.device, dtype=torch.float32)
     pos = torch.arange(x.shape[-2], dtype=torch.float32, device=x.device) + float(pos0)
     ang = pos[:, None] * inv[None, :]
     c, s = torch.cos(ang), torch.sin(ang)
-    x1, x2 = x[..., :half].to(torch.float32), x[..., half:].to(torch.float32)
-    return _bf(torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1))
+    xr = x[..., :R].to(torch.float32)
+    if mscale != 1.0:
+        xr = _bf(xr * mscale)
+    x1, x2 = xr[..., :half], xr[..., half:]
+    out = torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1)
+    if R < D:
+        out = torch.cat([out, x[..., R:].to(torch.float32)], dim=-1)
+    return _bf(out)
 
 
 def softplus(x):
@@ -63,11 +113,12 @@ def softplus(x):
     return torch.clamp(x, min=0) + torch.log1p(torch.exp(-x.abs()))
 
 
-def sdpa(q, k, v, scale, q_pos0, q_chunk=512):
+def sdpa(q, k, v, scale, q_pos0, q_chunk=512, window=None):
     """Causal attention for queries at positions q_pos0 + t over keys 0..S-1 (fp32, GQA),
-    output rounded to bf16. q [Hq, T, D], k/v [Hkv, S, D]. Rows of queries are independent,
-    so long prompts are processed ``q_chunk`` queries at a time (same values, bounded
-    memory)."""
+    output rounded to bf16. q [Hq, T, D], k/v [Hkv, S, D]. ``window`` W (sliding-window
+    layers, laguna.py:183-186): a query at p sees keys p - W < j <= p only. Rows of queries
+    are independent, so long prompts are processed ``q_chunk`` queries at a time (same
+    values, bounded memory)."""
     Hq, T, D = q.shape
     Hkv, S, _ = k.shape
     G = Hq // Hkv
@@ -80,7 +131,10 @@ def sdpa(q, k, v, scale, q_pos0, q_chunk=512):
         qc = q[:, a:b].to(torch.float32).reshape(Hkv, G * (b - a), D)
         s = (qc @ kk.transpose(1, 2)).view(Hkv, G, b - a, S) * scale
         qpos = torch.arange(a, b, device=q.device)[:, None] + q_pos0
-        s = s.masked_fill(kpos > qpos, float("-inf"))
+        hide = kpos > qpos
+        if window:
+            hide = hide | (kpos <= qpos - window)
+        s = s.masked_fill(hide, float("-inf"))
         pr = torch.softmax(s, dim=-1).view(Hkv, G * (b - a), S)
         out[:, a:b] = (pr @ vv).view(Hq, b - a, D)
     return _bf(out)
@@ -105,11 +159,16 @@ class Cache:
         self.kv_bits = kv_bits
         self.capacity = capacity
 
-    def _qdq(self, x):
+    def _bits(self, i):
+        """KV bits of layer i: ``kv_bits`` may be a per-layer list (None: bf16 rows, as the
+        sliding-window layers of a quantized cache keep, laguna_mlx/cache.py:147-157)."""
+        return self.kv_bits[i] if isinstance(self.kv_bits, (list, tuple)) else self.kv_bits
+
+    def _qdq(self, x, bits):
         from . import attn_ref, mlx_quant
-        packed, s_bits, b_bits = attn_ref.quantize_rows(x.cpu().numpy(), 64, self.kv_bits)
+        packed, s_bits, b_bits = attn_ref.quantize_rows(x.cpu().numpy(), 64, bits)
         return torch.from_numpy(mlx_quant.dequantize(packed, s_bits, b_bits, 64,
-                                                     self.kv_bits)).to(x.device)
+                                                     bits)).to(x.device)
 
     def _room(self, i, Hkv, D, need, device="cpu"):
         buf = self.kb[i]
@@ -143,8 +202,9 @@ class Cache:
         return [None if b is None else b[:, :n] for b, n in zip(self.vb, self.n)]
 
     def update(self, i, k, v):
-        if self.kv_bits:
-            k, v = self._qdq(k), self._qdq(v)
+        bits = self._bits(i)
+        if bits:
+            k, v = self._qdq(k, bits), self._qdq(v, bits)
         Hkv, T, D = k.shape
         n0 = self.n[i]
         self._room(i, Hkv, D, n0 + T, k.device)
@@ -152,7 +212,7 @@ class Cache:
         self.vb[i][:, n0:n0 + T] = v
         self.n[i] = n0 + T
         ck, cv = self.kb[i][:, :n0 + T], self.vb[i][:, :n0 + T]
-        if self.kv_bits and T > 1:
+        if bits and T > 1:
             return _bf(ck), _bf(cv)
         return ck, cv
 
@@ -167,11 +227,20 @@ def _attention(L, x, cache, i, args, pos0, lin):
     v = lin(x, L["v"]).view(T, Hkv, D).transpose(0, 1)
     q = rmsnorm(q, L["q_norm"], eps)
     k = rmsnorm(k, L["k_norm"], eps)
-    q = rope(q, pos0, args["rope_theta"])
-    k = rope(k, pos0, args["rope_theta"])
+    rp = args.get("rope", [None] * (i + 1))[i]
+    if isinstance(rp, dict):
+        rp = rope_params(rp, D)
+    if rp is None:
+        theta = args.get("rope_thetas", [args["rope_theta"]] * (i + 1))[i]
+        q = rope(q, pos0, theta)
+        k = rope(k, pos0, theta)
+    else:
+        q = rope(q, pos0, None, *rp)
+        k = rope(k, pos0, None, *rp)
     if cache is not None:
         k, v = cache.update(i, k, v)
-    o = sdpa(q, k, v, D ** -0.5, pos0).transpose(0, 1)  # [T, Hq, D]
+    window = args.get("window", [None] * (i + 1))[i]
+    o = sdpa(q, k, v, D ** -0.5, pos0, window=window).transpose(0, 1)  # [T, Hq, D]
     g = _bf(softplus(lin(x, L["g"]).to(torch.float32)))
     g = g[..., None] if args["gating"] == "per-head" else g.view(T, Hq, D)
     return lin(_bf(o * g).reshape(T, Hq * D), L["o"])
@@ -302,19 +371,23 @@ def _rms32(x, w, eps):
     return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * w
 
 
-def _rope32(x, pos0, theta):
+def _rope32(x, pos0, theta, R=None, inv=None, mscale=1.0):
+    """The vendored PyTorch model's RoPE (modeling_laguna.py:68-128, :277-312): cos and sin of
+    position x inv_freq times the attention scaling, rotate_half over the first R dims."""
     D = x.shape[-1]
-    half = D // 2
-    inv = 1.0 / (theta ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    R = D if R is None else R
+    half = R // 2
+    if inv is None:
+        inv = 1.0 / (theta ** (torch.arange(0, R, 2, dtype=torch.float32) / R))
     pos = torch.arange(x.shape[-2], dtype=torch.float32) + float(pos0)
     ang = pos[:, None] * inv[None, :]
-    c, s = torch.cos(ang), torch.sin(ang)
-    x1, x2 = x[..., :half], x[..., half:]
-    return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1)
+    c, s = torch.cos(ang) * mscale, torch.sin(ang) * mscale
+    x1, x2 = x[..., :half], x[..., half:R]
+    return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c, x[..., R:]], dim=-1)
 
 
-def forward_fp32(W, args, ids):
-    """fp32 logits [T, V] of a whole sequence from position 0 (no cache)."""
+def forward_fp32(W, args, ids, pos0=0):
+    """fp32 logits [T, V] of a whole sequence at positions pos0 + t (no cache)."""
     ids = torch.as_tensor(ids, dtype=torch.int64)
     T = ids.shape[0]
     eps, D = args["eps"], args["head_dim"]
@@ -325,11 +398,16 @@ def forward_fp32(W, args, ids):
         q = (xn @ L["q"].T).view(T, Hq, D).transpose(0, 1)
         k = (xn @ L["k"].T).view(T, Hkv, D).transpose(0, 1)
         v = (xn @ L["v"].T).view(T, Hkv, D).transpose(0, 1)
-        q = _rope32(_rms32(q, L["q_norm"], eps), 0, args["rope_theta"])
-        k = _rope32(_rms32(k, L["k_norm"], eps), 0, args["rope_theta"])
+        rp = args.get("rope", [None] * (i + 1))[i] or (None, None, 1.0)
+        q = _rope32(_rms32(q, L["q_norm"], eps), pos0, args["rope_theta"], *rp)
+        k = _rope32(_rms32(k, L["k_norm"], eps), pos0, args["rope_theta"], *rp)
         G = Hq // Hkv
         s = (q @ k.repeat_interleave(G, 0).transpose(1, 2)) * D ** -0.5
-        s = s.masked_fill(torch.ones(T, T, dtype=torch.bool).triu(1), float("-inf"))
+        hide = torch.ones(T, T, dtype=torch.bool).triu(1)
+        window = args.get("window", [None] * (i + 1))[i]
+        if window:
+            hide = hide | torch.ones(T, T, dtype=torch.bool).tril(-window)
+        s = s.masked_fill(hide, float("-inf"))
         o = (torch.softmax(s, -1) @ v.repeat_interleave(G, 0)).transpose(0, 1)
         g = softplus(xn @ L["g"].T)
         g = g[..., None] if args["gating"] == "per-head" else g.view(T, Hq, D)

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version_and_no_error():
-    assert _lib.lib().lg_abi_version() == 1
+    assert _lib.lib().lg_abi_version() == 2
     assert isinstance(_lib.lib().lg_last_error(), bytes)
 
 

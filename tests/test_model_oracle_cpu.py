@@ -53,6 +53,56 @@ def test_fp32_form_matches_the_pytorch_model():
     assert (got - ref).abs().max() <= 1e-4 * ref.abs().max() + 1e-5
 
 
+GOLDEN_SWA = Path(__file__).resolve().parent / "golden" / "model_swa.npz"
+SWA_YARN = {"rope_theta": 500000.0, "rope_type": "yarn", "factor": 32.0,
+            "original_max_position_embeddings": 8192, "beta_slow": 1.0, "beta_fast": 64.0,
+            "attention_factor": 1.3465735902799727, "partial_rotary_factor": 0.5}
+SWA_DEFAULT = {"rope_type": "default", "rope_theta": 10000.0, "partial_rotary_factor": 1.0}
+
+
+def _golden_swa():
+    d = np.load(GOLDEN_SWA)
+    t = lambda k: torch.from_numpy(d["w." + k]).float()
+    heads = [4, 4, 8, 4]
+    W = {"embed": t("model.embed_tokens.weight"), "norm": t("model.norm.weight"),
+         "lm_head": t("lm_head.weight"), "layers": []}
+    for i in range(4):
+        p = f"model.layers.{i}."
+        L = {"in_norm": t(p + "input_layernorm.weight"),
+             "post_norm": t(p + "post_attention_layernorm.weight"),
+             "q_norm": t(p + "self_attn.q_norm.weight"), "k_norm": t(p + "self_attn.k_norm.weight")}
+        for n in "qkvog":
+            L[n] = t(p + f"self_attn.{n}_proj.weight")
+        if "w." + p + "mlp.gate_proj.weight" in d:
+            L["mlp"] = ("dense", tuple(t(p + f"mlp.{n}_proj.weight") for n in ("gate", "up", "down")))
+        else:
+            gu = t(p + "mlp.experts.gate_up_proj")
+            I = gu.shape[1] // 2
+            L["mlp"] = ("moe", {
+                "gate": t(p + "mlp.gate.weight"), "bias": t(p + "mlp.gate.e_score_correction_bias"),
+                "experts": (gu[:, :I], gu[:, I:], t(p + "mlp.experts.down_proj")),
+                "shared": tuple(t(p + f"mlp.shared_expert.{n}_proj.weight")
+                                for n in ("gate", "up", "down"))})
+        W["layers"].append(L)
+    full = model_ref.rope_params(SWA_YARN, 32)
+    swa = model_ref.rope_params(SWA_DEFAULT, 32)
+    args = dict(head_dim=32, heads=heads, kv_heads=2, eps=1e-6, rope_theta=1e4,
+                gating="per-head", k=2, routed_scale=2.5, norm_topk_prob=True,
+                rope=[full, swa, swa, full], window=[None, 5, 5, None])
+    return W, args, torch.from_numpy(d["ids"]), int(d["pos0"]), torch.from_numpy(d["ref_logits"])
+
+
+def test_sliding_window_and_yarn_partial_rotary_match_the_pytorch_model():
+    """The real checkpoint's layer mix (laguna.py:62-72, :183-186, :209-214): sliding-window
+    layers with default RoPE and full layers with YaRN on half the head dims, at positions
+    3000.. (past the window, inside YaRN's frequency ramp)."""
+    W, args, ids, pos0, ref = _golden_swa()
+    got = model_ref.forward_fp32(W, args, ids, pos0)
+    assert (got - ref).abs().max() <= 1e-4 * ref.abs().max() + 1e-5
+    R, inv, ms = args["rope"][0]
+    assert R == 16 and inv.shape == (8,) and abs(ms - 1.3465735902799727) < 1e-12
+
+
 def _tiny_quantized(seed=0, V=160, H=128, D=64, Hq=4, Hkv=2, E=8, k=2, I=64, I_sh=64, I_d=128):
     """A 3-layer model with every inner dimension a multiple of 64 (quantizable at g64):
     fp32 weights, and the same weights in MLX 4-bit layout (router 8-bit)."""
