@@ -1,25 +1,28 @@
-"""Benchmark of the Laguna MoE block / q8 decode attention hot path on B200.
+"""Benchmark of the Laguna decoder hot path on B200 (the MoE block, the fused 8-bit KV decode
+attention, and the bs1 decoder they sit in).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload moe_prefill|moe_decode|q8_decode|decode]
+                    [--workload decode_q8|decode|moe_prefill|moe_decode|q8_decode]
 
-Prints ONE JSON line on rank 0. Default workload: one SparseMoeBlock
-forward (router + routed experts + shared expert + combine) on T = 4096 tokens, 128 experts,
-top-8, hidden 2048, intermediate 1024, 4-bit g64 weights, Zipf-skewed routing; metric
-"MoE-layer tokens/s". ``q8_decode`` is config 4 (40 layers of fused 8-bit KV decode attention
-at 82,671 keys, metric HBM GB/s); ``moe_decode`` is config 1 (T = 16); ``decode`` is config 3
-(the whole 40-layer decoder, bs1 greedy decode after an 8,192-token prefill, tokens/s; each
-step one CUDA-graph replay of the model).
+Prints ONE JSON line on rank 0. Default workload ``decode_q8`` (the headline metric): the
+config-3 decoder (40 layers, 64 experts top-8, 4-bit g64 weights) decoding one token per step
+at an 82,671-token context over the 8-bit quantized KV cache, each step one CUDA-graph replay;
+metric tokens/s. ``decode`` is config 3 as stated (8,192-token prefill, bf16 KV);
+``moe_prefill`` is config 2 (one MoE block on 4,096 Zipf-routed tokens, 128 experts, metric
+"MoE-layer tokens/s"); ``moe_decode`` is config 1 (T = 16, graph-replayed); ``q8_decode`` is
+config 4 (40 layers of fused 8-bit KV decode attention at 82,671 keys, HBM GB/s).
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and cuda synchronize, timed with
 CUDA events on the launching stream; the max over ranks is reported. Inputs are resident in
-HBM and larger than L2 (453 MB of expert weights; 3.6 GB of KV for q8_decode). ``e2e`` is the
-same metric through the public module API with the step's input copied from pinned host
-memory and the output copied back inside the timed region.
+HBM and larger than L2. ``e2e`` is the same metric through the public module API with the
+step's input copied from pinned host memory and the output copied back inside the timed
+region.
 
-Multi-GPU (torchrun, N > 1): expert-parallel — every rank holds E/N experts and routes its own
-4096 tokens; dispatch and combine are NCCL all-to-alls (weak scaling: tokens per rank fixed).
-``--impl reference`` times the CPU restatement of the reference's path on the host cores.
+Multi-GPU (torchrun, N > 1): decode workloads run N independent replicas; the MoE workloads
+run expert parallel (E/N experts per rank, NVLink peer-memory dispatch and return). Every line
+also carries ``ep_prefill``: BASELINE config 5's 32,768-token MoE-layer prefill split over the
+N ranks, with the one-GPU block as baseline and checker. ``--impl reference`` times the CPU
+restatement of the reference's path on the host cores.
 """
 import argparse
 import json
@@ -212,16 +215,33 @@ def run_moe(args, wl, ws, rank):
     clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.3)
     clocks.mark(True)
-    ms, gu_ms, launches = timed(lambda: fwd(x), args.steps, stream, "experts_gateup")
-    barrier(ws)
-    # end to end through the module API with host buffers
     x_host = x.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     x_dev = torch.empty_like(x)
+    # A decode-size block (config 1) is a few microseconds of kernels: eager ctypes calls
+    # would time the host, so one forward is captured in a CUDA graph and replayed per step
+    # (the expert-parallel forward passes its epoch as a launch argument and stays eager).
+    graphed = ws == 1 and T * k <= 512
+    held = {}
+    if graphed:
+        x_dev.copy_(x)
+        g, per_replay, ev = capture(lambda: held.__setitem__("y", fwd(x_dev)), "experts_gateup")
+        for _ in range(args.warmup):
+            g.replay()
+        ms, gu_ms = timed_graph(g, args.steps, stream, ev)
+        launches = per_replay * args.steps
+    else:
+        ms, gu_ms, launches = timed(lambda: fwd(x), args.steps, stream, "experts_gateup")
+    barrier(ws)
+    # end to end through the module API with host buffers
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        o = fwd(x_dev)
+        if graphed:
+            g.replay()
+            o = held["y"]  # the graph's output buffer, rewritten by every replay
+        else:
+            o = fwd(x_dev)
         out_host.copy_(o, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -300,6 +320,96 @@ def run_ep_prefill(args, ws, rank):
                        cosine=float(torch.nn.functional.cosine_similarity(
                            got.reshape(-1), ref.reshape(-1), dim=0)))
     del blk
+    torch.cuda.empty_cache()
+    barrier(ws)
+    return out
+
+
+DECODE_STREAMS = dict(B=64, ctx=8192, experts=128, seed=1, steps=8, warmup=3)
+
+
+def _stream_model(c):
+    from lagunalab_b200 import synth
+    wl = dict(WORKLOADS["decode"], experts=c["experts"], seed=c["seed"])
+    _, model = decode_model(wl)
+    synth.zipf_router(model, seed=c["seed"])
+    return model
+
+
+def run_decode_streams(args, ws, rank):
+    """BASELINE config 5's batched decode: the unpruned 128-expert decoder (config 2's MoE shape
+    in the config-3 decoder; Zipf(1.1)-skewed router), 64 concurrent streams at an 8,192-token
+    context each, one greedy token per stream per step, each step one CUDA-graph replay. The
+    streams are split evenly over the ranks (strong scaling: 64 streams in all); with N > 1
+    every MoE layer runs expert parallel (E/N experts per rank; dispatch and return are NVLink
+    peer stores issued by the kernels, with device-held epochs so the exchanges replay with the
+    graph). Each stream's cache holds synthetic K/V rows for its 8,192 context positions (seeded
+    N(0, 1)) instead of a prefill: a decode step reads the same bytes either way. Rank 0 also
+    times all 64 streams on its own GPU with every expert local (the one-GPU baseline)."""
+    import torch.distributed as dist
+    from lagunalab_b200 import _lib, ep, laguna, synth
+    c = DECODE_STREAMS
+    B, ctx = c["B"], c["ctx"]
+    Br = B // ws
+    K, Wm = c["steps"], c["warmup"]
+    cap = (ctx + K + Wm + 2 + 255) // 256 * 256
+    model = _stream_model(c)
+    stream = torch.cuda.current_stream()
+
+    def streams(first, n):
+        cache = model.make_stream_cache(n, cap)
+        synth.fill_stream_cache(cache, ctx, first_stream=first, seed=c["seed"])
+        g = torch.Generator().manual_seed(c["seed"] + 99)
+        ids = torch.randint(0, model.args.vocab_size, (B,), generator=g)[first:first + n]
+        return cache, ids.to(torch.int32).cuda(), torch.full((n,), ctx, dtype=torch.int32,
+                                                              device="cuda")
+
+    def time_graph(g):
+        for _ in range(Wm):
+            g.step()
+        torch.cuda.synchronize()
+        return timed_graph(g.graph, K, stream)[0]
+
+    out = dict(streams=B, context=ctx, experts=c["experts"], n_gpus=ws, streams_per_gpu=Br,
+               kv="bf16", steps=K,
+               data="synthetic K/V context rows (seeded N(0,1)); random-init 4-bit weights")
+    pes = []
+    if ws > 1:
+        moe = []
+        for L in model.layers:
+            if isinstance(L.mlp, laguna.SparseMoeBlock):
+                # the owners' product path is fixed so every rank takes the same one
+                pes.append(ep.PeerExpertParallel(L.mlp, capacity=Br, device_epoch=True,
+                                                 expert_path=_lib.LG_PATH_GEMV))
+                moe.append(pes[-1])
+            else:
+                moe.append(None)
+        cache, tok, pos = streams(rank * Br, Br)
+        g = laguna.StreamDecodeGraph(model, cache, tok, pos, moe=moe)
+        barrier(ws)
+        ms = max_over_ranks(time_graph(g), ws)
+        torch.cuda.synchronize()
+        status = int(max_over_ranks(float(max(p.status() for p in pes)), ws))
+        out.update(ms_per_step=ms, tokens_per_s=B / (ms * 1e-3), status=status,
+                   exchange="NVLink peer stores issued by the dispatch kernel and the expert "
+                            "down-product epilogue; device-held epochs; no collective")
+        del g, cache
+        torch.cuda.empty_cache()
+    if rank == 0:
+        cache, tok, pos = streams(0, B)
+        g1 = laguna.StreamDecodeGraph(model, cache, tok, pos)
+        ms1 = time_graph(g1)
+        out.update(one_gpu_ms=ms1, one_gpu_tokens_per_s=B / (ms1 * 1e-3))
+        if ws > 1:
+            out.update(speedup=ms1 / out["ms_per_step"],
+                       efficiency=ms1 / (out["ms_per_step"] * ws))
+        else:
+            out.update(ms_per_step=ms1, tokens_per_s=B / (ms1 * 1e-3))
+        del g1, cache
+    barrier(ws)
+    for p in pes:
+        p.close()
+    del model, pes
     torch.cuda.empty_cache()
     barrier(ws)
     return out
@@ -777,6 +887,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the config-5 expert-parallel prefill measurement")
+    ap.add_argument("--no-streams", action="store_true",
+                    help="skip the config-5 batched decode measurement (64 streams x 8k)")
     ap.add_argument("--layers", type=int, default=None,
                     help="q8_decode only: layers per step (default: the config's 40; fewer "
                          "for small profiling runs)")
@@ -890,6 +1002,8 @@ def main():
         line["decode"] = decode_info
     if not args.no_ep:
         line["ep_prefill"] = run_ep_prefill(args, ws, rank)
+    if not args.no_streams:
+        line["decode_streams"] = run_decode_streams(args, ws, rank)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cb = (cpu_q8(wl, 3, 1) if args.workload == "q8_decode" else
               cpu_decode(wl, 2, 1, budget_s=45.0) if args.workload in DECODE_WORKLOADS else cpu_moe(wl, 5, 1))

@@ -246,7 +246,7 @@ int lg_rmsnorm(const void* x, const void* residual, const void* w, int T, int H,
 /*
  * 4-bit group-64 dense linear at decode sizes, nn.QuantizedLinear (laguna.py:84-92, :197):
  *   out = bf16(x . W^T) [+ residual, in bf16], W = scale * code + bias per 64-group.
- * x bf16 [T, K] (T <= 16), W uint32 [N, K/8] with bf16 scales/biases [N, K/64], residual
+ * x bf16 [T, K] (T <= 64), W uint32 [N, K/8] with bf16 scales/biases [N, K/64], residual
  * and out bf16 [T, N].  K % 64 == 0.  Larger T: dequantize (lg_dequantize_rows) and use a
  * dense GEMM.
  */
@@ -298,6 +298,21 @@ int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, const void*
                     void* stream);
 
 /*
+ * lg_attn_prep for one decode step of B independent streams (batched decode, BASELINE config
+ * 5; the reference's caches hold one sequence: laguna_mlx/cache.py:66-157 has no batch merge,
+ * docs/architecture.md:347-349). Token t of qkvg [B, .] is the newest token of stream t, at
+ * position pos_dev[t] (device int32 [B]); its k/v rows go to row pos_dev[t] of stream t's
+ * caches (k_cache, v_cache bf16 [B, Hkv, cap, D]; ring > 0: row = position mod ring) and q_out
+ * is [B, Hq, D] (the layout lg_bf16_decode_attention_streams reads). Same arithmetic as
+ * lg_attn_prep.
+ */
+int lg_attn_prep_streams(const void* qkvg, int B, int Hq, int Hkv, int D, const void* qn_w,
+                         const void* kn_w, float eps, float rope_theta, const int32_t* pos_dev,
+                         int gate_per_head, void* q_out, void* k_cache, void* v_cache, int cap,
+                         void* gate_out, const float* inv_freq, int rot_dims, float mscale,
+                         int ring, void* stream);
+
+/*
  * One token's q/k/v/g projection (lg_decode_gemv with the layer's input RMSNorm fused in,
  * laguna.py:94-99) followed by its attention prologue (lg_attn_prep / lg_attn_prep_q8,
  * laguna.py:100-106) in one launch: qkvg_out = the projection row [q | k | v | g] (bf16,
@@ -341,6 +356,17 @@ int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, int D, const
                              const void* v, int cap, int n, const int32_t* n_dev, int n_add,
                              int n_plan, float scale, const void* gate, void* out,
                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * lg_bf16_decode_attention for B independent streams of different lengths (batched decode,
+ * BASELINE config 5): stream b attends over n_dev[b] + n_add keys of its own cache
+ * (n_dev: device int32 [B]); n_plan bounds every stream's length.
+ */
+int lg_bf16_decode_attention_streams(const void* q, int B, int Hq, int Hkv, int D,
+                                     const void* k, const void* v, int cap,
+                                     const int32_t* n_dev, int n_add, int n_plan, float scale,
+                                     const void* gate, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 
 /*
  * Greedy token: ids[t] = argmax of bf16 logits row t of [T, V] (first index among equal
@@ -458,6 +484,10 @@ int lg_decode_status(unsigned long long check[4], int reset);
  * A forward is, on every rank with the same epoch (1, 2, ... one per forward):
  *   lg_router_topk -> lg_ep_dispatch -> lg_qmlp (shared expert, into the arena's shared rows,
  *   lg_ep_arena_offsets) -> lg_ep_experts -> lg_ep_combine.
+ * Epoch 0 in every call of a forward selects the device-held epoch instead: one past the
+ * forwards this rank has completed, counted in its arena by lg_ep_advance (launched after
+ * each forward's lg_ep_combine), so that forwards can be captured in a CUDA graph and
+ * replayed. An arena uses one kind of epoch for its whole life.
  * The exchanges are peer stores issued by the kernels over NVLink (plain peer pointers); ranks
  * synchronise through epoch flags in the arenas with waits bounded by timeout_s (<= 0: 2 s).
  * An expired wait records (code | source << 8) in the arena's status word (lg_ep_status;
@@ -491,6 +521,9 @@ int lg_ep_experts(int W, int Tr, int H, int I, int El, int k, const uint32_t* ga
 int lg_ep_combine(const int32_t* inds, int T, int Tr, int H, int k, int E, float routed_scale,
                   int has_shared, int W, int rank, void* const* arenas, unsigned epoch,
                   double timeout_s, void* out, void* stream);
+/* After a forward with device-held epochs (epoch 0): one launch on `stream` that counts the
+ * forward as completed in this rank's arena. */
+int lg_ep_advance(void* arena, void* stream);
 /* Status word of an arena (0 = ok). Synchronous; reset != 0 clears it. */
 int lg_ep_status(const void* arena, int reset, int* status);
 

@@ -49,7 +49,11 @@ SIGNATURES = {
     "lg_embed": (c_int, [P, I, P, P, P, I, I, I, I, P, P]),
     "lg_attn_prep": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, I, P, P, P, I, P,
                              P, I, c_float, I, I, P]),
+    "lg_attn_prep_streams": (c_int, [P, I, I, I, I, P, P, c_float, c_float, P, I, P, P, P, I, P,
+                                     P, I, c_float, I, P]),
     "lg_bf16_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
+    "lg_bf16_decode_attention_streams": (c_int, [P, I, I, I, I, P, P, I, P, I, I, c_float, P, P,
+                                                 P, c_size_t, P]),
     "lg_bf16_decode_attention": (c_int, [P, I, I, I, I, P, P, I, I, P, I, I, c_float, P, P, P,
                                          c_size_t, P]),
     "lg_argmax": (c_int, [P, I, I, P, P, I, P]),
@@ -82,6 +86,7 @@ SIGNATURES = {
     "lg_ep_combine": (c_int, [P, I, I, I, I, I, c_float, I, I, I, P, ctypes.c_uint,
                               ctypes.c_double, P, P]),
     "lg_ep_status": (c_int, [P, I, P]),
+    "lg_ep_advance": (c_int, [P, P]),
     "lg_moe_decode": (c_int, [P, P, P, I, I, I, I, c_float, P, P, P, P, P, P, P, P, P, I,
                               P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),
 }

@@ -77,8 +77,9 @@ struct AbArgs {
   const __nv_bfloat16* k;   // [B, Hkv, cap, D]
   const __nv_bfloat16* v;
   const __nv_bfloat16* gate;  // [B, Hq] per-head output gate, or null
-  const int* n_dev;         // valid keys = n_dev[0] + n_add when non-null, else n_host
+  const int* n_dev;         // valid keys = n_dev[b * n_stride] + n_add when non-null, else n_host
   int n_host, n_add;
+  int n_stride;             // 0: one length for every batch row; 1: per stream (batched decode)
   int B, Hq, Hkv, G, cap, tpc, nsplit;
   float qscale;             // scale * log2(e)
   int* counters;            // [B * Hkv][32] (nsplit > 1); bit 20 and up: unused here
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = a.G;
   const int bh = b * a.Hkv + hk;
-  int n = a.n_dev ? a.n_dev[0] + a.n_add : a.n_host;
+  int n = a.n_dev ? a.n_dev[b * a.n_stride] + a.n_add : a.n_host;
   n = min(max(n, 0), a.cap);
   const int tile_lo = split * a.tpc;
   const int tile_hi = min(tile_lo + a.tpc, (n + AB_TK - 1) / AB_TK);
@@ -413,11 +414,10 @@ extern "C" size_t lg_bf16_decode_workspace_bytes(int B, int Hq, int Hkv, int n_p
   return ab_ws(B, Hq, Hkv, n_plan, nullptr, nullptr);
 }
 
-extern "C" int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
-                                        const void* k, const void* v, int cap, int n,
-                                        const int32_t* n_dev, int n_add, int n_plan, float scale,
-                                        const void* gate, void* out, void* workspace,
-                                        size_t workspace_bytes, void* stream) {
+static int bf16_decode_run(const void* q, int B, int Hq, int Hkv, int D, const void* k,
+                           const void* v, int cap, int n, const int32_t* n_dev, int n_stride,
+                           int n_add, int n_plan, float scale, const void* gate, void* out,
+                           void* workspace, size_t workspace_bytes, void* stream) {
   LG_CHECK_ARG(D == AB_D, "bf16 decode: head_dim %d != 128", D);
   LG_CHECK_ARG(B >= 1 && Hkv >= 1 && Hq >= 1 && Hq % Hkv == 0 && Hq / Hkv <= 16,
                "bf16 decode: bad heads Hq=%d Hkv=%d (group <= 16)", Hq, Hkv);
@@ -441,6 +441,7 @@ extern "C" int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, i
   a.n_dev = n_dev;
   a.n_host = n;
   a.n_add = n_add;
+  a.n_stride = n_stride;
   a.B = B;
   a.Hq = Hq;
   a.Hkv = Hkv;
@@ -463,4 +464,24 @@ extern "C" int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, i
   prof_end("bf16_decode", st);
   LG_LAUNCH_CHECK("bf16_decode");
   return LG_OK;
+}
+
+extern "C" int lg_bf16_decode_attention(const void* q, int B, int Hq, int Hkv, int D,
+                                        const void* k, const void* v, int cap, int n,
+                                        const int32_t* n_dev, int n_add, int n_plan, float scale,
+                                        const void* gate, void* out, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  return bf16_decode_run(q, B, Hq, Hkv, D, k, v, cap, n, n_dev, 0, n_add, n_plan, scale, gate,
+                         out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int lg_bf16_decode_attention_streams(const void* q, int B, int Hq, int Hkv, int D,
+                                                const void* k, const void* v, int cap,
+                                                const int32_t* n_dev, int n_add, int n_plan,
+                                                float scale, const void* gate, void* out,
+                                                void* workspace, size_t workspace_bytes,
+                                                void* stream) {
+  LG_CHECK_ARG(n_dev, "bf16 decode streams: NULL lengths");
+  return bf16_decode_run(q, B, Hq, Hkv, D, k, v, cap, 0, n_dev, 1, n_add, n_plan, scale, gate,
+                         out, workspace, workspace_bytes, stream);
 }

@@ -61,10 +61,11 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_kernel(const __nv_bfloat16
 // 4-bit dense linear at decode sizes (nn.QuantizedLinear, laguna.py:84-92, :197):
 // y[t, n] = sum_k x[t, k] * (scale[n, k/64] * code[n, k] + bias[n, k/64]), fp32 accumulation,
 // one bf16 rounding (quantized_matmul's output), then optionally + residual in bf16.
-// One CTA per 16-row tile of W, 16 warps split the K groups, each warp runs the tensor-core
-// group product of gemv_core.cuh against one or two 8-token tiles.
+// One CTA per (16-row tile of W, 16 tokens), 16 warps split the K groups, each warp runs the
+// tensor-core group product of gemv_core.cuh against one or two 8-token tiles.
 // ---------------------------------------------------------------------------------------
 constexpr int QL_WARPS = 16;
+constexpr int QL_MAX_T = 64;  // tokens per call: up to four 16-token CTA rows per W tile
 
 struct QlArgs {
   const __nv_bfloat16* x;  // [T, K]
@@ -84,6 +85,12 @@ __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = lane >> 2, c4 = lane & 3;
   const int m0 = blockIdx.x * 16;
+  // blockIdx.y: this CTA's 16 tokens (CTAs of the same W tile share its reads through L2)
+  const int t0 = blockIdx.y * 16;
+  const int T = min(a.T - t0, 16);
+  const __nv_bfloat16* xb = a.x + (size_t)t0 * a.K;
+  const __nv_bfloat16* resb = a.res ? a.res + (size_t)t0 * a.N : nullptr;
+  __nv_bfloat16* outb = a.out + (size_t)t0 * a.N;
   const int ra = min(m0 + r, a.N - 1), rb = min(m0 + r + 8, a.N - 1);
   const int K = a.K, wpr = K / 8, gpr = K / 64;
   float acc[NTT][4];
@@ -119,8 +126,8 @@ __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
       for (int tt = 0; tt < NTT; ++tt) {
         const int tok = 8 * tt + r;
         uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
-        if (tok < a.T) {
-          const __nv_bfloat16* xr = a.x + (size_t)tok * K + gg * 64 + 16 * c4;
+        if (tok < T) {
+          const __nv_bfloat16* xr = xb + (size_t)tok * K + gg * 64 + 16 * c4;
           xa0 = *reinterpret_cast<const uint4*>(xr);
           xa1 = *reinterpret_cast<const uint4*>(xr + 8);
         }
@@ -152,11 +159,102 @@ __global__ void __launch_bounds__(QL_WARPS * 32) qlinear_kernel(QlArgs a) {
     const int lr = l >> 2, lc = l & 3, tt = q / 4, j = q % 4;
     const int tok = 8 * tt + 2 * lc + (j & 1);
     const int n = m0 + lr + (j < 2 ? 0 : 8);
-    if (tok < a.T && n < a.N) {
+    if (tok < T && n < a.N) {
       float y = round_bf16(v);
-      if (a.res) y += bf2f(a.res[(size_t)tok * a.N + n]);
-      a.out[(size_t)tok * a.N + n] = __float2bfloat16_rn(y);
+      if (resb) y += bf2f(resb[(size_t)tok * a.N + n]);
+      outb[(size_t)tok * a.N + n] = __float2bfloat16_rn(y);
     }
+  }
+}
+
+// Staged form (2..64 tokens: batched decode steps, short prefills, for matrices with enough
+// 16-row tiles to fill the GPU): one CTA per (16 tokens, 16-row tile of W), the tile staged
+// into shared memory by bulk copies issued before the PDL wait (the weights are static); 4
+// warps split the K groups of the staged tile and the tokens run in blocks of 8 against it,
+// each block reduced across the warps and stored with the epilogue above. The CTAs of one
+// tile are adjacent in launch order, so the tile crosses HBM about once; the activations come
+// from L2.
+constexpr int QS_WARPS = 4;
+constexpr uint32_t QS_HDR = 128, QS_RED = QS_WARPS * 32 * 4 * 4;
+
+static uint32_t qs_smem(int K) { return QS_HDR + QS_RED + tile_bytes(K); }
+
+__global__ void __launch_bounds__(QS_WARPS * 32) qlinear_staged_kernel(QlArgs a) {
+  extern __shared__ __align__(128) uint8_t qs_smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qs_smem_raw);
+  int* berr = reinterpret_cast<int*>(qs_smem_raw + 8);
+  float (*red)[32][4] = reinterpret_cast<float (*)[32][4]>(qs_smem_raw + QS_HDR);
+  uint8_t* tile = qs_smem_raw + QS_HDR + QS_RED;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, r = lane >> 2, c4 = lane & 3;
+  // blockIdx.x: this CTA's 16 tokens (the CTAs of one tile are launched next to each other,
+  // so its later copies hit L2); blockIdx.y: the 16-row tile of W
+  const int m0 = blockIdx.y * 16, K = a.K, gpr = K / 64;
+  const int tbeg = blockIdx.x * 16, tend = min(a.T, tbeg + 16);
+  const uint32_t pitch = tile_pitch(K);
+  if (threadIdx.x == 0) {
+    *berr = 0;
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, tile_bulk_bytes(K));
+    tile_load_bulk(tile, a.wq, a.ws, a.wb, m0, K, bar);
+  }
+  pdl_wait();  // x (and the residual) come from the previous kernel
+  pdl_trigger();
+  __syncthreads();  // the barrier is initialised before anyone polls it
+  const bool ok = __syncthreads_and(mbar_wait(bar, 0, berr, 1, 400000000LL));
+  if (!ok && threadIdx.x == 0)  // the tile never arrived: drain (bounded); the rows become NaN
+    for (const long long t0 = clock64(); !mbar_try_wait(bar, 0) && clock64() - t0 < 400000000LL;) {
+    }
+  const __nv_bfloat16* ts = reinterpret_cast<const __nv_bfloat16*>(tile + tile_sc_off(K));
+  for (int t8 = tbeg; t8 < tend; t8 += 8) {
+    const int tok = t8 + r;
+    const bool tval = ok && tok < tend;
+    const __nv_bfloat16* xr = a.x + (size_t)(tval ? tok : 0) * K;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int gg = warp; ok && gg < gpr; gg += QS_WARPS) {
+      const uint32_t o0 = r * pitch + gg * 32 + c4 * 8;
+      const uint2 w0 = *reinterpret_cast<const uint2*>(tile + o0);
+      const uint2 w8 = *reinterpret_cast<const uint2*>(tile + o0 + 8 * pitch);
+      uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
+      if (tval) {
+        xa0 = *reinterpret_cast<const uint4*>(xr + gg * 64 + 16 * c4);
+        xa1 = *reinterpret_cast<const uint4*>(xr + gg * 64 + 16 * c4 + 8);
+      }
+      float xs = xsum16(xa0, xa1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+      const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
+      const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
+      const int i0 = r * gpr + gg, i8 = i0 + 8 * gpr, nb = 16 * gpr;  // scales, then biases
+      const float s0 = bf2f(ts[i0]), s8 = bf2f(ts[i8]);
+      const float b0 = bf2f(ts[nb + i0]), b8 = bf2f(ts[nb + i8]);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      group_mma(d, w0, w8, xa0, xa1);
+      acc[0] += s0 * d[0] + b0 * xs0;
+      acc[1] += s0 * d[1] + b0 * xs1;
+      acc[2] += s8 * d[2] + b8 * xs0;
+      acc[3] += s8 * d[3] + b8 * xs1;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[warp][lane][j] = acc[j];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < QS_WARPS; ++w) v += red[w][lane][j];
+        const int col = t8 + 2 * c4 + (j & 1);
+        const int n = m0 + r + (j < 2 ? 0 : 8);
+        if (col < tend) {
+          float y = round_bf16(v);
+          if (a.res) y += bf2f(a.res[(size_t)col * a.N + n]);
+          if (!ok) y = __int_as_float(0x7fc00000);
+          a.out[(size_t)col * a.N + n] = __float2bfloat16_rn(y);
+        }
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -282,7 +380,8 @@ extern "C" int lg_qlinear(const void* x, int T, int K, int N, const uint32_t* w_
                           const void* w_s, const void* w_b, int group_size, int bits,
                           const void* residual, void* out, void* stream) {
   LG_CHECK_ARG(bits == 4 && group_size == 64, "qlinear: 4-bit group-64 weights only");
-  LG_CHECK_ARG(T >= 0 && T <= 16, "qlinear: decode sizes only (T=%d > 16: dequantize instead)", T);
+  LG_CHECK_ARG(T >= 0 && T <= QL_MAX_T, "qlinear: decode sizes only (T=%d > %d: dequantize instead)",
+               T, QL_MAX_T);
   LG_CHECK_ARG(K > 0 && K % 64 == 0 && N > 0, "qlinear: need K %% 64 == 0 (K=%d, N=%d)", K, N);
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(x && w_q && w_s && w_b && out, "qlinear: NULL pointer");
@@ -298,18 +397,34 @@ extern "C" int lg_qlinear(const void* x, int T, int K, int N, const uint32_t* w_
   a.K = K;
   a.N = N;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int tiles = (N + 15) / 16;
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  // the staged form when it has CTAs to fill the GPU (small matrices keep the 16-warp form)
+  const int ctas = (N / 16) * ((T + 15) / 16);
+  if (T >= 2 && N % 16 == 0 && ctas >= 2 * device_sm_count() && al16(w_q) && al16(w_s) &&
+      al16(w_b)) {
+    const uint32_t smem = qs_smem(K);
+    if (smem > 48u * 1024u)
+      LG_CUDA_TRY(cudaFuncSetAttribute(qlinear_staged_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    prof_begin("qlinear", st);
+    LG_CUDA_TRY(launch_k(qlinear_staged_kernel, dim3((T + 15) / 16, N / 16), dim3(QS_WARPS * 32),
+                         smem, st, a));
+    prof_end("qlinear", st);
+    LG_LAUNCH_CHECK("qlinear_staged");
+    return LG_OK;
+  }
+  const dim3 grid((N + 15) / 16, (T + 15) / 16);
   prof_begin("qlinear", st);
   const int gpw = (K / 64 + QL_WARPS - 1) / QL_WARPS;  // groups per warp
   cudaError_t e;
   if (T <= 8)
-    e = gpw <= 2 ? launch_k(qlinear_kernel<1, 2>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
-        : gpw <= 4 ? launch_k(qlinear_kernel<1, 4>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
-                   : launch_k(qlinear_kernel<1, 8>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a);
+    e = gpw <= 2 ? launch_k(qlinear_kernel<1, 2>, grid, dim3(QL_WARPS * 32), 0, st, a)
+        : gpw <= 4 ? launch_k(qlinear_kernel<1, 4>, grid, dim3(QL_WARPS * 32), 0, st, a)
+                   : launch_k(qlinear_kernel<1, 8>, grid, dim3(QL_WARPS * 32), 0, st, a);
   else
-    e = gpw <= 2 ? launch_k(qlinear_kernel<2, 2>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
-        : gpw <= 4 ? launch_k(qlinear_kernel<2, 4>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a)
-                   : launch_k(qlinear_kernel<2, 8>, dim3(tiles), dim3(QL_WARPS * 32), 0, st, a);
+    e = gpw <= 2 ? launch_k(qlinear_kernel<2, 2>, grid, dim3(QL_WARPS * 32), 0, st, a)
+        : gpw <= 4 ? launch_k(qlinear_kernel<2, 4>, grid, dim3(QL_WARPS * 32), 0, st, a)
+                   : launch_k(qlinear_kernel<2, 8>, grid, dim3(QL_WARPS * 32), 0, st, a);
   LG_CUDA_TRY(e);
   prof_end("qlinear", st);
   LG_LAUNCH_CHECK("qlinear");
@@ -337,13 +452,14 @@ static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const 
                          int pos_host, int gate_per_head, void* q_out, void* k_cache,
                          void* v_cache, const uint32_t* const* q8, const void* const* q8sb,
                          int cap, void* gate_out, const float* inv_freq, int rot_dims,
-                         float mscale, int ring, int row0, void* stream) {
+                         float mscale, int ring, int row0, void* stream, int streams = 0) {
   LG_CHECK_ARG(D % 64 == 0 && D <= 256 && Hq > 0 && Hkv > 0 && T >= 0,
                "attn_prep: head_dim %d (need a multiple of 64, <= 256)", D);
   if (T == 0) return LG_OK;
   LG_CHECK_ARG(qkvg && qn_w && kn_w && q_out && ((k_cache && v_cache) || q8) && gate_out,
                "attn_prep: NULL pointer");
-  LG_CHECK_ARG(pos_dev || ring > 0 || (pos_host - row0 >= 0 && pos_host - row0 + T <= cap),
+  LG_CHECK_ARG(pos_dev || ring > 0 ||
+                   (pos_host - row0 >= 0 && pos_host - row0 + (streams ? 1 : T) <= cap),
                "attn_prep: positions %d..%d beyond the cache rows %d..%d", pos_host,
                pos_host + T - 1, row0, row0 + cap - 1);
   LG_CHECK_ARG(ring == 0 || ring == cap, "attn_prep: a ring buffer has %d rows, not %d", cap,
@@ -361,6 +477,7 @@ static int attn_prep_run(const void* qkvg, int T, int Hq, int Hkv, int D, const 
   a.D = D;
   a.cap = cap;
   a.gate_per_head = gate_per_head;
+  a.streams = streams;
   a.eps = eps;
   a.log2_theta = log2f(rope_theta);
   a.q_out = static_cast<__nv_bfloat16*>(q_out);
@@ -405,6 +522,18 @@ extern "C" int lg_attn_prep_q8(const void* qkvg, int T, int Hq, int Hkv, int D, 
   return attn_prep_run(qkvg, T, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, pos_host,
                        gate_per_head, q_out, nullptr, nullptr, q8, sb, cap, gate_out, inv_freq,
                        rot_dims, mscale, ring, row0, stream);
+}
+
+extern "C" int lg_attn_prep_streams(const void* qkvg, int B, int Hq, int Hkv, int D,
+                                    const void* qn_w, const void* kn_w, float eps,
+                                    float rope_theta, const int32_t* pos_dev, int gate_per_head,
+                                    void* q_out, void* k_cache, void* v_cache, int cap,
+                                    void* gate_out, const float* inv_freq, int rot_dims,
+                                    float mscale, int ring, void* stream) {
+  LG_CHECK_ARG(k_cache && v_cache && pos_dev, "attn_prep_streams: NULL cache or positions");
+  return attn_prep_run(qkvg, B, Hq, Hkv, D, qn_w, kn_w, eps, rope_theta, pos_dev, 0,
+                       gate_per_head, q_out, k_cache, v_cache, nullptr, nullptr, cap, gate_out,
+                       inv_freq, rot_dims, mscale, ring, 0, stream, 1);
 }
 
 extern "C" int lg_argmax(const void* logits, int T, int V, int32_t* ids, int32_t* pos, int inc,

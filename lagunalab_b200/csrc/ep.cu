@@ -3,8 +3,9 @@
 // The reference runs on one device and has no counterpart; BASELINE config 5 defines the split.
 //
 // Every rank owns the contiguous experts [r*El, (r+1)*El) and one "arena" of device memory that
-// its peers map (CUDA IPC, plain peer pointers). Per forward, with a host-side epoch e (the same on
-// every rank):
+// its peers map (CUDA IPC, plain peer pointers). Per forward, with an epoch e (the same on every
+// rank: given by the host, or held on the device and advanced by lg_ep_advance after each
+// forward, so that a forward can be replayed from a CUDA graph):
 //  1. ep_plan_kernel      per destination rank d, the source's tokens with a pick on d get
 //                         consecutive slots in token order (one CTA per d, block scans);
 //  2. ep_dispatch_kernel  one warp per (token, d): the token's row, its k expert ids local to
@@ -46,6 +47,7 @@ constexpr size_t EPH_COUNT = 128;      // [W] rows received from each src
 constexpr size_t EPH_STATUS = 192;     // status word (0 = ok)
 constexpr size_t EPH_DONE = 256;       // CTA completion counter of this rank's dispatch
 constexpr size_t EPH_SENDCNT = 320;    // [W] rows this rank sends to each owner
+constexpr size_t EPH_EPOCH = 384;      // forwards this rank has completed (device-held epochs)
 
 struct EpLayout {
   size_t recv_x, recv_lid, recv_w, recv_tok, ret, slot, total;
@@ -110,6 +112,14 @@ __device__ bool ep_wait_flags(char* arena, size_t flags_off, int W, unsigned epo
   return true;
 }
 
+// The epoch of this forward: the caller's, or for epoch 0 one past the forwards this rank has
+// completed, as counted on the device by ep_advance_kernel. Device-held epochs let a forward be
+// captured once in a CUDA graph and replayed; every rank replays the same number of forwards,
+// so the ranks' counters agree.
+__device__ __forceinline__ unsigned ep_epoch(char* self, unsigned epoch) {
+  return epoch ? epoch : *reinterpret_cast<volatile unsigned*>(hdr_u32(self, EPH_EPOCH)) + 1u;
+}
+
 __device__ __forceinline__ bool ep_owns(int e, int El, int W, int d) {
   return e >= 0 && e < El * W && e / El == d;
 }
@@ -149,6 +159,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
   pdl_wait();
   pdl_trigger();
   char* self = peers.arena[rank];
+  epoch = ep_epoch(self, epoch);
   const int lane = threadIdx.x & 31;
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int nw = (int)((gridDim.x * blockDim.x) >> 5);
@@ -199,7 +210,7 @@ __global__ void __launch_bounds__(256) ep_recv_kernel(char* self, int W, int Tr,
   __shared__ int ok;
   __shared__ unsigned cnt[EP_MAX_W];
   if (threadIdx.x == 0) {
-    ok = ep_wait_flags(self, EPH_DISPATCH, W, epoch, timeout_ns, 1u);
+    ok = ep_wait_flags(self, EPH_DISPATCH, W, ep_epoch(self, epoch), timeout_ns, 1u);
     for (int s = 0; s < W; ++s) cnt[s] = ok ? ld_acquire_sys(hdr_u32(self, EPH_COUNT) + s) : 0u;
   }
   __syncthreads();
@@ -215,6 +226,7 @@ __global__ void __launch_bounds__(256) ep_recv_kernel(char* self, int W, int Tr,
 
 // The owner, after its expert products: flag combine[owner] = epoch in every source.
 __global__ void ep_signal_kernel(EpPeers peers, int W, int rank, unsigned epoch) {
+  epoch = ep_epoch(peers.arena[rank], epoch);
   __threadfence_system();
   if ((int)threadIdx.x < W) st_release_sys(hdr_u32(peers.arena[threadIdx.x], EPH_COMBINE) + rank, epoch);
 }
@@ -233,7 +245,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(char* self, int W, int 
   pdl_wait();
   pdl_trigger();
   __shared__ int ok;
-  if (threadIdx.x == 0) ok = ep_wait_flags(self, EPH_COMBINE, W, epoch, timeout_ns, 2u);
+  if (threadIdx.x == 0)
+    ok = ep_wait_flags(self, EPH_COMBINE, W, ep_epoch(self, epoch), timeout_ns, 2u);
   __syncthreads();
   const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(self + L.ret);
   const __nv_bfloat16* sh = y + (size_t)Tr * k * H;
@@ -280,6 +293,11 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(char* self, int W, int 
     }
     *reinterpret_cast<uint4*>(out + t * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
+}
+
+// After a forward's combine (stream order): this rank has completed one more forward.
+__global__ void ep_advance_kernel(char* self) {
+  if (threadIdx.x == 0) *hdr_u32(self, EPH_EPOCH) += 1u;
 }
 
 }  // namespace lg
@@ -455,6 +473,13 @@ extern "C" int lg_ep_combine(const int32_t* inds, int T, int Tr, int H, int k, i
                        Tr, k, E, H, inds, routed_scale, has_shared, epoch,
                        ep_timeout_ns(timeout_s), L, static_cast<__nv_bfloat16*>(out)));
   LG_LAUNCH_CHECK("ep_combine");
+  return LG_OK;
+}
+
+extern "C" int lg_ep_advance(void* arena, void* stream) {
+  LG_CHECK_ARG(arena && aligned(arena, 256), "ep_advance: NULL or misaligned arena");
+  ep_advance_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<char*>(arena));
+  LG_LAUNCH_CHECK("ep_advance");
   return LG_OK;
 }
 

@@ -207,16 +207,19 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   a.ypick = mode == 0 ? w.yrows : static_cast<__nv_bfloat16*>(out);
   a.ep = {};
   if (mode == 2) a.ep = *ep;  // expert parallel: down outputs go to the source ranks
+  a.err = tc_err_word(w.tc, T, H, Ie, I_sh, E, k);
   int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
   // Tensor-core grouped GEMM when there are enough rows per expert to fill 128-row tiles;
   // the split-K GEMV otherwise (decode), or when the shapes do not tile.
   const bool tiles_ok = tc_supported(H, Ie, I_sh, E);
   const bool use_tc = (path == LG_PATH_TENSOR) ||
                       (path == LG_PATH_AUTO && tiles_ok && P + (with_sh ? T : 0) > 512);
-  if (use_tc)
-    rc = launch_tc(a, max_groups, w.tc, st);
-  else
+  if (use_tc) {
+    rc = launch_tc(a, max_groups, w.tc, st);  // clears the status word itself
+  } else {
+    LG_CUDA_TRY(cudaMemsetAsync(a.err, 0, sizeof(int), st));
     rc = launch_gemv(a, max_groups, st);
+  }
   if (rc) return rc;
   if (mode == 0)
     return launch_combine(w.yrows, inds, static_cast<const __nv_bfloat16*>(weights), T, a.k, E, H,

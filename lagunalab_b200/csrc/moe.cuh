@@ -40,7 +40,12 @@ struct GemvArgs {
   int h_stride;
   __nv_bfloat16* ypick;    // [P (+ T with the shared expert), H] per-pick down outputs
   EpRet ep;                // expert-parallel return (ep.on), replacing ypick
+  int* err;                // status word: a bounded wait that expired records a code here
 };
+
+// The status word of the tensor-core workspace (lg_moe_status reads it); the GEMV kernels
+// record their expired waits there too.
+int* tc_err_word(void* tc_ws, int T, int H, int I, int I_sh, int E, int k);
 
 int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32_t* counts,
                 int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s);

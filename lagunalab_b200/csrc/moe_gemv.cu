@@ -20,6 +20,7 @@
 //   row (routed picks, then the shared expert's rows); the weighted combine of
 //   laguna.py:149-150 is a separate fixed-order pass over those rows.
 #include "common.cuh"
+#include "decode_core.cuh"
 #include "gemv_core.cuh"
 #include "moe.cuh"
 
@@ -30,11 +31,43 @@ namespace lg {
 __device__ __forceinline__ int row_token(int p, int P, int k) { return p < P ? p / k : p - P; }
 
 constexpr int GV_WARPS = 4;
+// dynamic shared memory: [0, 128) mbarrier and wait flag, then the cross-warp reduction, then
+// (staged kernels) the weight tile(s) in the padded layout of decode_core.cuh
+constexpr uint32_t GV_HDR = 128;
+constexpr uint32_t GV_RED_GU = GV_WARPS * 2 * 32 * 4 * 4;
+constexpr uint32_t GV_RED_DN = GV_WARPS * 32 * 4 * 4;
+constexpr long long GV_WAIT_CYCLES = 400000000LL;  // ~0.2 s: the tile copies are long done
 
+static uint32_t gv_smem_gu(int H, bool staged) {
+  return GV_HDR + GV_RED_GU + (staged ? 2 * tile_bytes(H) : 0);
+}
+static uint32_t gv_smem_dn(int Kmax, bool staged) {
+  return GV_HDR + GV_RED_DN + (staged ? tile_bytes(Kmax) : 0);
+}
+
+// STAGED: the CTA's whole weight tile (16 code rows, their scales and biases) comes into shared
+// memory by bulk copies issued by one thread as soon as the group is known, so every byte of
+// the tile is in flight at once and no registers hold loads in flight (more CTAs per SM); the
+// arithmetic and its order are the same as the register-streaming form (!STAGED, used when a
+// matrix is not 16-row tiled or not 16-byte aligned).
+// Waits for the staged tile; false (recorded in a.err, every copy drained, bounded) when it
+// never arrives. Whole CTA.
+__device__ __forceinline__ bool gv_tile_wait(uint64_t* bar, int* berr, int* err) {
+  const bool ok = __syncthreads_and(mbar_wait(bar, 0, berr, 1, GV_WAIT_CYCLES));
+  if (!ok && threadIdx.x == 0) {
+    if (err) atomicCAS(err, 0, 0x47);  // 'G': a staged GEMV tile never arrived
+    for (const long long t0 = clock64(); !mbar_try_wait(bar, 0) && clock64() - t0 < GV_WAIT_CYCLES;) {
+    }
+  }
+  return ok;
+}
+
+template <bool STAGED>
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t gv_smem[];
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
-  __shared__ float red[GV_WARPS][2][32][4];
+  float (*red)[2][32][4] = reinterpret_cast<float (*)[2][32][4]>(gv_smem + GV_HDR);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int na = a.active[0];
   if ((int)blockIdx.y >= na) return;
@@ -43,7 +76,6 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
   const int Ig = sh ? a.I_sh : a.I;
   const int m0 = blockIdx.x * 16;
   if (m0 >= Ig) return;
-  const int row0 = a.offsets[g], cnt = a.offsets[g + 1] - row0;
   const int H = a.H;
   const int wpr = H / 8;         // words per weight row
   const int gpr = H / 64;        // groups per row
@@ -55,20 +87,48 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
   const __nv_bfloat16* ub = sh ? a.su_b : a.u_b + (size_t)g * a.I * gpr;
   const int r = lane >> 2, c4 = lane & 3;
   const int ra = m0 + r, rb = m0 + r + 8;
-
-  for (int tb = 0; tb < cnt; tb += 8) {
-    const int tn = tb + r;  // this thread's B-fragment token (row of the group)
+  // staged: rows r / r + 8 of the two tiles, and their scale and bias rows, in shared memory
+  uint8_t* ring = gv_smem + GV_HDR + GV_RED_GU;
+  const uint32_t tb = tile_bytes(H), pitch = tile_pitch(H);
+  if constexpr (STAGED) {
+    uint64_t* bar = reinterpret_cast<uint64_t*>(gv_smem);
+    int* berr = reinterpret_cast<int*>(gv_smem + 8);
+    if (threadIdx.x == 0) {
+      *berr = 0;
+      mbar_init(bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(bar, 2u * tile_bulk_bytes(H));
+      tile_load_bulk(ring, gq, gs, gb, m0, H, bar);
+      tile_load_bulk(ring + tb, uq, us, ub, m0, H, bar);
+    }
+    __syncthreads();  // the barrier is initialised before anyone polls it
+    if (!gv_tile_wait(bar, berr, a.err)) return;
+  }
+  const __nv_bfloat16* tgs = reinterpret_cast<const __nv_bfloat16*>(ring + tile_sc_off(H));
+  const __nv_bfloat16* tus = reinterpret_cast<const __nv_bfloat16*>(ring + tb + tile_sc_off(H));
+  const int row0 = a.offsets[g], cnt = a.offsets[g + 1] - row0;
+  for (int t8 = 0; t8 < cnt; t8 += 8) {
+    const int tn = t8 + r;  // this thread's B-fragment token (row of the group)
     const bool tval = tn < cnt;
     const int tok = tval ? row_token(a.perm[row0 + tn], a.P, a.k) : 0;
     const __nv_bfloat16* xrow = a.x + (size_t)tok * H;
     float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
+#pragma unroll(STAGED ? 1 : 2)
     for (int gg = warp; gg < gpr; gg += GV_WARPS) {
       const size_t wo = (size_t)gg * 8 + 2 * c4;
-      const uint2 g0 = *reinterpret_cast<const uint2*>(gq + (size_t)ra * wpr + wo);
-      const uint2 g8 = *reinterpret_cast<const uint2*>(gq + (size_t)rb * wpr + wo);
-      const uint2 u0 = *reinterpret_cast<const uint2*>(uq + (size_t)ra * wpr + wo);
-      const uint2 u8 = *reinterpret_cast<const uint2*>(uq + (size_t)rb * wpr + wo);
+      uint2 g0, g8, u0, u8;
+      if constexpr (STAGED) {
+        const uint32_t o0 = r * pitch + gg * 32 + c4 * 8, o8 = o0 + 8 * pitch;
+        g0 = *reinterpret_cast<const uint2*>(ring + o0);
+        g8 = *reinterpret_cast<const uint2*>(ring + o8);
+        u0 = *reinterpret_cast<const uint2*>(ring + tb + o0);
+        u8 = *reinterpret_cast<const uint2*>(ring + tb + o8);
+      } else {
+        g0 = *reinterpret_cast<const uint2*>(gq + (size_t)ra * wpr + wo);
+        g8 = *reinterpret_cast<const uint2*>(gq + (size_t)rb * wpr + wo);
+        u0 = *reinterpret_cast<const uint2*>(uq + (size_t)ra * wpr + wo);
+        u8 = *reinterpret_cast<const uint2*>(uq + (size_t)rb * wpr + wo);
+      }
       uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
       if (tval) {
         xa0 = *reinterpret_cast<const uint4*>(xrow + gg * 64 + 16 * c4);
@@ -80,10 +140,17 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
       xs += __shfl_xor_sync(0xffffffffu, xs, 2);
       const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
       const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
-      const float sg0 = bf2f(gs[(size_t)ra * gpr + gg]), sg8 = bf2f(gs[(size_t)rb * gpr + gg]);
-      const float bg0 = bf2f(gb[(size_t)ra * gpr + gg]), bg8 = bf2f(gb[(size_t)rb * gpr + gg]);
-      const float su0 = bf2f(us[(size_t)ra * gpr + gg]), su8 = bf2f(us[(size_t)rb * gpr + gg]);
-      const float bu0 = bf2f(ub[(size_t)ra * gpr + gg]), bu8 = bf2f(ub[(size_t)rb * gpr + gg]);
+      float sg0, sg8, bg0, bg8, su0, su8, bu0, bu8;
+      if constexpr (STAGED) {  // the tile's scales [16][gpr], then its biases [16][gpr]
+        const int i0 = r * gpr + gg, i8 = i0 + 8 * gpr, nb = 16 * gpr;
+        sg0 = bf2f(tgs[i0]); sg8 = bf2f(tgs[i8]); bg0 = bf2f(tgs[nb + i0]); bg8 = bf2f(tgs[nb + i8]);
+        su0 = bf2f(tus[i0]); su8 = bf2f(tus[i8]); bu0 = bf2f(tus[nb + i0]); bu8 = bf2f(tus[nb + i8]);
+      } else {
+        sg0 = bf2f(gs[(size_t)ra * gpr + gg]); sg8 = bf2f(gs[(size_t)rb * gpr + gg]);
+        bg0 = bf2f(gb[(size_t)ra * gpr + gg]); bg8 = bf2f(gb[(size_t)rb * gpr + gg]);
+        su0 = bf2f(us[(size_t)ra * gpr + gg]); su8 = bf2f(us[(size_t)rb * gpr + gg]);
+        bu0 = bf2f(ub[(size_t)ra * gpr + gg]); bu8 = bf2f(ub[(size_t)rb * gpr + gg]);
+      }
       float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
       group_mma(dg, g0, g8, xa0, xa1);
       group_mma(du, u0, u8, xa0, xa1);
@@ -111,7 +178,7 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
           gv += red[w][0][lane][j];
           uv += red[w][1][lane][j];
         }
-        const int col = tb + 2 * c4 + (j & 1);   // group row (token tile column)
+        const int col = t8 + 2 * c4 + (j & 1);   // group row (token tile column)
         const int n = (j < 2) ? ra : rb;        // intermediate index
         if (col < cnt) {
           const float gr = round_bf16(gv), ur = round_bf16(uv);
@@ -125,10 +192,12 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
   }
 }
 
+template <bool STAGED>
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t gv_smem[];
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
-  __shared__ float red[GV_WARPS][32][4];
+  float (*red)[32][4] = reinterpret_cast<float (*)[32][4]>(gv_smem + GV_HDR);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int na = a.active[0];
   if ((int)blockIdx.y >= na) return;
@@ -145,17 +214,40 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
   const __nv_bfloat16* db = sh ? a.sd_b : a.d_b + (size_t)g * H * (a.I / 64);
   const int r = lane >> 2, c4 = lane & 3;
   const int ra = m0 + r, rb = m0 + r + 8;
+  uint8_t* tile = gv_smem + GV_HDR + GV_RED_DN;
+  const uint32_t pitch = tile_pitch(Kg);
+  if constexpr (STAGED) {
+    uint64_t* bar = reinterpret_cast<uint64_t*>(gv_smem);
+    int* berr = reinterpret_cast<int*>(gv_smem + 8);
+    if (threadIdx.x == 0) {
+      *berr = 0;
+      mbar_init(bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(bar, tile_bulk_bytes(Kg));
+      tile_load_bulk(tile, dq, ds, db, m0, Kg, bar);
+    }
+    __syncthreads();  // the barrier is initialised before anyone polls it
+    if (!gv_tile_wait(bar, berr, a.err)) return;
+  }
+  const __nv_bfloat16* tds = reinterpret_cast<const __nv_bfloat16*>(tile + tile_sc_off(Kg));
 
-  for (int tb = 0; tb < cnt; tb += 8) {
-    const int tn = tb + r;
+  for (int t8 = 0; t8 < cnt; t8 += 8) {
+    const int tn = t8 + r;
     const bool tval = tn < cnt;
     const __nv_bfloat16* hrow = a.h + (size_t)(row0 + (tval ? tn : 0)) * a.h_stride;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
+#pragma unroll(STAGED ? 1 : 2)
     for (int gg = warp; gg < gpr; gg += GV_WARPS) {
       const size_t wo = (size_t)gg * 8 + 2 * c4;
-      const uint2 w0 = *reinterpret_cast<const uint2*>(dq + (size_t)ra * wpr + wo);
-      const uint2 w8 = *reinterpret_cast<const uint2*>(dq + (size_t)rb * wpr + wo);
+      uint2 w0, w8;
+      if constexpr (STAGED) {
+        const uint32_t o0 = r * pitch + gg * 32 + c4 * 8;
+        w0 = *reinterpret_cast<const uint2*>(tile + o0);
+        w8 = *reinterpret_cast<const uint2*>(tile + o0 + 8 * pitch);
+      } else {
+        w0 = *reinterpret_cast<const uint2*>(dq + (size_t)ra * wpr + wo);
+        w8 = *reinterpret_cast<const uint2*>(dq + (size_t)rb * wpr + wo);
+      }
       uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
       if (tval) {
         xa0 = *reinterpret_cast<const uint4*>(hrow + gg * 64 + 16 * c4);
@@ -166,8 +258,14 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
       xs += __shfl_xor_sync(0xffffffffu, xs, 2);
       const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
       const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
-      const float s0 = bf2f(ds[(size_t)ra * gpr + gg]), s8 = bf2f(ds[(size_t)rb * gpr + gg]);
-      const float b0 = bf2f(db[(size_t)ra * gpr + gg]), b8 = bf2f(db[(size_t)rb * gpr + gg]);
+      float s0, s8, b0, b8;
+      if constexpr (STAGED) {
+        const int i0 = r * gpr + gg, i8 = i0 + 8 * gpr, nb = 16 * gpr;
+        s0 = bf2f(tds[i0]); s8 = bf2f(tds[i8]); b0 = bf2f(tds[nb + i0]); b8 = bf2f(tds[nb + i8]);
+      } else {
+        s0 = bf2f(ds[(size_t)ra * gpr + gg]); s8 = bf2f(ds[(size_t)rb * gpr + gg]);
+        b0 = bf2f(db[(size_t)ra * gpr + gg]); b8 = bf2f(db[(size_t)rb * gpr + gg]);
+      }
       float d[4] = {0.f, 0.f, 0.f, 0.f};
       group_mma(d, w0, w8, xa0, xa1);
       acc[0] += s0 * d[0] + b0 * xs0;
@@ -184,7 +282,7 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < GV_WARPS; ++w) v += red[w][lane][j];
-        const int col = tb + 2 * c4 + (j & 1);
+        const int col = t8 + 2 * c4 + (j & 1);
         const int n = (j < 2) ? ra : rb;
         if (col < cnt) {
           const int p = a.perm[row0 + col];
@@ -205,17 +303,42 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_down_kernel(GemvArgs a
   if (a.ep.on) __threadfence_system();  // peer stores visible before the signal
 }
 
+// The staged kernels need whole 16-row tiles and 16-byte aligned rows, scale and bias blocks
+// (every tile's rows start at a multiple of 16 rows); otherwise the register-streaming form.
+static bool gv_aligned(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static bool gv_stageable(const GemvArgs& a) {
+  bool ok = a.H % 16 == 0 && a.I % 16 == 0 && a.I_sh % 16 == 0;
+  const void* ps[] = {a.g_q, a.u_q, a.d_q, a.g_s, a.g_b, a.u_s, a.u_b, a.d_s, a.d_b,
+                      a.sg_q, a.su_q, a.sd_q, a.sg_s, a.sg_b, a.su_s, a.su_b, a.sd_s, a.sd_b};
+  for (const void* p : ps) ok = ok && (p == nullptr || gv_aligned(p));
+  return ok;
+}
+
+template <typename K>
+static cudaError_t gv_launch(K kernel, dim3 grid, uint32_t smem, cudaStream_t s, const GemvArgs& a) {
+  if (smem > 48u * 1024u) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_k(kernel, grid, dim3(GV_WARPS * 32), smem, s, a);
+}
+
 int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s) {
   if (max_groups <= 0) return LG_OK;
+  const bool staged = gv_stageable(a);
   const int Imax = a.I > a.I_sh ? a.I : a.I_sh;
   dim3 g1((Imax + 15) / 16, max_groups);
   prof_begin("experts_gateup", s);
-  LG_CUDA_TRY(launch_k(moe_gemv_gateup_kernel, g1, dim3(GV_WARPS * 32), 0, s, a));
+  LG_CUDA_TRY(staged ? gv_launch(moe_gemv_gateup_kernel<true>, g1, gv_smem_gu(a.H, true), s, a)
+                     : gv_launch(moe_gemv_gateup_kernel<false>, g1, gv_smem_gu(a.H, false), s, a));
   prof_end("experts_gateup", s);
   LG_LAUNCH_CHECK("moe_gemv_gateup");
   dim3 g2((a.H + 15) / 16, max_groups);
   prof_begin("experts_down", s);
-  LG_CUDA_TRY(launch_k(moe_gemv_down_kernel, g2, dim3(GV_WARPS * 32), 0, s, a));
+  LG_CUDA_TRY(staged ? gv_launch(moe_gemv_down_kernel<true>, g2, gv_smem_dn(Imax, true), s, a)
+                     : gv_launch(moe_gemv_down_kernel<false>, g2, gv_smem_dn(Imax, false), s, a));
   prof_end("experts_down", s);
   LG_LAUNCH_CHECK("moe_gemv_down");
   return LG_OK;

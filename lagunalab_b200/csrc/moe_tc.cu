@@ -729,6 +729,12 @@ int launch_tc(const GemvArgs& a, int max_groups, void* tc_ws, cudaStream_t st) {
 
 // Status word of the last tensor-core launch in this workspace (0 = ok; otherwise the role
 // whose bounded wait expired). Synchronous; for tests and diagnostics.
+int* tc_err_word(void* tc_ws, int T, int H, int I, int I_sh, int E, int k) {
+  TcWs w;
+  carve_tc(tc_ws, T, H, I, I_sh, E, k, &w);
+  return w.counts + 2;
+}
+
 int tc_status(const void* tc_ws, int T, int H, int I, int I_sh, int E, int k, int* status) {
   TcWs w;
   carve_tc(const_cast<void*>(tc_ws), T, H, I, I_sh, E, k, &w);

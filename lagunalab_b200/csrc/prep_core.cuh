@@ -35,6 +35,10 @@ struct PrepArgs {
   float mscale;           // YaRN attention factor on the rotated dims (1: none)
   int ring;               // > 0: cache row = position mod ring (sliding window)
   int row0;               // linear caches: cache row = position - row0
+  // 0: the T tokens are consecutive positions of one sequence (pos + t); 1: token t is the
+  // newest token of stream t, at position pos_dev[t] (or pos_host), and the caches hold T
+  // streams [T, Hkv, cap, D] (batched decode)
+  int streams;
   __nv_bfloat16* q_out;
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
@@ -132,8 +136,10 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
                                                bool write_gate, uint8_t* sb) {
   constexpr int D = 64 * P;
   const int l = threadIdx.x & 31;
-  const int pos = (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
+  const int pos = a.streams ? (a.pos_dev ? a.pos_dev[t] : a.pos_host)
+                            : (a.pos_dev ? a.pos_dev[0] : a.pos_host) + t;
   const int crow = a.ring > 0 ? pos % a.ring : pos - a.row0;  // the position's cache row
+  const size_t srow = a.streams ? (size_t)t * a.Hkv * a.cap : 0;  // the stream's first row
   const int row_stride = (a.Hq + 2 * a.Hkv) * D + (a.gate_per_head ? a.Hq : a.Hq * D);
   const __nv_bfloat16* row = a.qkvg + (size_t)t * row_stride;
   float x[2 * P];
@@ -144,9 +150,9 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
     if (a.vq) {
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) x[k] = bf2f(__ldcg(src + l + 32 * k));
-      quantize_row8_warp<P>(x, (size_t)h * a.cap + crow, a.vq, a.vs, a.vb, sb);
+      quantize_row8_warp<P>(x, srow + (size_t)h * a.cap + crow, a.vq, a.vs, a.vb, sb);
     } else {
-      __nv_bfloat16* dst = a.v_cache + ((size_t)h * a.cap + crow) * D;
+      __nv_bfloat16* dst = a.v_cache + (srow + (size_t)h * a.cap + crow) * D;
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __ldcg(src + l + 32 * k);
     }
@@ -184,7 +190,8 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
     if constexpr (P >= 4) if (Pr == 4) rope_table<P, 4>(x, a, pos, l);
   }
   if (is_q) {
-    __nv_bfloat16* dst = a.q_out + ((size_t)h * a.T + t) * D;
+    // q_out: [Hq, T, D], or [T, Hq, D] for streams (the batched attention's layout)
+    __nv_bfloat16* dst = a.q_out + (a.streams ? (size_t)t * a.Hq + h : (size_t)h * a.T + t) * D;
 #pragma unroll
     for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __float2bfloat16_rn(x[k]);
     if (write_gate) {
@@ -202,9 +209,9 @@ __device__ __forceinline__ void prep_head_warp(const PrepArgs& a, int t, int slo
     if (a.kq) {
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) x[k] = round_bf16(x[k]);
-      quantize_row8_warp<P>(x, (size_t)h * a.cap + crow, a.kq, a.ks, a.kb, sb);
+      quantize_row8_warp<P>(x, srow + (size_t)h * a.cap + crow, a.kq, a.ks, a.kb, sb);
     } else {
-      __nv_bfloat16* dst = a.k_cache + ((size_t)h * a.cap + crow) * D;
+      __nv_bfloat16* dst = a.k_cache + (srow + (size_t)h * a.cap + crow) * D;
 #pragma unroll
       for (int k = 0; k < 2 * P; ++k) dst[l + 32 * k] = __float2bfloat16_rn(x[k]);
     }

@@ -197,9 +197,10 @@ __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloa
   }
 }
 
-// ---- small-T router logits (decode): one warp per expert -------------------------------
+// ---- small-T router logits (decode): one warp per (expert, token) --------------------------
 // Lanes stride over the hidden dimension two elements at a time (coalesced bf16x2 / float2
-// loads; the weight row stays in L1 across the T <= 32 tokens) and reduce across the warp.
+// loads) and reduce across the warp; the tokens are spread over blockIdx.y, so the T <= 32
+// tokens' dot products run in parallel and each weight row is re-read from L2.
 template <int GBITS>
 __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int H, const void* __restrict__ gw,
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
   const int lane = threadIdx.x & 31;
   const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (e >= E) return;
-  for (int t = 0; t < T; ++t) {
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {  // tokens spread over blockIdx.y
     const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (size_t)t * H);
     if (GBITS == 8) {  // the fused one-token router computes the same function
       const float v = router_logit8(xr, static_cast<const uint32_t*>(gw) + (size_t)e * (H / 4),
@@ -357,14 +358,15 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
   const bool xa = aligned(x, 16) && aligned(gate_w, 16);
   prof_begin("router_logits", s);
   if (T <= 32) {
-    // decode: one warp per expert, weight row in registers
+    // decode sizes: one warp per (expert, token)
     const __nv_bfloat16* nb = nullptr;
+    const dim3 grid((E + 7) / 8, T);  // one (8 experts, token) per CTA: the rows come from L2
     if (gate_bits == 0)
-      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<0>, dim3((E + 7) / 8), dim3(256), 0, s, xb, T,
-                           H, gate_w, nb, nb, E, logits));
+      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<0>, grid, dim3(256), 0, s, xb, T, H, gate_w,
+                           nb, nb, E, logits));
     else
-      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<8>, dim3((E + 7) / 8), dim3(256), 0, s, xb, T,
-                           H, gate_w, gsb, gbb, E, logits));
+      LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<8>, grid, dim3(256), 0, s, xb, T, H, gate_w,
+                           gsb, gbb, E, logits));
   } else if (gate_bits == 0 && xa) {
     dim3 g((E + RM_EB - 1) / RM_EB, (T + RM_TT - 1) / RM_TT);
     LG_CUDA_TRY(launch_k(router_logits_mma_kernel, g, dim3(128), 0, s, xb, T, H,

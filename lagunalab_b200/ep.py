@@ -132,9 +132,15 @@ class PeerExpertParallel:
     Outputs equal the one-GPU block's bit for bit when both take the same product path: the
     owners run the tensor-core path when the capacity exceeds 512 / (k + 1) tokens, as the
     one-GPU block does for that many tokens.
+
+    ``device_epoch=True``: the forwards' epochs are counted on the device (every call passes
+    epoch 0 and ends with ``lg_ep_advance``), so a forward can be captured in a CUDA graph and
+    replayed (batched decode steps); ``expert_path`` forces the owners' product path
+    (``_lib.LG_PATH_*``) instead of the capacity rule.
     """
 
-    def __init__(self, blk, capacity, group=None, timeout_s=5.0):
+    def __init__(self, blk, capacity, group=None, timeout_s=5.0, device_epoch=False,
+                 expert_path=None):
         from . import _lib, ops
         self.lib = _lib.lib()
         self.blk = blk
@@ -185,6 +191,9 @@ class PeerExpertParallel:
         # the owner's path for the received rows: the same on every rank (by the capacity)
         self.expert_path = _lib.LG_PATH_TENSOR if self.cap * (self.k + 1) > 512 \
             else _lib.LG_PATH_GEMV
+        if expert_path is not None:
+            self.expert_path = int(expert_path)
+        self.device_epoch = bool(device_epoch)
         self.epoch = 0
         torch.cuda.synchronize(self.dev)
         dist.barrier(group=group)  # every peer mapped before anyone writes
@@ -197,6 +206,7 @@ class PeerExpertParallel:
         if T > self.cap:
             raise ValueError(f"{T} tokens exceed the capacity {self.cap}")
         self.epoch += 1
+        ep_arg = 0 if self.device_epoch else self.epoch
         st = torch.cuda.current_stream(self.dev).cuda_stream
         if T:
             inds, w = self.blk.route(x2)
@@ -206,7 +216,7 @@ class PeerExpertParallel:
             w = torch.empty(0, self.k, dtype=torch.bfloat16, device=self.dev)
         arenas = ctypes.addressof(self.ptrs)
         _lib.call("lg_ep_dispatch", x2.data_ptr(), inds.data_ptr(), w.data_ptr(), T, self.cap,
-                  H, self.k, self.E, self.W, self.rank, arenas, self.epoch, st)
+                  H, self.k, self.E, self.W, self.rank, arenas, ep_arg, st)
         # the product path the one-GPU block takes for these tokens (tensor cores above 512
         # pick rows), so that the outputs equal it bit for bit
         big = T * (self.k + 1) > 512
@@ -216,12 +226,14 @@ class PeerExpertParallel:
         g, u, d = (ops._qm(m) for m in self.local.mats)
         _lib.call("lg_ep_experts", self.W, self.cap, H, self.I, self.El, self.k,
                   *(t.data_ptr() for t in g), *(t.data_ptr() for t in u),
-                  *(t.data_ptr() for t in d), self.rank, arenas, self.epoch, self.timeout,
+                  *(t.data_ptr() for t in d), self.rank, arenas, ep_arg, self.timeout,
                   self.expert_path, self.ws.data_ptr(), self.ws_bytes, st)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
         _lib.call("lg_ep_combine", inds.data_ptr(), T, self.cap, H, self.k, self.E,
                   float(self.blk.routed_scaling_factor), int(sh is not None), self.W, self.rank,
-                  arenas, self.epoch, self.timeout, out.data_ptr(), st)
+                  arenas, ep_arg, self.timeout, out.data_ptr(), st)
+        if self.device_epoch:
+            _lib.call("lg_ep_advance", self.arena.data_ptr(), st)
         return out.reshape(*lead, H)
 
     def status(self, reset=True):

@@ -566,6 +566,33 @@ class Attention:
         out = self.o_proj(o, residual=None if residual is None else residual.reshape(L, H))
         return out.reshape(B, L, H)
 
+    def step_streams(self, xn, cache, pos_dev, residual=None):
+        """One decode step of B independent streams (batched decode, BASELINE config 5; the
+        reference decodes one sequence per cache, laguna_mlx/cache.py has no batch merge):
+        ``xn`` [B, H] the normalised inputs, one token per stream; ``cache`` a KVCache (or a
+        sliding layer's RotatingKVCache) reserved for the B streams [B, Hkv, cap, D];
+        ``pos_dev`` device int32 [B], the new tokens' positions. Returns o_proj(attention)
+        [+ residual] as [B, H]."""
+        B, H = xn.shape
+        Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
+        if getattr(cache, "q", None) is not None:
+            raise NotImplementedError("batched decode runs over bf16 caches")
+        ring = cache.max_size if isinstance(cache, RotatingKVCache) else 0
+        if cache.keys is None or cache.keys.shape[0] != B:
+            raise ValueError(f"the cache must be reserved for the {B} streams")
+        qkvg = self._qkvg(xn)
+        per_head = self.per_head_gate
+        q, gate = ops.attn_prep_streams(qkvg, Hq, Hkv, D, self.q_norm.weight, self.k_norm.weight,
+                                        self.eps, self.rope_theta, cache.keys, cache.values,
+                                        pos_dev, gate_per_head=per_head, rope=self.rope,
+                                        ring=ring)
+        o = ops.bf16_decode_attention_streams(q, cache.keys, cache.values, pos_dev, 1, self.scale,
+                                              gate=gate if per_head else None)
+        o = o.view(B, Hq * D)
+        if not per_head:
+            o = o * gate.view(B, Hq * D)
+        return self.o_proj(o, residual=residual)
+
     def _fused_token(self, x, cache, residual, pos_dev, in_norm):
         """A device-position single-token step with the q/k/v/g projection and the attention
         prologue in one launch (``ops.decode_qkv_prep``); None when the shape needs the
@@ -755,6 +782,22 @@ class LagunaModel:
             x, xn = ops.rmsnorm(m, nxt.weight, nxt.eps, residual=h)
         return xn
 
+    def step_streams(self, ids, cache, pos_dev, moe=None):
+        """Final normalised hidden states [B, H] of one decode step of B independent streams:
+        ``ids`` device int32 [B] (each stream's newest token), ``cache`` from
+        ``Model.make_stream_cache``, ``pos_dev`` device int32 [B] (the tokens' positions).
+        ``moe``: per layer a callable that replaces the MLP sub-block's forward on the
+        normalised [B, H] rows (the expert-parallel block), or None for the layer's own."""
+        x = self.embed_tokens(ids.reshape(1, -1)).reshape(ids.shape[0], -1)
+        xn = self.layers[0].input_layernorm(x)
+        for i, (layer, c) in enumerate(zip(self.layers, cache)):
+            h = layer.self_attn.step_streams(xn, c, pos_dev, residual=x)
+            fwd = moe[i] if moe is not None and moe[i] is not None else layer.mlp
+            m = fwd(layer.post_attention_layernorm(h))
+            nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else self.norm
+            x, xn = ops.rmsnorm(m, nxt.weight, nxt.eps, residual=h)
+        return xn
+
     def _token(self, x, cache, pos_dev):
         """One token through every layer: per layer the input norm runs inside the q/k/v/g
         GEMV, the attention residual inside o_proj, and the MLP sub-block (norm, router,
@@ -793,6 +836,26 @@ class Model:
                                    norm=(n.weight, n.eps)).reshape(1, 1, -1)
         h = self.model(ids, cache, pos_dev=pos_dev)
         return self.lm_head(h[:, -1:])
+
+    def step_streams(self, ids, cache, pos_dev, moe=None):
+        """Logits [B, V] of one decode step of B independent streams (see
+        ``LagunaModel.step_streams``); the caller advances ``pos_dev``."""
+        return self.lm_head(self.model.step_streams(ids, cache, pos_dev, moe))
+
+    def make_stream_cache(self, B, capacity, device="cuda"):
+        """Per layer a bf16 cache holding B streams of ``capacity`` rows each ([B, Hkv,
+        capacity, D]; a sliding layer's ring holds its window), for ``step_streams``."""
+        a = self.args
+        out = []
+        for L in self.layers:
+            at = L.self_attn
+            c = RotatingKVCache(at.window) if at.window else KVCache(capacity)
+            if at.window:
+                c.reserve(B, a.num_key_value_heads, a.head_dim, device)
+            else:
+                c.reserve(B, a.num_key_value_heads, a.head_dim, capacity, device)
+            out.append(c)
+        return out
 
     @property
     def layers(self):
@@ -979,6 +1042,41 @@ class DecodeGraph:
     def position(self):
         """Tokens in the cache now (host copy of the device counter)."""
         return int(self.pos.item())
+
+
+class StreamDecodeGraph:
+    """Greedy decoding of B independent streams, one CUDA-graph replay per step (BASELINE
+    config 5's batched decode). The streams' newest tokens ``tok`` and positions ``pos``
+    (device int32 [B]) stay on the device: each replay embeds the B tokens, runs every layer
+    over the B streams' own caches, writes each stream's argmax into ``tok`` and advances every
+    position. ``moe`` (optional, per layer): expert-parallel MoE forwards with device-held
+    epochs, whose exchanges replay with the graph. The first step runs eagerly (it also sizes
+    every workspace) before the graph is captured."""
+
+    def __init__(self, model, cache, tok, pos, moe=None):
+        self.model, self.cache, self.moe = model, cache, moe
+        self.tok = tok.reshape(-1).to(torch.int32).clone()
+        self.pos = pos.reshape(-1).to(torch.int32).clone()
+        full = [c for c in cache if not isinstance(c, RotatingKVCache)]
+        self.cap = full[0].keys.shape[2] if full else 1 << 30
+        self._body()
+        self.first_logits = self.logits.clone()
+        self.steps = 1
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+
+    def _body(self):
+        logits = self.model.step_streams(self.tok, self.cache, self.pos, self.moe)
+        ops.argmax(logits, ids=self.tok)
+        self.pos.add_(1)
+        self.logits = logits  # the captured step's logits buffer: valid after each replay
+
+    def step(self):
+        """One token per stream (asynchronous); ``tok`` holds them afterwards."""
+        self.graph.replay()
+        self.steps += 1
 
 
 def generate(model, prompt, max_tokens, cache=None):

@@ -296,14 +296,15 @@ def rmsnorm(x, w, eps, residual=None, sum_out=None):
 
 def qlinear(x, mat, residual=None, group_size=64, bits=4, out=None):
     """x [..., K] bf16 @ W^T for an MLX 4-bit [N, K] matrix -> [..., N] bf16 (+ residual).
-    Decode sizes (<= 16 rows) run the tensor-core GEMV; larger inputs dequantize W to bf16
-    and use a dense GEMM (fp32 accumulate, one bf16 rounding)."""
+    Decode sizes (<= 64 rows: a bs1 step, or one token of each of up to 64 streams) run the
+    tensor-core GEMV; larger inputs dequantize W to bf16 and use a dense GEMM (fp32
+    accumulate, one bf16 rounding)."""
     q, s, b = _qm(mat)
     K = x.shape[-1]
     N = q.shape[0]
     x2 = _c(x, torch.bfloat16).reshape(-1, K)
     T = x2.shape[0]
-    if T > 16:
+    if T > 64:
         w = dequantize(q, s, b, group_size, bits)
         y = x2 @ w.t()
         if residual is not None:
@@ -505,6 +506,25 @@ def attn_prep(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos=0,
     return q, gate
 
 
+def attn_prep_streams(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, k_cache, v_cache, pos_dev,
+                      gate_per_head=True, rope=None, ring=0):
+    """One decode step of B independent streams: row t of the fused projections qkvg [B, .] is
+    stream t's newest token, at position pos_dev[t] (device int32 [B]); its k, v rows go into
+    stream t's caches [B, Hkv, cap, D] (row = position, or position mod ``ring``). Returns
+    (q [B, Hq, D] normed + roped, gate [B, Hq or Hq*D])."""
+    qkvg = _c(qkvg, torch.bfloat16)
+    B = qkvg.shape[0]
+    cap = k_cache.shape[-2]
+    q = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=qkvg.device)
+    gate = torch.empty(B, Hq if gate_per_head else Hq * D, dtype=torch.bfloat16, device=qkvg.device)
+    inv, rot, ms, ring, _ = _rope_args(rope, ring, 0)
+    _lib.call("lg_attn_prep_streams", _p(qkvg), B, Hq, Hkv, D, _p(_c(qn_w)), _p(_c(kn_w)),
+              float(eps), float(theta), _p(_c(pos_dev, torch.int32)), int(bool(gate_per_head)),
+              _p(q), _p(k_cache), _p(v_cache), cap, _p(gate), inv, rot, ms, ring,
+              _stream(qkvg.device))
+    return q, gate
+
+
 def attn_prep_q8(qkvg, Hq, Hkv, D, qn_w, kn_w, eps, theta, keys, values, pos=0, pos_dev=None,
                  gate_per_head=True, rope=None, ring=0, row0=0):
     """attn_prep with an 8-bit group-64 cache: the new k, v rows are quantized into rows
@@ -558,6 +578,26 @@ def bf16_decode_attention(q, k_cache, v_cache, n, scale, gate=None, n_dev=None, 
     _lib.call("lg_bf16_decode_attention", _p(q), B, Hq, Hkv, D, _p(k_cache), _p(v_cache), cap,
               int(n), _p(n_dev), int(n_add), n_plan, float(scale), _p(_c(gate)), _p(out),
               _p(ws), ws.numel(), _stream(q.device))
+    return out
+
+
+def bf16_decode_attention_streams(q, k_cache, v_cache, n_dev, n_add, scale, gate=None,
+                                  n_plan=None, out=None):
+    """Single-token attention of B independent streams over their bf16 caches [B, Hkv, cap, D]:
+    stream b attends over n_dev[b] + n_add keys (device int32 [B]; clamped to cap, so a
+    sliding window's ring gives min(position + 1, window)). q [B, Hq, D]; gate [B, Hq]
+    per-head or None. Returns [B, Hq, D] bf16 (gated)."""
+    q = _c(q, torch.bfloat16)
+    B, Hq, D = q.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    n_plan = cap if n_plan is None else int(n_plan)
+    nb = _lib.lib().lg_bf16_decode_workspace_bytes(B, Hq, Hkv, n_plan)
+    ws = workspace(q.device, "bf16_attn", nb, zero=True)
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.call("lg_bf16_decode_attention_streams", _p(q), B, Hq, Hkv, D, _p(k_cache),
+              _p(v_cache), cap, _p(_c(n_dev, torch.int32)), int(n_add), n_plan, float(scale),
+              _p(_c(gate)), _p(out), _p(ws), ws.numel(), _stream(q.device))
     return out
 
 

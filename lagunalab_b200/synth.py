@@ -297,6 +297,43 @@ def fill_q8_cache(cache, n, seed=0):
         del k, v
 
 
+def zipf_router(model, seed=0):
+    """Zipf(1.1)-skewed routing for every MoE layer of a decoder: each
+    layer's selection-only bias becomes ``zipf_bias`` with its own seeded permutation."""
+    for i, L in enumerate(model.layers):
+        m = L.mlp
+        if isinstance(m, laguna.SparseMoeBlock):
+            dev = m.e_score_correction_bias.device
+            m.e_score_correction_bias = zipf_bias(m.num_experts, seed + 1000 * i, device=dev)
+
+
+STREAM_KV_BASE = 1 << 20  # hash_normal stream ids of the batched-decode caches
+
+
+def fill_stream_cache(cache, n, first_stream=0, seed=0):
+    """Synthetic context for batched decode: rows [0, n) of every stream of every layer of a
+    ``Model.make_stream_cache`` list get hash_normal N(0, 1) K and V rows (one generator stream
+    per (layer, global stream index), so the rows of a stream do not depend on how the streams
+    are split over ranks); a sliding layer's ring gets the last window's rows at position mod
+    window. A decode step over such a cache reads the same bytes as one after a prefill."""
+    s = seed + KV_SEED_OFFSET
+    for i, c in enumerate(cache):
+        B, Hkv, cap, D = c.keys.shape
+        ring = isinstance(c, laguna.RotatingKVCache)
+        for b in range(B):
+            sid = STREAM_KV_BASE + 2 * (i * 4096 + first_stream + b)
+            k = hash_normal((Hkv, n, D), s, sid, 1.0, c.keys.device).to(torch.bfloat16)
+            v = hash_normal((Hkv, n, D), s, sid + 1, 1.0, c.keys.device).to(torch.bfloat16)
+            if ring:
+                p = torch.arange(max(0, n - cap), n, device=c.keys.device)
+                c.keys[b][:, p % cap] = k[:, p]
+                c.values[b][:, p % cap] = v[:, p]
+            else:
+                c.keys[b, :, :n] = k
+                c.values[b, :, :n] = v
+            del k, v
+
+
 def oracle_weights(model):
     """The model's weights as the CPU oracle's dict (oracle/model_ref.py)."""
     cpu = lambda m: tuple(t.cpu() for t in m.mat)

@@ -40,7 +40,8 @@ def test_rmsnorm_with_and_without_residual():
     assert _bf16_close(got, model_ref.rmsnorm(hw, w.float(), 1e-6))
 
 
-@pytest.mark.parametrize("T,K,N", [(1, 2048, 5152), (3, 4096, 2048), (16, 2048, 100), (9, 8192, 2048)])
+@pytest.mark.parametrize("T,K,N", [(1, 2048, 5152), (3, 4096, 2048), (16, 2048, 100), (9, 8192, 2048),
+                                   (17, 2048, 1000), (40, 4096, 2048), (64, 2048, 5152)])
 def test_qlinear_decode_gemv(T, K, N):
     from lagunalab_b200 import ops
     from tests._util import quant_np

@@ -1,12 +1,12 @@
 """Expert parallelism over NVLink peer memory (lagunalab_b200/ep.py PeerExpertParallel,
-csrc/ep.cu) on 2 GPUs, one process per GPU.
+csrc/ep.cu) on 2 and 4 GPUs, one process per GPU.
 
 Each rank routes its own tokens through the seed-0 Zipf-routed config-2 block with its expert
 slice; the output must equal, bit for bit, the one-GPU block (``SparseMoeBlock.__call__``)
 on the same tokens: the exchange moves rows and pick outputs without arithmetic, and the
 combine is the one-GPU combine. Three forwards in a row (the epoch flags and buffer reuse),
-one with fewer tokens than the capacity, and a rank with no tokens. Skipped with fewer than
-two GPUs.
+one with fewer tokens than the capacity, and a rank with no tokens. Skipped when the box has
+fewer GPUs than ranks.
 """
 import datetime
 import os
@@ -61,11 +61,15 @@ def _worker(rank, W, port, cfg, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_expert_parallel_equals_one_gpu_block():
-    W = 2
-    cfg = dict(E=32, H=2048, I=1024, scale=2.5, cap=1024,
-               T=[[1024, 700, 1024], [1024, 0, 333]])
+TOKENS = {2: [[1024, 700, 1024], [1024, 0, 333]],
+          4: [[1024, 700, 1024], [1024, 0, 333], [17, 1024, 0], [512, 1, 1024]]}
+
+
+@pytest.mark.parametrize("W", [2, 4])
+def test_peer_expert_parallel_equals_one_gpu_block(W):
+    if torch.cuda.device_count() < W:
+        pytest.skip(f"needs {W} GPUs")
+    cfg = dict(E=32, H=2048, I=1024, scale=2.5, cap=1024, T=TOKENS[W])
     ctx = mp.get_context("spawn")
     with ctx.Manager() as man:
         results = man.dict()
@@ -80,7 +84,7 @@ def test_peer_expert_parallel_equals_one_gpu_block():
             p.kill()
         assert not alive, "a rank hung"
         res = {r: results[r] for r in results.keys()}
-    assert sorted(res) == [0, 1]
+    assert sorted(res) == list(range(W))
     for r, (status, rep, st) in res.items():
         assert status == "ok", rep
         assert st == 0, f"rank {r}: a bounded wait expired (status {st:#x})"
