@@ -364,11 +364,17 @@ def run_decode_streams(args, ws, rank):
         return cache, ids.to(torch.int32).cuda(), torch.full((n,), ctx, dtype=torch.int32,
                                                               device="cuda")
 
-    def time_graph(g):
+    def time_graph(g, profiled=False):
         for _ in range(Wm):
             g.step()
         torch.cuda.synchronize()
-        return timed_graph(g.graph, K, stream)[0]
+        if profiled:  # an NVTX range a profiler can select (ncu --nvtx-include decode_streams/)
+            torch.cuda.nvtx.range_push("decode_streams")
+        try:
+            return timed_graph(g.graph, K, stream)[0]
+        finally:
+            if profiled:
+                torch.cuda.nvtx.range_pop()
 
     out = dict(streams=B, context=ctx, experts=c["experts"], n_gpus=ws, streams_per_gpu=Br,
                kv="bf16", steps=K,
@@ -398,7 +404,7 @@ def run_decode_streams(args, ws, rank):
     if rank == 0:
         cache, tok, pos = streams(0, B)
         g1 = laguna.StreamDecodeGraph(model, cache, tok, pos)
-        ms1 = time_graph(g1)
+        ms1 = time_graph(g1, profiled=ws == 1)
         out.update(one_gpu_ms=ms1, one_gpu_tokens_per_s=B / (ms1 * 1e-3))
         if ws > 1:
             out.update(speedup=ms1 / out["ms_per_step"],

@@ -1,9 +1,10 @@
 // Router (laguna_mlx/laguna.py:137-145) and routing plan kernels.
 //
 // router logits: logits[T, E] = x[T, H] . W[E, H]^T in fp32 (W fp32, or MLX 8-bit group-64
-//   dequantized, whose bf16 matmul output is rounded to bf16). Three kernels: a warp per expert
-//   for T <= 32 (decode), a tensor-core kernel for fp32 W at larger T (W split into three bf16
-//   parts, so the result keeps fp32 accuracy), and a CUDA-core tiled kernel otherwise.
+//   dequantized, whose bf16 matmul output is rounded to bf16). Three kernels: a warp per
+//   (expert, token) for T <= 256 (decode, batched decode), a tensor-core kernel for fp32 W at
+//   larger T (W split into three bf16 parts, so the result keeps fp32 accuracy), and a
+//   CUDA-core tiled kernel otherwise.
 // router_topk_kernel:   one warp per token: sigmoid (or softmax), + selection bias, top-k by
 //   repeated warp arg-max (larger first, equal keys -> lower index), unbiased weights,
 //   renormalisation, bf16 weights; a per-CTA histogram in shared memory (the warp's winning
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloa
 
 // ---- small-T router logits (decode): one warp per (expert, token) --------------------------
 // Lanes stride over the hidden dimension two elements at a time (coalesced bf16x2 / float2
-// loads) and reduce across the warp; the tokens are spread over blockIdx.y, so the T <= 32
+// loads) and reduce across the warp; the tokens are spread over blockIdx.y, so the T <= 256
 // tokens' dot products run in parallel and each weight row is re-read from L2.
 template <int GBITS>
 __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
@@ -357,8 +358,9 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
   const __nv_bfloat16* gbb = static_cast<const __nv_bfloat16*>(gate_biases);
   const bool xa = aligned(x, 16) && aligned(gate_w, 16);
   prof_begin("router_logits", s);
-  if (T <= 32) {
-    // decode sizes: one warp per (expert, token)
+  if (T <= 256) {
+    // decode sizes and batched decode steps: one warp per (expert, token); the tiled kernels
+    // below run one CTA per 32 tokens x 64 experts, a handful of CTAs at these sizes
     const __nv_bfloat16* nb = nullptr;
     const dim3 grid((E + 7) / 8, T);  // one (8 experts, token) per CTA: the rows come from L2
     if (gate_bits == 0)
