@@ -100,6 +100,9 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
   const int G = a.G;
   const int bh = b * a.Hkv + hk;
   int n = a.n_dev ? a.n_dev[b * a.n_stride] + a.n_add : a.n_host;
+  // the row the previous kernel appends: n - 1, or, in a sliding window's ring buffer that
+  // has wrapped (n > cap), position n - 1 mod cap
+  const int newest = n > a.cap ? (n - 1) % a.cap : n - 1;
   n = min(max(n, 0), a.cap);
   const int tile_lo = split * a.tpc;
   const int tile_hi = min(tile_lo + a.tpc, (n + AB_TK - 1) / AB_TK);
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(AB_THREADS) bf16_decode_kernel(const AbArgs a)
   // it); everything else (q, the newest row, the gate) is read after the wait.
   uint4 kw[2][4], vw[2][4], kn[2][4], vn[2][4];
   int tile = tile_lo + warp;
-  const bool early = tile < tile_hi && tile * AB_TK + AB_TK <= n - 1;
+  const bool early = tile < tile_hi && (newest < tile * AB_TK || newest >= tile * AB_TK + AB_TK);
   if (early) load_tile(tile, kw, vw);
   pdl_wait();
   pdl_trigger();

@@ -163,17 +163,30 @@ def test_model_prefill_logits():
     assert rel_err(got, want) <= REL_TOL and cos(got, want) >= COS_TOL
 
 
+def _teacher_forced(model, cache, prompt, toks, gaps, near_tie=0.02):
+    """Feed the oracle's greedy tokens one at a time and compare the engine's argmax at every
+    step: a step may differ only where the oracle's top-2 logit margin is a near-tie. Returns
+    the number of differing steps."""
+    from lagunalab_b200 import ops
+    logits = model.last_logits(prompt.cuda().to(torch.int32).view(1, -1), cache)
+    flips = 0
+    for i, t in enumerate(toks):
+        got = int(ops.argmax(logits.view(1, -1)))
+        if got != t:
+            assert gaps[i] < near_tie, f"step {i}: {got} != {t} (oracle margin {gaps[i]:.4f})"
+            flips += 1
+        logits = model.last_logits(torch.tensor([[t]], dtype=torch.int32, device="cuda"), cache)
+    return flips
+
+
 def test_model_greedy_decode_matches_oracle():
-    from lagunalab_b200 import laguna
+    """Teacher-forced against the oracle's greedy decode: every one of 16 steps is compared
+    (the engine is fed the oracle's previous token, so a near-tie flip does not end the
+    comparison); at most 2 steps may differ, each on a near-tie."""
     args, model, W, oargs = _tiny(2)
     prompt = torch.randint(0, 512, (9,), generator=torch.Generator().manual_seed(3))
-    steps = 10
-    got = laguna.generate(model, prompt.cuda(), steps)
-    want, gaps = model_ref.greedy(W, oargs, prompt, steps)
-    for i, (a, b) in enumerate(zip(got, want)):
-        if a != b:
-            assert gaps[i] < 0.02, f"step {i}: {a} != {b} (oracle margin {gaps[i]:.4f})"
-            break  # after a near-tie the continuations legitimately diverge
+    toks, gaps = model_ref.greedy(W, oargs, prompt, 16)
+    assert _teacher_forced(model, model.make_cache(), prompt, toks, gaps) <= 2
 
 
 def test_graph_replayed_decode_equals_eager_decode():

@@ -95,13 +95,11 @@ def test_greedy_decode_with_quantized_cache_matches_oracle():
     prompt = torch.randint(0, 512, (11,), generator=torch.Generator().manual_seed(9))
     steps = 10
     c = qcache.make_quantized_cache(model, fused_decode=True, capacity=256)
-    got = laguna.generate(model, prompt.cuda(), steps, c)
-    assert all(x.fused_step for x in c)  # the last step ran the fused q8 kernel
     want, gaps = model_ref.greedy(W, oargs, prompt, steps, kv_bits=8)
-    for i, (a, b) in enumerate(zip(got, want)):
-        if a != b:
-            assert gaps[i] < 0.02, f"step {i}: {a} != {b} (oracle margin {gaps[i]:.4f})"
-            break
+    # teacher-forced: every step compared, a differing step only on an oracle near-tie
+    from tests.test_decoder_gpu import _teacher_forced
+    assert _teacher_forced(model, c, prompt, want, gaps) <= 2
+    assert all(x.fused_step for x in c)  # the last step ran the fused q8 kernel
 
 
 def test_graph_replayed_decode_with_quantized_cache_equals_eager():

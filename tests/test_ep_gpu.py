@@ -3,8 +3,9 @@ csrc/ep.cu) on 2 and 4 GPUs, one process per GPU.
 
 Each rank routes its own tokens through the seed-0 Zipf-routed config-2 block with its expert
 slice; the output must equal, bit for bit, the one-GPU block (``SparseMoeBlock.__call__``)
-on the same tokens: the exchange moves rows and pick outputs without arithmetic, and the
-combine is the one-GPU combine. Three forwards in a row (the epoch flags and buffer reuse),
+on the same tokens whenever both take the tensor-core product path (the exchange moves rows
+and pick outputs without arithmetic, and the combine is the one-GPU combine); a rank with so
+few tokens that the one-GPU block takes the GEMV path is held to the parity bar instead. Three forwards in a row (the epoch flags and buffer reuse),
 one with fewer tokens than the capacity, and a rank with no tokens. Skipped when the box has
 fewer GPUs than ranks.
 """
@@ -47,8 +48,12 @@ def _worker(rank, W, port, cfg, results):
             got = pe(x)
             want = blk(x) if T else got
             torch.cuda.synchronize()
-            rep.append((T, bool(torch.equal(got, want)),
-                        float((got.float() - want.float()).abs().max()) if T else 0.0))
+            # the owners take the tensor-core path (capacity above 512 / (k + 1) tokens); the
+            # one-GPU block takes it for its own T only above that too
+            same_path = T == 0 or T * 9 > 512
+            err = float((got.float() - want.float()).abs().max()) if T else 0.0
+            rel = err / max(float(want.float().abs().max()), 1e-30) if T else 0.0
+            rep.append((T, bool(torch.equal(got, want)), err, same_path, rel))
         results[rank] = ("ok", rep, pe.status())
     except Exception as e:
         results[rank] = ("error", repr(e), None)
@@ -88,5 +93,8 @@ def test_peer_expert_parallel_equals_one_gpu_block(W):
     for r, (status, rep, st) in res.items():
         assert status == "ok", rep
         assert st == 0, f"rank {r}: a bounded wait expired (status {st:#x})"
-        for T, same, err in rep:
-            assert same, f"rank {r}, {T} tokens: differs from the one-GPU block by {err}"
+        for T, same, err, same_path, rel in rep:
+            if same_path:  # the same products in the same order: bit for bit
+                assert same, f"rank {r}, {T} tokens: differs from the one-GPU block by {err}"
+            else:  # GEMV against tensor-core sums: the parity bar
+                assert rel <= 2e-2, f"rank {r}, {T} tokens: max relative error {rel}"

@@ -28,11 +28,11 @@ W = 16
 NEAR_TIE = 0.05  # logit margin below which a routing-flip may change the token
 
 
-def _model(seed=0):
+def _model(seed=0, window=W):
     from lagunalab_b200 import synth
     args = synth.decoder_args(vocab=512, hidden=256, layers=4, heads=4, kv_heads=2,
                               head_dim=128, experts=8, top_k=2, moe_inter=128, shared_inter=128,
-                              dense_inter=256, rope_parameters=ROPE, sliding_window=W,
+                              dense_inter=256, rope_parameters=ROPE, sliding_window=window,
                               layer_types=["full_attention", "sliding_attention",
                                            "sliding_attention", "full_attention"],
                               heads_per_layer=[4, 4, 8, 4])
@@ -109,6 +109,25 @@ def test_graph_replayed_decode_equals_eager_on_sliding_layers():
         toks.append(int(dg.tok))
     assert toks == eager
     assert ops.decode_status() == (0, 0, 0, 0)
+
+
+def test_graph_replayed_decode_with_a_multi_tile_window():
+    """A 48-row window spans three 16-key attention tiles: once the ring has wrapped, the
+    newest row sits in any of them, and the graph-replayed step (programmatic dependent launch:
+    the attention streams tiles before the prologue that appends the newest row finishes) must
+    not read that row early. Tokens equal eager decoding over 70 steps past the window."""
+    from lagunalab_b200 import laguna, ops
+    args, model, _, _ = _model(5, window=48)
+    prompt = _ids(30, 6).cuda()
+    eager = laguna.generate(model, prompt, 72)
+    cache = model.make_cache(capacity=256)
+    tok = ops.argmax(model.last_logits(prompt.to(torch.int32).view(1, -1), cache).view(1, -1))
+    dg = laguna.DecodeGraph(model, cache, tok)
+    toks = [int(tok), int(dg.tok)]
+    for _ in range(70):
+        dg.step()
+        toks.append(int(dg.tok))
+    assert toks == eager
 
 
 def test_quantized_cache_keeps_bf16_windows():
