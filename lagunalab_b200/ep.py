@@ -207,7 +207,22 @@ class PeerExpertParallel:
             raise ValueError(f"{T} tokens exceed the capacity {self.cap}")
         self.epoch += 1
         ep_arg = 0 if self.device_epoch else self.epoch
-        st = torch.cuda.current_stream(self.dev).cuda_stream
+        main = torch.cuda.current_stream(self.dev)
+        st = main.cuda_stream
+        # the product path the one-GPU block takes for these tokens (tensor cores above 512
+        # pick rows), so that the outputs equal it bit for bit
+        big = T * (self.k + 1) > 512
+        sh = self.blk.shared_expert
+        side = None
+        if sh is not None and T:
+            # the shared expert needs only x: it runs on a second stream beside the routing, the
+            # dispatch's peer stores and the owners' wait for the other sources; the combine
+            # waits for it
+            side = self._side_stream()
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                ops.qmlp(x2, sh.mats, path="tensor" if big else "gemv",
+                         out=self.shared_rows[:T])
         if T:
             inds, w = self.blk.route(x2)
             inds, w = ops._c(inds, torch.int32), ops._c(w, torch.bfloat16)
@@ -217,24 +232,25 @@ class PeerExpertParallel:
         arenas = ctypes.addressof(self.ptrs)
         _lib.call("lg_ep_dispatch", x2.data_ptr(), inds.data_ptr(), w.data_ptr(), T, self.cap,
                   H, self.k, self.E, self.W, self.rank, arenas, ep_arg, st)
-        # the product path the one-GPU block takes for these tokens (tensor cores above 512
-        # pick rows), so that the outputs equal it bit for bit
-        big = T * (self.k + 1) > 512
-        sh = self.blk.shared_expert
-        if sh is not None and T:
-            ops.qmlp(x2, sh.mats, path="tensor" if big else "gemv", out=self.shared_rows[:T])
         g, u, d = (ops._qm(m) for m in self.local.mats)
         _lib.call("lg_ep_experts", self.W, self.cap, H, self.I, self.El, self.k,
                   *(t.data_ptr() for t in g), *(t.data_ptr() for t in u),
                   *(t.data_ptr() for t in d), self.rank, arenas, ep_arg, self.timeout,
                   self.expert_path, self.ws.data_ptr(), self.ws_bytes, st)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
+        if side is not None:
+            main.wait_stream(side)
         _lib.call("lg_ep_combine", inds.data_ptr(), T, self.cap, H, self.k, self.E,
                   float(self.blk.routed_scaling_factor), int(sh is not None), self.W, self.rank,
                   arenas, ep_arg, self.timeout, out.data_ptr(), st)
         if self.device_epoch:
             _lib.call("lg_ep_advance", self.arena.data_ptr(), st)
         return out.reshape(*lead, H)
+
+    def _side_stream(self):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.dev)
+        return self._side
 
     def status(self, reset=True):
         """Status word of this rank's arena: 0, or (code | source << 8) of the first wait that
