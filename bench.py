@@ -403,9 +403,33 @@ def run_decode_streams(args, ws, rank):
         torch.cuda.empty_cache()
     if rank == 0:
         cache, tok, pos = streams(0, B)
-        g1 = laguna.StreamDecodeGraph(model, cache, tok, pos)
+        # the library records an event pair around the attention launches while the step is
+        # captured; the pair ends up around the step's last one
+        L = _lib.lib()
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        ev[1].record()
+        L.lg_profile_stage(b"bf16_decode", ev[0].cuda_event, ev[1].cuda_event)
+        try:
+            g1 = laguna.StreamDecodeGraph(model, cache, tok, pos)
+        finally:
+            L.lg_profile_stage(None, None, None)
         ms1 = time_graph(g1, profiled=ws == 1)
-        out.update(one_gpu_ms=ms1, one_gpu_tokens_per_s=B / (ms1 * 1e-3))
+        at = []
+        for _ in range(3):
+            g1.step()
+            torch.cuda.synchronize()
+            at.append(_lib.event_elapsed_ms(ev[0], ev[1]))
+        at_ms = statistics.median(at)
+        nbytes = B * model.args.num_key_value_heads * (ctx + K + Wm + 4) * 512
+        pk, pk_kind = peaks()
+        out.update(one_gpu_ms=ms1, one_gpu_tokens_per_s=B / (ms1 * 1e-3),
+                   attention={"kernel": "bf16_decode_kernel", "us": at_ms * 1e3,
+                              "achieved_gbs": nbytes / (at_ms * 1e-3) / 1e9,
+                              "frac": nbytes / (at_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                              "peak_source": pk_kind,
+                              "algorithmic": "streams x kv heads x keys x 512 B (bf16 K and V "
+                                             "rows), at the timed steps' context"})
         if ws > 1:
             out.update(speedup=ms1 / out["ms_per_step"],
                        efficiency=ms1 / (out["ms_per_step"] * ws))

@@ -23,6 +23,7 @@ struct MoeWs {
   __nv_bfloat16* h;
   __nv_bfloat16* yrows;  // [P + T, H] per-pick down outputs (combine mode)
   void* tc;
+  int32_t* plan;         // segmented-plan scratch (many picks)
 };
 
 static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh, MoeWs* w,
@@ -38,6 +39,7 @@ static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh,
   t.h = c.take<__nv_bfloat16>(((size_t)P + T) * Imax);
   t.yrows = c.take<__nv_bfloat16>(with_yrows ? ((size_t)P + T) * H : 0);
   t.tc = c.take<char>(tc_workspace_bytes(T, H, I, I_sh, E, k));
+  t.plan = c.take<int32_t>(plan_scratch_bytes(T, k, E) / sizeof(int32_t));
   if (w) *w = t;
   return align_up(c.used, 256);
 }
@@ -168,7 +170,7 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   const bool with_sh = I_sh > 0;
   if (mode == 1) LG_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(uint16_t) * (size_t)P * H, st));
   int rc = launch_plan(inds, T, E > 0 ? k : 0, E, with_sh ? 1 : 0, w.counts, w.offsets, w.perm,
-                       w.active, st);
+                       w.active, st, w.plan);
   if (rc) return rc;
   GemvArgs a;
   a.x = static_cast<const __nv_bfloat16*>(x);

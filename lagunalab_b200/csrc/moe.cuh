@@ -47,8 +47,11 @@ struct GemvArgs {
 // record their expired waits there too.
 int* tc_err_word(void* tc_ws, int T, int H, int I, int I_sh, int E, int k);
 
+// scratch: plan_scratch_bytes(T, k, E) bytes (null: the one-CTA-per-group kernel at any size)
 int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32_t* counts,
-                int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s);
+                int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s,
+                int32_t* scratch);
+size_t plan_scratch_bytes(int T, int k, int E);
 int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s);
 // out[t] = bf16(bf16(bf16(sum_j bf16(y[t*k+j] * w[t*k+j])) * scale) + y[P + t]) per token, the
 // picks summed in order j = 0..k-1 (picks whose expert id is outside [0, E) skipped), the shared

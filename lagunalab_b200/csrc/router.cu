@@ -330,6 +330,127 @@ __global__ void __launch_bounds__(512) moe_plan_kernel(const int32_t* __restrict
   }
 }
 
+// ---- segmented plan for many picks (P >= PL_MIN_PICKS) ---------------------------------------
+// The kernel above gives every group one CTA that scans all P picks, so its time does not
+// fall with the group count (an expert-parallel owner with 16 local experts scans as many picks
+// as the one-GPU block). The segmented form gives the same outputs with the scan split over
+// warps: (1) every warp histograms its PL_SEG consecutive picks; (2) one CTA scans the
+// (group, segment) counts in group-major order into each segment's first row per group, and
+// writes counts, offsets and the active list; (3) every warp walks its segment in order and
+// places each pick at its segment's running row for its group (lanes with the same group ranked
+// by __match_any_sync), so perm is ordered by group, then pick id, as before.
+constexpr int PL_SEG = 1024;         // picks per warp segment
+constexpr int PL_WARPS = 8;          // warps per CTA in the histogram and placement kernels
+constexpr int PL_MIN_PICKS = 65536;  // below this the one-CTA-per-group kernel is as fast
+
+__host__ __device__ constexpr int pl_nseg(int P) { return (P + PL_SEG - 1) / PL_SEG; }
+
+// cnt [nseg][E]: picks of group e in segment seg (valid routed picks only)
+__global__ void __launch_bounds__(PL_WARPS * 32) plan_count_kernel(const int32_t* __restrict__ inds,
+                                                                   int P, int E,
+                                                                   int32_t* __restrict__ cnt) {
+  pdl_wait();  // inds come from the previous kernel
+  pdl_trigger();
+  __shared__ int hist[PL_WARPS][256];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int seg = blockIdx.x * PL_WARPS + warp;
+  for (int e = lane; e < E; e += 32) hist[warp][e] = 0;
+  __syncwarp();
+  const int p0 = seg * PL_SEG, p1 = min(P, p0 + PL_SEG);
+  for (int p = p0 + lane; p < p1; p += 32) {
+    const int e = inds[p];
+    if (e >= 0 && e < E) atomicAdd(&hist[warp][e], 1);
+  }
+  __syncwarp();
+  if (p0 < P)
+    for (int e = lane; e < E; e += 32) cnt[(size_t)seg * E + e] = hist[warp][e];
+}
+
+// One CTA: base[seg][e] = rows of groups < e (all segments) + rows of group e in segments
+// < seg; counts, offsets (the shared group after every valid routed pick) and the active list.
+__global__ void __launch_bounds__(1024) plan_scan_kernel(const int32_t* __restrict__ cnt, int nseg,
+                                                         int E, int T, int with_shared,
+                                                         int32_t* __restrict__ base,
+                                                         int32_t* __restrict__ counts,
+                                                         int32_t* __restrict__ offsets,
+                                                         int32_t* __restrict__ active) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int warp_tot[32];
+  __shared__ int s_total;
+  const int N = nseg * E;  // entries in group-major order: i = e * nseg + seg
+  const int per = (N + blockDim.x - 1) / blockDim.x;
+  const int i0 = min(N, (int)threadIdx.x * per), i1 = min(N, i0 + per);
+  int sum = 0;
+  for (int i = i0; i < i1; ++i) sum += cnt[(size_t)(i % nseg) * E + i / nseg];
+  int run = block_excl_scan(sum, warp_tot, &s_total);
+  for (int i = i0; i < i1; ++i) {
+    const int seg = i % nseg, e = i / nseg;
+    base[(size_t)seg * E + e] = run;
+    if (seg == 0) offsets[e] = run;
+    run += cnt[(size_t)seg * E + e];
+  }
+  __syncthreads();  // every group's offset is written
+  const int total = s_total;
+  if (threadIdx.x == 0) {
+    int na = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = (e + 1 < E ? offsets[e + 1] : total) - offsets[e];
+      counts[e] = c;
+      if (active && c > 0) active[1 + na++] = e;
+    }
+    if (with_shared) {
+      counts[E] = T;
+      offsets[E] = total;
+      offsets[E + 1] = total + T;
+      if (active && T > 0) active[1 + na++] = E;
+    } else {
+      offsets[E] = offsets[E + 1] = total;
+    }
+    if (active) active[0] = na;
+  }
+}
+
+// Every warp places its segment's picks in order; the shared group's identity rows follow the
+// routed picks (rows offsets[E] + t = pick P + t).
+__global__ void __launch_bounds__(PL_WARPS * 32) plan_place_kernel(const int32_t* __restrict__ inds,
+                                                                   int P, int E, int T,
+                                                                   int with_shared,
+                                                                   const int32_t* __restrict__ base,
+                                                                   const int32_t* __restrict__ offsets,
+                                                                   int32_t* __restrict__ perm) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int next[PL_WARPS][256];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int seg = blockIdx.x * PL_WARPS + warp;
+  const int p0 = seg * PL_SEG, p1 = min(P, p0 + PL_SEG);
+  if (p0 < P) {
+    for (int e = lane; e < E; e += 32) next[warp][e] = base[(size_t)seg * E + e];
+    __syncwarp();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int q = p0; q < p1; q += 32) {  // warp-uniform trip count
+      const int p = q + lane;
+      const int e = p < p1 ? inds[p] : -1;
+      const bool valid = e >= 0 && e < E;
+      const unsigned same = __match_any_sync(0xffffffffu, valid ? e : E + lane);
+      if (valid) perm[next[warp][e] + __popc(same & lt)] = p;
+      __syncwarp();  // every lane has read its group's row before the leader moves it on
+      if (valid && (same & lt) == 0) next[warp][e] += __popc(same);
+      __syncwarp();
+    }
+  }
+  if (with_shared && blockIdx.x == 0) {
+    const int sb = offsets[E];
+    for (int t = threadIdx.x; t < T; t += blockDim.x) perm[sb + t] = P + t;
+  }
+}
+
+size_t plan_scratch_bytes(int T, int k, int E) {
+  const int P = T * k;
+  return P >= PL_MIN_PICKS ? 2 * sizeof(int32_t) * (size_t)pl_nseg(P) * E : 0;
+}
+
 }  // namespace lg
 
 using namespace lg;
@@ -399,9 +520,29 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
 namespace lg {
 // Host-side plan launch shared with the MoE orchestration. active: int32 [1 + E + 1].
 int launch_plan(const int32_t* inds, int T, int k, int E, int with_shared, int32_t* counts,
-                int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s) {
+                int32_t* offsets, int32_t* perm, int32_t* active, cudaStream_t s,
+                int32_t* scratch) {
   int G = E + (with_shared ? 1 : 0);
   if (G == 0) return LG_OK;
+  const int P = T * k;
+  if (scratch && P >= PL_MIN_PICKS && E > 0 && E <= 256) {  // segmented form
+    const int nseg = pl_nseg(P);
+    int32_t* cnt = scratch;
+    int32_t* base = scratch + (size_t)nseg * E;
+    const int blocks = (nseg + PL_WARPS - 1) / PL_WARPS;
+    prof_begin("plan", s);
+    LG_CUDA_TRY(launch_k(plan_count_kernel, dim3(blocks), dim3(PL_WARPS * 32), 0, s, inds, P, E,
+                         cnt));
+    LG_CUDA_TRY(launch_k(plan_scan_kernel, dim3(1), dim3(1024), 0, s,
+                         static_cast<const int32_t*>(cnt), nseg, E, T, with_shared, base, counts,
+                         offsets, active));
+    LG_CUDA_TRY(launch_k(plan_place_kernel, dim3(blocks), dim3(PL_WARPS * 32), 0, s, inds, P, E,
+                         T, with_shared, static_cast<const int32_t*>(base),
+                         static_cast<const int32_t*>(offsets), perm));
+    prof_end("plan", s);
+    LG_LAUNCH_CHECK("moe_plan_segmented");
+    return LG_OK;
+  }
   if (active) LG_CUDA_TRY(cudaMemsetAsync(active, 0, sizeof(int32_t), s));
   prof_begin("plan", s);
   LG_CUDA_TRY(launch_k(moe_plan_kernel, dim3(G), dim3(512), 0, s, inds, T, k, E, with_shared,
@@ -418,5 +559,5 @@ extern "C" int lg_moe_plan(const int32_t* inds, int T, int k, int E, int with_sh
   LG_CHECK_ARG(counts && offsets && perm, "plan: NULL pointer");
   LG_CHECK_ARG(T * k == 0 || inds, "plan: NULL inds");
   return launch_plan(inds, T, k, E, with_shared, counts, offsets, perm, nullptr,
-                     static_cast<cudaStream_t>(stream));
+                     static_cast<cudaStream_t>(stream), nullptr);
 }

@@ -162,3 +162,22 @@ def test_prefill_combine_is_deterministic(path):
     outs = [ops.moe_experts(x, inds, w, 1.0, blk.switch_mlp.mats, sh, path=path)
             for _ in range(3)]
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+@pytest.mark.parametrize("path", ["tensor", "gemv"])
+def test_segmented_plan_block_equals_the_block_on_halves(path):
+    """At 65,536 picks and above the routing plan is built by the segmented kernels (per-warp
+    histograms, one scan, in-order placement); below, by one CTA per expert. A token's output
+    does not depend on the other tokens of the batch (each row's products and combine are its
+    own), so the block on 12,288 Zipf-routed tokens (98,304 picks) must equal, bit for bit, the
+    block on its two halves (49,152 picks each, the other plan kernel)."""
+    from lagunalab_b200 import ops, synth
+    blk, x = synth.moe_block(12288, 128, 8, 2048, 1024, 1024, seed=3, zipf=True)
+    inds, w = blk.route(x)
+    run = lambda xs, i, ww: ops.moe_experts(xs, i, ww, 1.0, blk.switch_mlp.mats,
+                                            blk.shared_expert.mats, path=path)
+    whole = run(x, inds, w)
+    h = 6144
+    halves = torch.cat([run(x[:h], inds[:h], w[:h]), run(x[h:], inds[h:], w[h:])])
+    assert ops.moe_status(x.device, 12288, 2048, 1024, 128, 8, 1024) == 0
+    assert torch.equal(whole, halves)
