@@ -156,16 +156,20 @@ class Engine:
         return self.make_cache(), 0
 
     def generate(self, ids, max_tokens, temperature=0.0):
-        """Yields generated ids; a stop id ends the generation without being yielded. Returns
-        (through StopIteration) the finish reason, "stop" or "length"."""
-        import torch
-
-        from . import laguna, ops
+        """A generator of the generated ids; a stop id ends the generation without being
+        yielded, and the generator returns (through StopIteration) the finish reason, "stop" or
+        "length". The prompt is checked here, before the generator runs (ValueError)."""
         if not ids:
             raise ValueError("empty prompt")
         if len(ids) >= self.max_context:
             raise ValueError(f"prompt of {len(ids)} tokens exceeds the context {self.max_context}")
-        max_tokens = max(0, min(int(max_tokens), self.max_context - len(ids) - 1))
+        return self._generate(list(ids), int(max_tokens), float(temperature or 0.0))
+
+    def _generate(self, ids, max_tokens, temperature):
+        import torch
+
+        from . import laguna, ops
+        max_tokens = max(0, min(max_tokens, self.max_context - len(ids) - 1))
         cache, n = self._cache_for(ids)
         dev = self.model.lm_head.weight.device
         held = list(ids)
@@ -298,12 +302,19 @@ def make_handler(engine, model_name, default_max_tokens=512):
             with engine.lock:
                 try:
                     gen = engine.generate(ids, max_tokens, temperature)
+                except ValueError as e:
+                    self._send_json(400, {"error": {"message": str(e)}})
+                    return
+                try:
                     if req.get("stream"):
                         self._stream(rid, chat, gen, stop)
                     else:
                         self._complete(rid, chat, gen, stop, len(ids))
-                except ValueError as e:
-                    self._send_json(400, {"error": {"message": str(e)}})
+                finally:
+                    # a client that went away mid-stream leaves the generator suspended: close it
+                    # here, under the lock, so its caches are synchronised and returned to the
+                    # prompt cache before the next request
+                    gen.close()
 
         def _pieces(self, gen, stop):
             """(piece, tokens so far) with the stop strings applied: text that could still be

@@ -81,6 +81,9 @@ class _FakeEngine:
         self.calls.append((list(ids), max_tokens, temperature))
         if not ids:
             raise ValueError("empty prompt")
+        return self._gen(ids, max_tokens)
+
+    def _gen(self, ids, max_tokens):
         t = ids[-1]
         for _ in range(max_tokens):
             t += 1
@@ -155,3 +158,7 @@ def test_errors(server):
     with pytest.raises(urllib.error.HTTPError) as e:
         _post(base + "/v1/completions", {"max_tokens": 3})  # no prompt
     assert e.value.code == 400
+    for stream in (False, True):  # an empty prompt is refused before any response starts
+        with pytest.raises(urllib.error.HTTPError) as e:
+            _post(base + "/v1/completions", {"prompt": "", "stream": stream})
+        assert e.value.code == 400
