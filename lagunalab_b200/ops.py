@@ -171,9 +171,11 @@ def switch_glu(x, inds, experts, path="auto", group_size=64, bits=4):
     return y
 
 
-def qmlp(x, mats, path="auto", group_size=64, bits=4, out=None):
+def qmlp(x, mats, path="auto", group_size=64, bits=4, out=None, ws=None):
     """Dense quantized SwiGLU MLP: down(silu(gate x) * up x) -> bf16 [T, H] (into ``out``, a
-    contiguous [T, H] bf16 tensor, when given)."""
+    contiguous [T, H] bf16 tensor, when given). ``ws``: the caller's own workspace (a uint8
+    CUDA tensor of at least ``lg_moe_workspace_bytes(T, H, 0, 0, 0, I)`` bytes) instead of the
+    shared one, for calls that overlap other MoE calls on another stream."""
     x = _c(x, torch.bfloat16)
     dev = x.device
     T, H = x.shape
@@ -184,7 +186,10 @@ def qmlp(x, mats, path="auto", group_size=64, bits=4, out=None):
     elif not (out.is_contiguous() and out.dtype == torch.bfloat16 and tuple(out.shape) == (T, H)):
         raise ValueError("qmlp: out must be a contiguous bf16 [T, H] tensor")
     nb = _lib.lib().lg_moe_workspace_bytes(T, H, 0, 0, 0, I)
-    ws = workspace(dev, "moe", nb)
+    if ws is None:
+        ws = workspace(dev, "moe", nb)
+    elif ws.numel() < nb:
+        raise ValueError(f"qmlp: workspace of {ws.numel()} bytes, need {nb}")
     _lib.call("lg_qmlp", _p(x), T, H, I, *map(_p, g), *map(_p, u), *map(_p, d),
               group_size, bits, _PATHS[path], _p(out), _p(ws), ws.numel(), _stream(dev))
     return out
