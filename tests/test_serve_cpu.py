@@ -162,3 +162,31 @@ def test_errors(server):
         with pytest.raises(urllib.error.HTTPError) as e:
             _post(base + "/v1/completions", {"prompt": "", "stream": stream})
         assert e.value.code == 400
+
+
+class _FakeKV:
+    def __init__(self, n, trimmable=True):
+        self.offset, self.trimmable = n, trimmable
+
+    def is_trimmable(self):
+        return self.trimmable
+
+    def trim(self, n):
+        self.offset -= n
+        return n
+
+
+def test_engine_reuses_the_longest_cached_prefix():
+    eng = serve.Engine(model=None, tokenizer=_Tok(), make_cache=lambda: "fresh",
+                       max_context=64, prompt_cache=serve.PromptCache(2))
+    held = [_FakeKV(10), _FakeKV(10)]
+    eng.prompt_cache.put(list(range(10)), held)
+    cache, n = eng._cache_for(list(range(7)) + [30, 31])  # shares 7 tokens
+    assert cache is held and n == 7 and all(c.offset == 7 for c in held)
+    assert eng.prompt_cache.entries == []  # taken out while the request runs
+    eng.prompt_cache.put(list(range(7)), held)
+    cache, n = eng._cache_for(list(range(7)))  # the whole prompt cached: one token is re-fed
+    assert cache is held and n == 6 and all(c.offset == 6 for c in held)
+    ring = [_FakeKV(9, trimmable=False)]  # a wrapped sliding window cannot be cut back
+    eng.prompt_cache.put(list(range(9)), ring)
+    assert eng._cache_for(list(range(5)) + [40]) == ("fresh", 0)
