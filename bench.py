@@ -286,7 +286,22 @@ def run_ep_prefill(args, ws, rank):
     outs = None
     if ws > 1:
         x = tokens(rank)
-        pe = ep.PeerExpertParallel(blk, capacity=Tr)
+        # expert placement balanced on the routing of a separate calibration batch (the same
+        # router and Zipf bias, other tokens): greedy, E/N experts per rank
+        g = torch.Generator(device="cuda")
+        g.manual_seed(3000 + rank)
+        xc = torch.randn(Tr, c["H"], generator=g, device="cuda").to(torch.bfloat16)
+        cnt = torch.bincount(blk.route(xc)[0].reshape(-1).long(), minlength=c["E"])
+        dist.all_reduce(cnt)
+        placement = ep.balanced_placement(cnt.tolist(), ws)
+        pe = ep.PeerExpertParallel(blk, capacity=Tr, placement=placement)
+        # picks per owner on the measured batch under that placement
+        own = torch.empty(c["E"], dtype=torch.long, device="cuda")
+        for d, p in enumerate(placement):
+            own[torch.tensor(p, device="cuda")] = d
+        mine = torch.bincount(own[blk.route(x)[0].reshape(-1).long()], minlength=ws)
+        dist.all_reduce(mine)
+        loads = mine.tolist()
         for _ in range(args.warmup):
             pe(x)
         torch.cuda.synchronize()
@@ -302,7 +317,11 @@ def run_ep_prefill(args, ws, rank):
         out.update(ms_per_step=ms, tokens_per_s=c["T"] / (ms * 1e-3), status=status,
                    gpu_launches_per_step=launches // max(1, args.steps),
                    exchange="NVLink peer stores issued by the dispatch kernel and the expert "
-                            "down-product epilogue; epoch flags with bounded waits; no collective")
+                            "down-product epilogue; epoch flags with bounded waits; no collective",
+                   placement="balanced (greedy, E/N experts per rank) on the picks of a separate "
+                             "calibration batch",
+                   picks_per_owner=loads,
+                   owner_max_over_mean=max(loads) * len(loads) / max(1, sum(loads)))
     if rank == 0:
         xa = torch.cat([tokens(r) for r in range(ws)])
         for _ in range(args.warmup):

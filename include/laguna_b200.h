@@ -507,6 +507,13 @@ int lg_ep_ipc_close(void* base);
 int lg_ep_dispatch(const void* x, const int32_t* inds, const void* weights, int T, int Tr,
                    int H, int k, int E, int W, int rank, void* const* arenas, unsigned epoch,
                    void* stream);
+/* lg_ep_dispatch with a placement of the experts over the ranks: rank owner_of[e] holds
+ * expert e as its local expert local_of[e] (int32 [E] device tables, each rank holding E/W
+ * experts; both NULL: the contiguous ranges). Lets a caller balance the experts' load. */
+int lg_ep_dispatch_mapped(const void* x, const int32_t* inds, const void* weights, int T, int Tr,
+                          int H, int k, int E, int W, int rank, void* const* arenas,
+                          unsigned epoch, const int32_t* owner_of, const int32_t* local_of,
+                          void* stream);
 size_t lg_ep_experts_workspace_bytes(int W, int Tr, int H, int I, int El, int k);
 /* Waits for every source's dispatch, runs this rank's El experts (MLX 4-bit g64 weights
  * [El, I, H/8] / [El, H, I/8] with bf16 scales and biases) over the received rows and stores

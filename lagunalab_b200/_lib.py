@@ -86,6 +86,7 @@ SIGNATURES = {
     "lg_ep_combine": (c_int, [P, I, I, I, I, I, c_float, I, I, I, P, ctypes.c_uint,
                               ctypes.c_double, P, P]),
     "lg_ep_status": (c_int, [P, I, P]),
+    "lg_ep_dispatch_mapped": (c_int, [P, P, P, I, I, I, I, I, I, I, P, ctypes.c_uint, P, P, P]),
     "lg_ep_advance": (c_int, [P, P]),
     "lg_moe_decode": (c_int, [P, P, P, I, I, I, I, c_float, P, P, P, P, P, P, P, P, P, I,
                               P, P, P, P, P, P, P, P, P, P, P, P, c_size_t, P]),

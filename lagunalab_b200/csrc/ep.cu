@@ -124,11 +124,27 @@ __device__ __forceinline__ bool ep_owns(int e, int El, int W, int d) {
   return e >= 0 && e < El * W && e / El == d;
 }
 
+// Expert placement: owner[e] (the rank holding expert e) and local[e] (its index among that
+// rank's El experts), or null for the contiguous ranges (owner e / El, local e % El).
+struct EpMap {
+  const int32_t* owner;
+  const int32_t* local;
+};
+
+__device__ __forceinline__ bool ep_owns_m(const EpMap& m, int e, int El, int W, int d) {
+  if (!m.owner) return ep_owns(e, El, W, d);
+  return e >= 0 && e < El * W && __ldg(m.owner + e) == d;
+}
+
+__device__ __forceinline__ int ep_local_m(const EpMap& m, int e, int El, int d) {
+  return m.owner ? __ldg(m.local + e) : e - d * El;
+}
+
 // One CTA per destination rank d: tokens with at least one pick on d take consecutive slots
 // (token order); slot[t * W + d] = -1 for the others; the total goes to the send count.
 __global__ void __launch_bounds__(512) ep_plan_kernel(const int32_t* __restrict__ inds, int T,
                                                       int k, int El, int W, char* self,
-                                                      EpLayout L) {
+                                                      EpLayout L, EpMap map) {
   pdl_wait();
   pdl_trigger();
   __shared__ int warp_tot[32];
@@ -140,7 +156,7 @@ __global__ void __launch_bounds__(512) ep_plan_kernel(const int32_t* __restrict_
     const int t = t0 + threadIdx.x;
     int has = 0;
     if (t < T)
-      for (int j = 0; j < k; ++j) has |= ep_owns(inds[(size_t)t * k + j], El, W, d);
+      for (int j = 0; j < k; ++j) has |= ep_owns_m(map, inds[(size_t)t * k + j], El, W, d);
     const int off = block_excl_scan(has, warp_tot, &s_total);
     if (t < T) slot[(size_t)t * W + d] = has ? base + off : -1;
     base += s_total;
@@ -155,7 +171,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* __restrict__ w,
                                                           int T, int Tr, int H, int k, int El,
                                                           int W, int rank, EpPeers peers,
-                                                          EpLayout L, unsigned epoch) {
+                                                          EpLayout L, unsigned epoch, EpMap map) {
   pdl_wait();
   pdl_trigger();
   char* self = peers.arena[rank];
@@ -177,7 +193,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
     if (lane < k) {
       const int e = inds[(size_t)t * k + lane];
       reinterpret_cast<int32_t*>(dst + L.recv_lid)[row * k + lane] =
-          ep_owns(e, El, W, d) ? e - d * El : -1;
+          ep_owns_m(map, e, El, W, d) ? ep_local_m(map, e, El, d) : -1;
       reinterpret_cast<__nv_bfloat16*>(dst + L.recv_w)[row * k + lane] = w[(size_t)t * k + lane];
     }
     if (lane == 0) reinterpret_cast<int32_t*>(dst + L.recv_tok)[row] = t;
@@ -385,20 +401,24 @@ extern "C" int lg_ep_ipc_close(void* base) {
   return LG_OK;
 }
 
-extern "C" int lg_ep_dispatch(const void* x, const int32_t* inds, const void* weights, int T,
-                              int Tr, int H, int k, int E, int W, int rank,
-                              void* const* arenas, unsigned epoch, void* stream) {
+extern "C" int lg_ep_dispatch_mapped(const void* x, const int32_t* inds, const void* weights,
+                                     int T, int Tr, int H, int k, int E, int W, int rank,
+                                     void* const* arenas, unsigned epoch,
+                                     const int32_t* owner_of, const int32_t* local_of,
+                                     void* stream) {
   if (int rc = ep_check(W, rank, Tr, k, H)) return rc;
   LG_CHECK_ARG(T >= 0 && T <= Tr, "ep_dispatch: %d tokens exceed the capacity %d", T, Tr);
   LG_CHECK_ARG(E >= W && E % W == 0, "ep_dispatch: %d experts do not split over %d ranks", E, W);
   LG_CHECK_ARG(T == 0 || (x && inds && weights && aligned(x, 16)),
                "ep_dispatch: NULL or misaligned x/inds/weights");
+  LG_CHECK_ARG(!owner_of == !local_of, "ep_dispatch: owner and local maps go together");
   EpPeers peers;
   if (int rc = ep_peers(arenas, W, &peers)) return rc;
   const EpLayout L = ep_layout(W, Tr, k, H);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const EpMap map = {owner_of, local_of};
   LG_CUDA_TRY(launch_k(ep_plan_kernel, dim3(W), dim3(512), 0, st, inds, T, k, E / W, W,
-                       peers.arena[rank], L));
+                       peers.arena[rank], L, map));
   LG_LAUNCH_CHECK("ep_plan");
   int grid = (T * W + 7) / 8;  // 8 warps per CTA
   if (grid > 148 * 8) grid = 148 * 8;
@@ -406,9 +426,16 @@ extern "C" int lg_ep_dispatch(const void* x, const int32_t* inds, const void* we
   LG_CUDA_TRY(launch_k(ep_dispatch_kernel, dim3(grid), dim3(256), 0, st,
                        static_cast<const __nv_bfloat16*>(x), inds,
                        static_cast<const __nv_bfloat16*>(weights), T, Tr, H, k, E / W, W, rank,
-                       peers, L, epoch));
+                       peers, L, epoch, map));
   LG_LAUNCH_CHECK("ep_dispatch");
   return LG_OK;
+}
+
+extern "C" int lg_ep_dispatch(const void* x, const int32_t* inds, const void* weights, int T,
+                              int Tr, int H, int k, int E, int W, int rank,
+                              void* const* arenas, unsigned epoch, void* stream) {
+  return lg_ep_dispatch_mapped(x, inds, weights, T, Tr, H, k, E, W, rank, arenas, epoch, nullptr,
+                               nullptr, stream);
 }
 
 extern "C" size_t lg_ep_experts_workspace_bytes(int W, int Tr, int H, int I, int El, int k) {

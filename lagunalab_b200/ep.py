@@ -110,16 +110,41 @@ class CollectiveExpertParallel:
         return out.to(x.dtype).reshape(*lead, H)
 
 
-def local_switch_glu(sw, lo, hi):
-    """A SwitchGLU holding experts [lo, hi) of ``sw`` (copied contiguous)."""
+def local_switch_glu(sw, lo, hi=None):
+    """A SwitchGLU holding experts [lo, hi) of ``sw`` (copied contiguous), or, with ``lo`` a list
+    of expert ids, those experts in that order."""
     from .laguna import SwitchGLU, SwitchLinear
+    if hi is None:
+        idx = torch.tensor(list(lo), dtype=torch.long, device=sw.gate_proj.weight.device)
+        take = lambda t: t.index_select(0, idx).contiguous()  # noqa: E731
+        n = idx.numel()
+    else:
+        take = lambda t: t[lo:hi].contiguous()  # noqa: E731
+        n = hi - lo
 
     def cut(p):
-        return SwitchLinear(p.weight[lo:hi].contiguous(), p.scales[lo:hi].contiguous(),
-                            p.biases[lo:hi].contiguous(), p.group_size, p.bits)
+        return SwitchLinear(take(p.weight), take(p.scales), take(p.biases), p.group_size, p.bits)
 
-    return SwitchGLU(sw.input_dims, sw.hidden_dims, hi - lo, cut(sw.gate_proj),
-                     cut(sw.up_proj), cut(sw.down_proj))
+    return SwitchGLU(sw.input_dims, sw.hidden_dims, n, cut(sw.gate_proj), cut(sw.up_proj),
+                     cut(sw.down_proj))
+
+
+def balanced_placement(counts, W):
+    """Experts over W ranks, E/W each, balancing the picks: ``counts`` [E] (picks per expert
+    on representative traffic, e.g. summed over the ranks of a calibration batch); experts are
+    taken busiest first and each goes to the least-loaded rank that still has room (greedy
+    longest-processing-time). Returns W lists of expert ids (ascending)."""
+    counts = [int(c) for c in counts]
+    E = len(counts)
+    if E % W:
+        raise ValueError(f"{E} experts do not split evenly over {W} ranks")
+    El = E // W
+    load, held = [0] * W, [[] for _ in range(W)]
+    for e in sorted(range(E), key=lambda e: (-counts[e], e)):
+        d = min((r for r in range(W) if len(held[r]) < El), key=lambda r: (load[r], r))
+        held[d].append(e)
+        load[d] += counts[e]
+    return [sorted(h) for h in held]
 
 
 class PeerExpertParallel:
@@ -140,7 +165,7 @@ class PeerExpertParallel:
     """
 
     def __init__(self, blk, capacity, group=None, timeout_s=5.0, device_epoch=False,
-                 expert_path=None):
+                 expert_path=None, placement=None):
         from . import _lib, ops
         self.lib = _lib.lib()
         self.blk = blk
@@ -154,8 +179,27 @@ class PeerExpertParallel:
         self.E, self.El, self.k = E, E // W, blk.top_k
         self.H, self.I = sw.input_dims, sw.hidden_dims
         self.cap, self.timeout = int(capacity), float(timeout_s)
-        self.local = local_switch_glu(sw, r * self.El, (r + 1) * self.El)
         self.dev = sw.gate_proj.weight.device
+        # ``placement``: W lists of expert ids (E/W each, together every expert once; the same
+        # on every rank), e.g. ``balanced_placement``; None: rank r holds [r*E/W, (r+1)*E/W)
+        self.owner_of = self.local_of = None
+        if placement is None:
+            self.local = local_switch_glu(sw, r * self.El, (r + 1) * self.El)
+        else:
+            placement = [list(map(int, p)) for p in placement]
+            flat = sorted(e for p in placement for e in p)
+            if len(placement) != W or flat != list(range(E)) or \
+                    any(len(p) != self.El for p in placement):
+                raise ValueError(f"placement must split the {E} experts into {W} lists of "
+                                 f"{self.El}")
+            owner, local = [0] * E, [0] * E
+            for d, p in enumerate(placement):
+                for j, e in enumerate(p):
+                    owner[e], local[e] = d, j
+            self.owner_of = torch.tensor(owner, dtype=torch.int32, device=self.dev)
+            self.local_of = torch.tensor(local, dtype=torch.int32, device=self.dev)
+            self.local = local_switch_glu(sw, placement[r])
+        self.placement = placement
         nb = self.lib.lg_ep_arena_bytes(W, self.cap, self.k, self.H)
         self.arena = torch.zeros(nb, dtype=torch.uint8, device=self.dev)  # flags start at 0
         hb = self.lib.lg_ep_ipc_handle_bytes()
@@ -230,8 +274,10 @@ class PeerExpertParallel:
             inds = torch.empty(0, self.k, dtype=torch.int32, device=self.dev)
             w = torch.empty(0, self.k, dtype=torch.bfloat16, device=self.dev)
         arenas = ctypes.addressof(self.ptrs)
-        _lib.call("lg_ep_dispatch", x2.data_ptr(), inds.data_ptr(), w.data_ptr(), T, self.cap,
-                  H, self.k, self.E, self.W, self.rank, arenas, ep_arg, st)
+        _lib.call("lg_ep_dispatch_mapped", x2.data_ptr(), inds.data_ptr(), w.data_ptr(), T,
+                  self.cap, H, self.k, self.E, self.W, self.rank, arenas, ep_arg,
+                  None if self.owner_of is None else self.owner_of.data_ptr(),
+                  None if self.local_of is None else self.local_of.data_ptr(), st)
         g, u, d = (ops._qm(m) for m in self.local.mats)
         _lib.call("lg_ep_experts", self.W, self.cap, H, self.I, self.El, self.k,
                   *(t.data_ptr() for t in g), *(t.data_ptr() for t in u),

@@ -134,3 +134,14 @@ def test_ep_failed_rank_ends_the_others_with_an_error():
                timeout=120)
     assert res[1][0] == "error" and "planted failure" in res[1][1]
     assert res[0][0] == "error"  # its exchange ended with an error instead of waiting forever
+
+
+def test_balanced_placement_splits_evenly_and_balances():
+    from lagunalab_b200 import ep
+    counts = [1000, 900, 10, 10, 500, 400, 5, 5]
+    pl = ep.balanced_placement(counts, 2)
+    assert sorted(e for p in pl for e in p) == list(range(8)) and all(len(p) == 4 for p in pl)
+    loads = [sum(counts[e] for e in p) for p in pl]
+    assert max(loads) - min(loads) <= 200  # contiguous halves would be 1920 against 910
+    with pytest.raises(ValueError):
+        ep.balanced_placement(counts, 3)

@@ -39,7 +39,8 @@ def _worker(rank, W, port, cfg, results):
         E, cap = cfg["E"], cfg["cap"]
         blk, _ = synth.moe_block(0, E, 8, cfg["H"], cfg["I"], cfg["I"], seed=0, zipf=True,
                                  routed_scaling_factor=cfg["scale"])
-        pe = ep.PeerExpertParallel(blk, capacity=cap, timeout_s=10.0)
+        placement = cfg.get("placement")
+        pe = ep.PeerExpertParallel(blk, capacity=cap, timeout_s=10.0, placement=placement)
         rep = []
         for step, T in enumerate(cfg["T"][rank]):
             g = torch.Generator(device="cuda")
@@ -70,11 +71,15 @@ TOKENS = {2: [[1024, 700, 1024], [1024, 0, 333]],
           4: [[1024, 700, 1024], [1024, 0, 333], [17, 1024, 0], [512, 1, 1024]]}
 
 
-@pytest.mark.parametrize("W", [2, 4])
-def test_peer_expert_parallel_equals_one_gpu_block(W):
+@pytest.mark.parametrize("W,placed", [(2, False), (2, True), (4, False)])
+def test_peer_expert_parallel_equals_one_gpu_block(W, placed):
+    """``placed``: the experts spread over the ranks by a non-contiguous placement (interleaved,
+    as ``ep.balanced_placement`` may give) instead of contiguous ranges."""
     if torch.cuda.device_count() < W:
         pytest.skip(f"needs {W} GPUs")
     cfg = dict(E=32, H=2048, I=1024, scale=2.5, cap=1024, T=TOKENS[W])
+    if placed:
+        cfg["placement"] = [[e for e in range(32) if (e * 7) % W == d] for d in range(W)]
     ctx = mp.get_context("spawn")
     with ctx.Manager() as man:
         results = man.dict()
