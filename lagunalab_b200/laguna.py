@@ -1059,6 +1059,9 @@ class StreamDecodeGraph:
         self.pos = pos.reshape(-1).to(torch.int32).clone()
         full = [c for c in cache if not isinstance(c, RotatingKVCache)]
         self.cap = full[0].keys.shape[2] if full else 1 << 30
+        self.pos0 = int(self.pos.max()) if self.pos.numel() else 0  # the furthest stream's row
+        if self.pos0 >= self.cap:
+            raise ValueError(f"a stream is at position {self.pos0}; the caches hold {self.cap}")
         self._body()
         self.first_logits = self.logits.clone()
         self.steps = 1
@@ -1083,6 +1086,8 @@ class StreamDecodeGraph:
 
     def step(self):
         """One token per stream (asynchronous); ``tok`` holds them afterwards."""
+        if self.pos0 + self.steps >= self.cap:  # the row this replay would write
+            raise ValueError(f"the caches hold {self.cap} rows")
         self.graph.replay()
         self.steps += 1
 
