@@ -81,7 +81,8 @@ int lg_event_elapsed_ms(void* ev_start, void* ev_end, float* ms);
  * gate_bits == 8 -> MLX 8-bit group-64 (laguna.py:236-238): gate_w uint32 [E, H/4],
  * scales/biases bf16 [E, H/64]; the quantized matmul's bf16 output is what the sigmoid sees.
  * e_bias fp32 [E] or NULL (zeros).  Outputs: inds int32 [T, k], weights bf16 [T, k],
- * logits fp32 [T, E] (optional, NULL to skip), counts int32 [E] (optional histogram of picks).
+ * logits fp32 [T, E] (required: the top-k reads the logits from it), counts int32 [E]
+ * (optional histogram of picks, NULL to skip).
  * Limits: E <= 256, 1 <= k <= min(E, 32), H % 64 == 0.
  */
 int lg_router_topk(const void* x, int T, int H,

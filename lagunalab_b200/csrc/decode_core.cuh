@@ -99,22 +99,25 @@ __device__ __forceinline__ bool topk_better(float a, int ia, float b, int ib) {
 constexpr int TOPK_MAXE_PER_LANE = 8;  // E <= 256
 
 // The router's top-k in three phases, so that the middle one can run on any number of
-// threads: (1) one warp turns the E logits (logit(e), e < E) into scores (sigmoid, or softmax
-// over the E logits) and selection keys (score + bias): keys[e], vals[e] = score;
+// threads (the one-token router; the batched router uses topk_select_regs below): (1) one
+// warp turns the E logits (logit(e), e < E) into scores (sigmoid, or softmax over the E
+// logits) and selection keys (score + bias): keys[e], vals[e] = score;
 // (2) every candidate's rank = the number of better keys under "larger first, equal keys ->
 // lower index" (NaN keys are never picked); slot[rank] = e for the k best; (3) one warp reads
 // the picks in rank order, adds their scores in that order and renormalises. Shared memory:
 // keys [E], vals [E], slot [k] (ints).
 
-template <typename LogitFn>
-__device__ __forceinline__ void topk_scores_warp(LogitFn logit, int E, const float* ebias,
-                                                 int score_fn, float* keys, float* vals) {
+// Phase 1 in registers: lane l holds candidates e = l + 32 j (j < NPER, 32 NPER >= E):
+// sc[j] = score, key[j] = score + bias (meaningless for e >= E, which the callers skip).
+template <int NPER, typename LogitFn>
+__device__ __forceinline__ void topk_scores_regs(LogitFn logit, int E, const float* ebias,
+                                                 int score_fn, float (&sc)[NPER],
+                                                 float (&key)[NPER]) {
   const int lane = threadIdx.x & 31;
   const int nper = (E + 31) / 32;
-  float sc[TOPK_MAXE_PER_LANE];
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < TOPK_MAXE_PER_LANE; ++j) {
+  for (int j = 0; j < NPER; ++j) {
     const int e = lane + 32 * j;
     const float l = (j < nper && e < E) ? logit(e) : -INFINITY;
     sc[j] = l;
@@ -124,7 +127,7 @@ __device__ __forceinline__ void topk_scores_warp(LogitFn logit, int E, const flo
     mx = warp_max(mx);
     float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < TOPK_MAXE_PER_LANE; ++j) {
+    for (int j = 0; j < NPER; ++j) {
       const int e = lane + 32 * j;
       const float v = (j < nper && e < E) ? expf(sc[j] - mx) : 0.f;
       sc[j] = v;
@@ -132,18 +135,97 @@ __device__ __forceinline__ void topk_scores_warp(LogitFn logit, int E, const flo
     }
     sum = warp_sum(sum);
 #pragma unroll
-    for (int j = 0; j < TOPK_MAXE_PER_LANE; ++j) sc[j] = sc[j] / sum;
+    for (int j = 0; j < NPER; ++j) sc[j] = sc[j] / sum;
   } else {
 #pragma unroll
-    for (int j = 0; j < TOPK_MAXE_PER_LANE; ++j) sc[j] = 1.0f / (1.0f + expf(-sc[j]));
+    for (int j = 0; j < NPER; ++j) sc[j] = 1.0f / (1.0f + expf(-sc[j]));
   }
+#pragma unroll
+  for (int j = 0; j < NPER; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = sc[j] + ((ebias && j < nper && e < E) ? ebias[e] : 0.f);
+  }
+}
+
+template <typename LogitFn>
+__device__ __forceinline__ void topk_scores_warp(LogitFn logit, int E, const float* ebias,
+                                                 int score_fn, float* keys, float* vals) {
+  const int lane = threadIdx.x & 31;
+  const int nper = (E + 31) / 32;
+  float sc[TOPK_MAXE_PER_LANE], key[TOPK_MAXE_PER_LANE];
+  topk_scores_regs<TOPK_MAXE_PER_LANE>(logit, E, ebias, score_fn, sc, key);
 #pragma unroll
   for (int j = 0; j < TOPK_MAXE_PER_LANE; ++j) {
     const int e = lane + 32 * j;
     if (j < nper && e < E) {
-      keys[e] = sc[j] + (ebias ? ebias[e] : 0.f);
+      keys[e] = key[j];
       vals[e] = sc[j];
     }
+  }
+}
+
+// Phases 2 and 3 for one warp in registers, after topk_scores_regs: k rounds of a warp
+// arg-max over the candidates still in play, in the same total order as topk_rank (larger key
+// first, equal keys -> lower index, NaN keys never picked), so the picks, their order and the
+// weight sum are those of topk_rank + topk_pick_warp. A candidate is one 64-bit word: the key
+// mapped to an order-preserving unsigned integer in the high half, 0xFFFF - e in the low half
+// (0 = out of play). Lane j < k ends with pick j (-1 and weight 0 past the keys that are not
+// NaN); its histogram count is added to hist (shared memory) when hist is not NULL.
+__device__ __forceinline__ uint64_t topk_cand(float key, int e) {
+  if (key != key) return 0ull;
+  const uint32_t u = __float_as_uint(key == 0.f ? 0.f : key);  // -0 == +0 as in topk_better
+  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<uint64_t>(o) << 32) | static_cast<uint32_t>(0xFFFF - e);
+}
+
+template <int NPER>
+__device__ __forceinline__ void topk_select_regs(const float (&sc)[NPER], const float (&key)[NPER],
+                                                 int E, int k, int norm, int* idx, float* wt,
+                                                 int* hist) {
+  const int lane = threadIdx.x & 31;
+  uint64_t cand[NPER];
+#pragma unroll
+  for (int j = 0; j < NPER; ++j) {
+    const int e = lane + 32 * j;
+    cand[j] = e < E ? topk_cand(key[j], e) : 0ull;
+  }
+  int my_i = -1;
+  float my_w = 0.f, wsum = 0.f;  // the picks' scores added in pick order
+  for (int r = 0; r < k; ++r) {
+    uint64_t best = 0ull;
+    float bv = 0.f;
+#pragma unroll
+    for (int j = 0; j < NPER; ++j) {
+      if (cand[j] > best) {
+        best = cand[j];
+        bv = sc[j];
+      }
+    }
+    uint64_t m = best;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const uint64_t y = __shfl_xor_sync(0xffffffffu, m, o);
+      m = y > m ? y : m;
+    }
+    if (m == 0ull) break;  // warp-uniform: no candidate left
+    const int e = 0xFFFF - static_cast<int>(m & 0xFFFFu);
+    const int src = e & 31;  // candidate e lives on lane e % 32
+    const float v = __shfl_sync(0xffffffffu, bv, src);
+    if (lane == src) {
+#pragma unroll
+      for (int j = 0; j < NPER; ++j)
+        if (cand[j] == m) cand[j] = 0ull;
+    }
+    if (lane == r) {
+      my_i = e;
+      my_w = v;
+    }
+    wsum += v;
+  }
+  if (lane < k) {
+    if (hist && my_i >= 0) atomicAdd(&hist[my_i], 1);
+    *idx = my_i;
+    *wt = norm ? my_w / wsum : my_w;
   }
 }
 
@@ -176,23 +258,6 @@ __device__ __forceinline__ void topk_pick_warp(const float* vals, const int* slo
     *idx = my_i;
     *wt = norm ? my_w / wsum : my_w;
   }
-}
-
-// All three phases in one warp (one token per warp). keys/vals: 2 E + k words of shared
-// memory owned by this warp.
-template <typename LogitFn>
-__device__ __forceinline__ void topk_warp(LogitFn logit, int E, const float* ebias, int k,
-                                          int norm, int score_fn, int* idx, float* wt, int* hist,
-                                          float* keys, float* vals) {
-  const int lane = threadIdx.x & 31;
-  int* slot = reinterpret_cast<int*>(vals + E);
-  topk_scores_warp(logit, E, ebias, score_fn, keys, vals);
-  if (lane < k) slot[lane] = -1;
-  __syncwarp();
-  topk_rank(keys, E, k, slot, lane, 32);
-  __syncwarp();
-  topk_pick_warp(vals, slot, k, norm, idx, wt, hist);
-  __syncwarp();
 }
 
 // Router logit of one expert row for one token (a warp): dot(x, scale * code + bias) over H

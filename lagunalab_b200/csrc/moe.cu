@@ -53,11 +53,14 @@ __device__ __forceinline__ void bf16x8(uint4 v, float* f) {
   }
 }
 
+constexpr int CB_J = 8;  // picks whose rows a thread loads at once
+
 // laguna.py:149-150 with the MLX graph's bf16 materialisation points: per pick
 // bf16(y * w), their fp32 sum in pick order rounded to bf16, times the routed scale (bf16),
 // plus the shared expert's row (bf16). One thread per 8 columns of a token; the order of
 // every sum is fixed, so the result does not depend on scheduling.
-__global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ y,
+
+__global__ void __launch_bounds__(256) combine_rows_kernel(const __nv_bfloat16* __restrict__ y,
                                     const int32_t* __restrict__ inds,
                                     const __nv_bfloat16* __restrict__ w, int T, int k, int E,
                                     int H, float scale, int has_shared,
@@ -71,18 +74,40 @@ __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ y,
     const size_t t = i / H8;
     const int c = (int)(i % H8) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < k; ++j) {
-      const size_t p = t * k + j;
-      const int e = inds[p];
-      if (e < 0 || e >= E) continue;
-      const float wj = bf2f(w[p]);
-      float v[8];
-      bf16x8(*reinterpret_cast<const uint4*>(y + p * H + c), v);
+    uint4 shv = make_uint4(0u, 0u, 0u, 0u);
+    if (has_shared) shv = *reinterpret_cast<const uint4*>(y + (P + t) * H + c);
+    // up to CB_J picks at a time: their ids and weights, then all their row loads in flight
+    // together, then the sum in pick order
+    for (int j0 = 0; j0 < k; j0 += CB_J) {
+      const int n = min(CB_J, k - j0);
+      bool ok[CB_J];
+      float wj[CB_J];
+      uint4 rv[CB_J];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += round_bf16(v[q] * wj);
+      for (int j = 0; j < CB_J; ++j) {
+        ok[j] = false;
+        wj[j] = 0.f;
+        if (j < n) {
+          const size_t p = t * k + j0 + j;
+          const int e = inds[p];
+          ok[j] = e >= 0 && e < E;
+          wj[j] = bf2f(w[p]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < CB_J; ++j)
+        if (ok[j]) rv[j] = *reinterpret_cast<const uint4*>(y + (t * k + j0 + j) * H + c);
+#pragma unroll
+      for (int j = 0; j < CB_J; ++j) {
+        if (!ok[j]) continue;
+        float v[8];
+        bf16x8(rv[j], v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += round_bf16(v[q] * wj[j]);
+      }
     }
     float sh[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (has_shared) bf16x8(*reinterpret_cast<const uint4*>(y + (P + t) * H + c), sh);
+    if (has_shared) bf16x8(shv, sh);
     float r[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {

@@ -5,10 +5,10 @@
 //   (expert, token) for T <= 256 (decode, batched decode), a tensor-core kernel for fp32 W at
 //   larger T (W split into three bf16 parts, so the result keeps fp32 accuracy), and a
 //   CUDA-core tiled kernel otherwise.
-// router_topk_kernel:   one warp per token: sigmoid (or softmax), + selection bias, top-k by
-//   repeated warp arg-max (larger first, equal keys -> lower index), unbiased weights,
-//   renormalisation, bf16 weights; a per-CTA histogram in shared memory (the warp's winning
-//   lane-0 adds one count per pick), then one global atomic per used bin and CTA.
+// router_topk_kernel:   one warp per token, in registers: sigmoid (or softmax), + selection
+//   bias, top-k by k rounds of a warp arg-max (larger first, equal keys -> lower index),
+//   unbiased weights, renormalisation, bf16 weights; a per-CTA histogram in shared memory
+//   (lane j < k adds pick j), then one global atomic per used bin and CTA.
 // moe_plan_kernel:      one CTA per expert group: its exclusive offset, then an
 //   order-preserving compaction of the picks of that group (warp ballot + popc prefix sums),
 //   so perm is ordered by expert then pick id, independent of timing.
@@ -92,13 +92,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
   }
 }
 
-// ---- tensor-core router logits (fp32 weight, T > 32) -----------------------------------
-// x (bf16, exact) times W (fp32) with W split into three bf16 parts, hi + mid + lo = W to
-// within 2^-24 relative, each product exact in the fp32 accumulator: fp32-accurate logits
-// on mma.sync m16n8k16. CTA tile 64 tokens x 32 experts, 4 warps of 16 tokens, K chunk 64;
-// the next chunk's global loads are issued into registers before the current chunk's MMAs.
-constexpr int RM_TT = 64, RM_EB = 32, RM_KC = 64, RM_LD = RM_KC + 8;  // padded smem rows
-
 __device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
   const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -107,92 +100,145 @@ __device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r
                : "r"(a));
 }
 
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  __syncwarp();  // mma.sync.aligned needs the whole warp converged
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+// ---- tensor-core router logits (fp32 W, T > 256) ------------------------------------------
+// x (bf16, exact) times W (fp32) with W split into three bf16 parts, hi + mid + lo = W to
+// within 2^-24 relative, each product exact in the fp32 accumulator: fp32-accurate logits on
+// mma.sync m16n8k16. The split is done on the B fragments in registers: each fp32 pair a
+// thread loads becomes its hi, mid and lo bf16 pairs and feeds the MMAs of both of the warp's
+// 16-token tiles. CTA tile 64 tokens x 64 experts, 8 warps: warp (wm, wn, kh) covers 32 tokens
+// x 32 experts over k16 steps 2 kh, 2 kh + 1 of every 64-wide K chunk; the two K halves are
+// added at the end. x and W chunks move by cp.async through a 4-stage ring (two CTAs fit on
+// an SM); the first chunks of the static W are requested before the PDL wait.
+constexpr int RX_TT = 64, RX_EB = 64, RX_KC = 64, RX_STAGES = 4;
+constexpr int RX_XLD = RX_KC + 8;                  // bf16 per x row (144 B: ldmatrix rows spread)
+constexpr int RX_WLD = RX_KC + 8;                  // fp32 per W row (288 B: float2 reads spread)
+constexpr int RX_XB = RX_TT * RX_XLD * 2;          // 9,216 B
+constexpr int RX_STAGE = RX_XB + RX_EB * RX_WLD * 4;  // 27,648 B
+constexpr int RX_SMEM = RX_STAGES * RX_STAGE;      // 110,592 B
+
+__device__ __forceinline__ void cp16_zfill(uint32_t dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(ok ? 16 : 0)
+               : "memory");
 }
 
-__global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                int T, int H,
-                                                                const float* __restrict__ W,
-                                                                int E, float* __restrict__ logits) {
-  pdl_wait();  // inputs come from the previous kernel
-  pdl_trigger();
-  __shared__ __align__(16) __nv_bfloat16 xs[RM_TT][RM_LD];
-  __shared__ __align__(16) __nv_bfloat16 ws[3][RM_EB][RM_LD];
+// bf16x2 parts of an fp32 pair (element x in the low half): hi + mid + lo = f within 2^-24.
+__device__ __forceinline__ void split3(float2 f, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  const float r1x = f.x - bf_lo(hi), r1y = f.y - bf_hi(hi);
+  __nv_bfloat162 m = __floats2bfloat162_rn(r1x, r1y);
+  mid = *reinterpret_cast<uint32_t*>(&m);
+  __nv_bfloat162 l = __floats2bfloat162_rn(r1x - bf_lo(mid), r1y - bf_hi(mid));
+  lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
+__global__ void __launch_bounds__(256) router_logits_rx_kernel(const __nv_bfloat16* __restrict__ x,
+                                                               int T, int H,
+                                                               const float* __restrict__ W, int E,
+                                                               float* __restrict__ logits) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int t0 = blockIdx.y * RM_TT, e0 = blockIdx.x * RM_EB;
-  // per thread: 4 uint4 of x (rows tid/8 + 16j, 8-element column block tid%8) and
-  // 4 float4 of W (rows tid/16 + 8j, 4-element column block tid%16)
-  uint4 xv[4];
-  float4 wv[4];
-  auto load = [&](int h0) {
+  const int wm = warp & 1, wn = (warp >> 1) & 1, kh = warp >> 2;
+  const int r = lane >> 2, c4 = lane & 3;
+  const int t0 = blockIdx.y * RX_TT, e0 = blockIdx.x * RX_EB;
+  const uint32_t sb = smem_u32(smem);
+  const int nch = H / RX_KC;
+  auto load_x = [&](int st, int h0) {  // 64 rows x 8 chunks of 16 B: 2 per thread
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = (tid >> 3) + 16 * j, c = (tid & 7) * 8;
-      xv[j] = (t0 + r < T) ? *reinterpret_cast<const uint4*>(x + (size_t)(t0 + r) * H + h0 + c)
-                           : make_uint4(0, 0, 0, 0);
-      const int er = (tid >> 4) + 8 * j, ec = (tid & 15) * 4;
-      wv[j] = (e0 + er < E) ? *reinterpret_cast<const float4*>(W + (size_t)(e0 + er) * H + h0 + ec)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < 2; ++j) {
+      const int i = tid + 256 * j, row = i >> 3, cc = i & 7;
+      const bool ok = t0 + row < T;
+      cp16_zfill(sb + st * RX_STAGE + row * (RX_XLD * 2) + cc * 16,
+                 ok ? x + (size_t)(t0 + row) * H + h0 + cc * 8 : x, ok);
     }
   };
-  float acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  load(0);
-  for (int h0 = 0; h0 < H; h0 += RM_KC) {
-    // registers -> shared (W split into three bf16 parts)
+  auto load_w = [&](int st, int h0) {  // 64 rows x 16 chunks of 16 B: 4 per thread
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      *reinterpret_cast<uint4*>(&xs[(tid >> 3) + 16 * j][(tid & 7) * 8]) = xv[j];
-      const int er = (tid >> 4) + 8 * j, ec = (tid & 15) * 4;
-      const float f[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+      const int i = tid + 256 * j, row = i >> 4, cc = i & 15;
+      const bool ok = e0 + row < E;
+      cp16_zfill(sb + st * RX_STAGE + RX_XB + row * (RX_WLD * 4) + cc * 16,
+                 ok ? W + (size_t)(e0 + row) * H + h0 + cc * 4 : W, ok);
+    }
+  };
+  // the weight is static: its first chunks are requested while the previous kernel finishes
+  for (int s = 0; s < RX_STAGES - 1; ++s)
+    if (s < nch) load_w(s, s * RX_KC);
+  pdl_wait();  // x comes from the previous kernel
+  pdl_trigger();
+  for (int s = 0; s < RX_STAGES - 1; ++s) {
+    if (s < nch) load_x(s, s * RX_KC);
+    cp_async_commit();
+  }
+  float acc[2][4][4];
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.f;
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait(RX_STAGES - 2);  // chunk c has landed (this thread's copies) ...
+    __syncthreads();               // ... everyone's; and the stage refilled below is free
+    const int nx = c + RX_STAGES - 1;
+    if (nx < nch) {
+      load_w(nx % RX_STAGES, nx * RX_KC);
+      load_x(nx % RX_STAGES, nx * RX_KC);
+    }
+    cp_async_commit();
+    const uint8_t* st = smem + (c % RX_STAGES) * RX_STAGE;
+    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st);
+    const float* ws = reinterpret_cast<const float*>(st + RX_XB);
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int k16 = (kh * 2 + kk) * 16;
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+        ldsm_x4(&xs[(wm * 32 + mi * 16 + (lane & 15)) * RX_XLD + k16 + ((lane >> 4) << 3)],
+                a[mi][0], a[mi][1], a[mi][2], a[mi][3]);
+      __syncwarp();  // mma.sync.aligned: the whole warp converged
+      uint32_t b[3][4][2];  // [part][n tile][k half]
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const float* wr = ws + (wn * 32 + ni * 8 + r) * RX_WLD + k16 + 2 * c4;
+        split3(*reinterpret_cast<const float2*>(wr), b[0][ni][0], b[1][ni][0], b[2][ni][0]);
+        split3(*reinterpret_cast<const float2*>(wr + 8), b[0][ni][1], b[1][ni][1], b[2][ni][1]);
+      }
+      // part-major: the 8 accumulators take turns, so an MMA never waits for the one just
+      // issued (the asm statements keep their order)
+#pragma unroll
+      for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi)
+            mma_bf16(acc[mi][ni], a[mi][0], a[mi][1], a[mi][2], a[mi][3], b[p][ni][0],
+                     b[p][ni][1]);
+    }
+  }
+  cp_async_wait(0);
+  __syncthreads();  // the ring is free: the upper K half's sums go through it
+  float* red = reinterpret_cast<float*>(smem) + (warp & 3) * 32 * 32;
+  if (kh == 1) {
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) red[((mi * 4 + ni) * 4 + q) * 32 + lane] = acc[mi][ni][q];
+  }
+  __syncthreads();
+  if (kh == 1) return;
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi) {
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const __nv_bfloat16 hi = __float2bfloat16_rn(f[q]);
-        const float r1 = f[q] - __bfloat162float(hi);
-        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
-        ws[0][er][ec + q] = hi;
-        ws[1][er][ec + q] = mid;
-        ws[2][er][ec + q] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
-      }
-    }
-    __syncthreads();
-    if (h0 + RM_KC < H) load(h0 + RM_KC);  // next chunk in flight during the MMAs
-#pragma unroll
-    for (int k16 = 0; k16 < RM_KC; k16 += 16) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(&xs[warp * 16 + (lane & 15)][k16 + ((lane >> 4) << 3)], a0, a1, a2, a3);
-#pragma unroll
-      for (int part = 0; part < 3; ++part) {
-#pragma unroll
-        for (int nt = 0; nt < 4; nt += 2) {
-          const int m = lane >> 3;
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(&ws[part][(nt + (m >> 1)) * 8 + (lane & 7)][k16 + ((m & 1) << 3)], b0, b1, b2, b3);
-          mma16816(acc[nt], a0, a1, a2, a3, b0, b1);
-          mma16816(acc[nt + 1], a0, a1, a2, a3, b2, b3);
-        }
-      }
-    }
-    __syncthreads();
-  }
-  const int r = lane >> 2, c4 = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int t = t0 + warp * 16 + r + 8 * h;
-      const int e = e0 + nt * 8 + 2 * c4;
-      if (t < T) {
-        if (e < E) logits[(size_t)t * E + e] = acc[nt][2 * h];
-        if (e + 1 < E) logits[(size_t)t * E + e + 1] = acc[nt][2 * h + 1];
+        const int t = t0 + wm * 32 + mi * 16 + r + 8 * (q >> 1);
+        const int e = e0 + wn * 32 + ni * 8 + 2 * c4 + (q & 1);
+        const float v = acc[mi][ni][q] + red[((mi * 4 + ni) * 4 + q) * 32 + lane];
+        if (t < T && e < E) logits[(size_t)t * E + e] = v;
       }
     }
   }
@@ -235,6 +281,8 @@ __global__ void __launch_bounds__(256) router_logits_gemv_kernel(
 
 constexpr int TK_WARPS = 8;
 
+// One warp per token, all in registers (NPER = candidates per lane, 32 NPER >= E).
+template <int NPER>
 __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
     const float* __restrict__ logits, int T, int E, const float* __restrict__ ebias, int k,
     int norm, int score_fn, int32_t* __restrict__ inds, __nv_bfloat16* __restrict__ wout,
@@ -242,16 +290,16 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(
   pdl_wait();  // inputs come from the previous kernel
   pdl_trigger();
   __shared__ int hist[256];
-  __shared__ float kv[TK_WARPS][2 * 256 + 32];  // per warp: keys [E], scores [E], picks [k]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   for (int t = blockIdx.x * TK_WARPS + warp; t < T; t += gridDim.x * TK_WARPS) {
     const float* row = logits + (size_t)t * E;
+    float sc[NPER], key[NPER];
+    topk_scores_regs<NPER>([&](int e) { return row[e]; }, E, ebias, score_fn, sc, key);
     int idx = -1;
     float wt = 0.f;
-    topk_warp([&](int e) { return row[e]; }, E, ebias, k, norm, score_fn, &idx, &wt, hist,
-              kv[warp], kv[warp] + E);
+    topk_select_regs<NPER>(sc, key, E, k, norm, &idx, &wt, counts ? hist : nullptr);
     if (lane < k) {
       inds[(size_t)t * k + lane] = idx;
       wout[(size_t)t * k + lane] = __float2bfloat16_rn(wt);
@@ -491,8 +539,10 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
       LG_CUDA_TRY(launch_k(router_logits_gemv_kernel<8>, grid, dim3(256), 0, s, xb, T, H, gate_w,
                            gsb, gbb, E, logits));
   } else if (gate_bits == 0 && xa) {
-    dim3 g((E + RM_EB - 1) / RM_EB, (T + RM_TT - 1) / RM_TT);
-    LG_CUDA_TRY(launch_k(router_logits_mma_kernel, g, dim3(128), 0, s, xb, T, H,
+    dim3 g((E + RX_EB - 1) / RX_EB, (T + RX_TT - 1) / RX_TT);
+    LG_CUDA_TRY(cudaFuncSetAttribute(router_logits_rx_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, RX_SMEM));
+    LG_CUDA_TRY(launch_k(router_logits_rx_kernel, g, dim3(256), (size_t)RX_SMEM, s, xb, T, H,
                          static_cast<const float*>(gate_w), E, logits));
   } else {
     dim3 g1((E + RL_EB - 1) / RL_EB, (T + RL_TT - 1) / RL_TT);
@@ -509,9 +559,13 @@ extern "C" int lg_router_topk(const void* x, int T, int H, const void* gate_w,
   int blocks = (T + TK_WARPS - 1) / TK_WARPS;
   if (blocks > 1184) blocks = 1184;
   prof_begin("router_topk", s);
-  LG_CUDA_TRY(launch_k(router_topk_kernel, dim3(blocks), dim3(TK_WARPS * 32), 0, s,
-                       static_cast<const float*>(logits), T, E, e_bias, k, norm_topk_prob,
-                       score_fn, inds, static_cast<__nv_bfloat16*>(weights), counts));
+  {
+    auto kern = E <= 32 ? router_topk_kernel<1> : E <= 64 ? router_topk_kernel<2>
+              : E <= 128 ? router_topk_kernel<4> : router_topk_kernel<8>;
+    LG_CUDA_TRY(launch_k(kern, dim3(blocks), dim3(TK_WARPS * 32), 0, s,
+                         static_cast<const float*>(logits), T, E, e_bias, k, norm_topk_prob,
+                         score_fn, inds, static_cast<__nv_bfloat16*>(weights), counts));
+  }
   prof_end("router_topk", s);
   LG_LAUNCH_CHECK("router_topk");
   return LG_OK;

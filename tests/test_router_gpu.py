@@ -32,7 +32,8 @@ def _check(inds, w, logits, bias, k, norm=True, score_fn="sigmoid"):
 
 
 @pytest.mark.parametrize("T,E,k,H", [(16, 128, 8, 2048), (4096, 128, 8, 2048), (1, 64, 8, 2048),
-                                     (10, 8, 2, 64), (33, 256, 16, 128), (7, 40, 5, 192)])
+                                     (10, 8, 2, 64), (33, 256, 16, 128), (7, 40, 5, 192),
+                                     (300, 40, 5, 192), (520, 256, 16, 128), (777, 100, 8, 1024)])
 def test_router_matches_oracle(T, E, k, H):
     g = gen(T * 1000 + E)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
