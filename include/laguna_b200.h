@@ -37,6 +37,9 @@ enum {
 enum { LG_SCORE_SIGMOID = 0, LG_SCORE_SOFTMAX = 1 };
 
 enum { LG_PATH_AUTO = 0, LG_PATH_GEMV = 1, LG_PATH_TENSOR = 2 };
+/* LG_PATH_AUTO's crossover: the GEMV kernels up to this many expert rows (routed picks plus the
+ * shared expert's rows), the tcgen05 grouped GEMM above it. */
+enum { LG_MOE_GEMV_MAX_ROWS = 768 };
 
 /* ABI version of this library (bumped on any signature change). */
 int lg_abi_version(void);
@@ -115,8 +118,8 @@ size_t lg_moe_workspace_bytes(int T, int H, int I, int E, int k, int I_shared);
  * Shared expert (laguna.py:114-122, :135): same layout without the E axis, intermediate
  * I_shared (0 = no shared expert, all sh_* may then be NULL).
  * x bf16 [T, H]; inds int32 [T, k]; weights bf16 [T, k]; out bf16 [T, H].
- * path: LG_PATH_AUTO picks the split-K GEMV kernels for few picks (<= 512 rows including the
- * shared expert's) and the tcgen05 grouped GEMM otherwise; LG_PATH_TENSOR forces the latter
+ * path: LG_PATH_AUTO picks the split-K GEMV kernels for few picks (<= LG_MOE_GEMV_MAX_ROWS rows
+ * including the shared expert's) and the tcgen05 grouped GEMM otherwise; LG_PATH_TENSOR forces the latter
  * (needs H % 256 == 0, I % 128 == 0, I_shared % 128 == 0).  bits == 4, group_size == 64 (the
  * MLX default the reference converts with, scripts/convert.py:14); H, I, I_shared % 64 == 0.
  */

@@ -11,6 +11,7 @@ LIB_PATH = Path(__file__).resolve().parent / "liblaguna_b200.so"
 LG_OK, LG_ERR_INVALID, LG_ERR_UNSUPPORTED, LG_ERR_CUDA, LG_ERR_WORKSPACE = range(5)
 LG_SCORE_SIGMOID, LG_SCORE_SOFTMAX = 0, 1
 LG_PATH_AUTO, LG_PATH_GEMV, LG_PATH_TENSOR = 0, 1, 2
+LG_MOE_GEMV_MAX_ROWS = 768
 
 P = c_void_p
 I = c_int

@@ -240,7 +240,7 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   // the split-K GEMV otherwise (decode), or when the shapes do not tile.
   const bool tiles_ok = tc_supported(H, Ie, I_sh, E);
   const bool use_tc = (path == LG_PATH_TENSOR) ||
-                      (path == LG_PATH_AUTO && tiles_ok && P + (with_sh ? T : 0) > 512);
+                      (path == LG_PATH_AUTO && tiles_ok && P + (with_sh ? T : 0) > LG_MOE_GEMV_MAX_ROWS);
   if (use_tc) {
     rc = launch_tc(a, max_groups, w.tc, st);  // clears the status word itself
   } else {

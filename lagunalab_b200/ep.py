@@ -155,8 +155,8 @@ class PeerExpertParallel:
     Calls are collective: every rank calls once per forward, in the same order. ``timeout_s``
     bounds each cross-GPU wait; an expired wait leaves NaN outputs and a nonzero ``status()``.
     Outputs equal the one-GPU block's bit for bit when both take the same product path: the
-    owners run the tensor-core path when the capacity exceeds 512 / (k + 1) tokens, as the
-    one-GPU block does for that many tokens.
+    owners run the tensor-core path when the capacity exceeds LG_MOE_GEMV_MAX_ROWS / (k + 1)
+    tokens, as the one-GPU block does for that many tokens.
 
     ``device_epoch=True``: the forwards' epochs are counted on the device (every call passes
     epoch 0 and ends with ``lg_ep_advance``), so a forward can be captured in a CUDA graph and
@@ -233,7 +233,8 @@ class PeerExpertParallel:
                                                               self.El, self.k)
         self.ws = ops.workspace(self.dev, "ep_moe", self.ws_bytes)
         # the owner's path for the received rows: the same on every rank (by the capacity)
-        self.expert_path = _lib.LG_PATH_TENSOR if self.cap * (self.k + 1) > 512 \
+        self.expert_path = _lib.LG_PATH_TENSOR \
+            if self.cap * (self.k + 1) > _lib.LG_MOE_GEMV_MAX_ROWS \
             else _lib.LG_PATH_GEMV
         if expert_path is not None:
             self.expert_path = int(expert_path)
@@ -253,9 +254,9 @@ class PeerExpertParallel:
         ep_arg = 0 if self.device_epoch else self.epoch
         main = torch.cuda.current_stream(self.dev)
         st = main.cuda_stream
-        # the product path the one-GPU block takes for these tokens (tensor cores above 512
-        # pick rows), so that the outputs equal it bit for bit
-        big = T * (self.k + 1) > 512
+        # the product path the one-GPU block takes for these tokens (tensor cores above
+        # LG_MOE_GEMV_MAX_ROWS pick rows), so that the outputs equal it bit for bit
+        big = T * (self.k + 1) > _lib.LG_MOE_GEMV_MAX_ROWS
         sh = self.blk.shared_expert
         side = None
         if sh is not None and T:

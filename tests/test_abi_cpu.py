@@ -29,6 +29,17 @@ def test_library_exports_every_declared_symbol():
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
 
 
+def test_header_enum_values_match_the_binding():
+    text = HEADER.read_text()
+    values = {}
+    for body in re.findall(r"enum\s*\{([^}]*)\}", text):
+        for name, val in re.findall(r"(LG_\w+)\s*=\s*(-?\d+)", body):
+            values[name] = int(val)
+    for name in ("LG_SCORE_SIGMOID", "LG_SCORE_SOFTMAX", "LG_PATH_AUTO", "LG_PATH_GEMV",
+                 "LG_PATH_TENSOR", "LG_MOE_GEMV_MAX_ROWS"):
+        assert values[name] == getattr(_lib, name), name
+
+
 def test_abi_version_and_no_error():
     assert _lib.lib().lg_abi_version() == 2
     assert isinstance(_lib.lib().lg_last_error(), bytes)

@@ -35,7 +35,7 @@ def _worker(rank, W, port, cfg, results):
                             device_id=torch.device("cuda", rank))
     pe = None
     try:
-        from lagunalab_b200 import ep, synth
+        from lagunalab_b200 import _lib, ep, synth
         E, cap = cfg["E"], cfg["cap"]
         blk, _ = synth.moe_block(0, E, 8, cfg["H"], cfg["I"], cfg["I"], seed=0, zipf=True,
                                  routed_scaling_factor=cfg["scale"])
@@ -49,9 +49,9 @@ def _worker(rank, W, port, cfg, results):
             got = pe(x)
             want = blk(x) if T else got
             torch.cuda.synchronize()
-            # the owners take the tensor-core path (capacity above 512 / (k + 1) tokens); the
-            # one-GPU block takes it for its own T only above that too
-            same_path = T == 0 or T * 9 > 512
+            # the owners take the tensor-core path (capacity above LG_MOE_GEMV_MAX_ROWS / (k + 1)
+            # tokens); the one-GPU block takes it for its own T only above that too
+            same_path = T == 0 or T * 9 > _lib.LG_MOE_GEMV_MAX_ROWS
             err = float((got.float() - want.float()).abs().max()) if T else 0.0
             rel = err / max(float(want.float().abs().max()), 1e-30) if T else 0.0
             rep.append((T, bool(torch.equal(got, want)), err, same_path, rel))
