@@ -92,6 +92,31 @@ def test_router_more_picks_than_live_experts():
     _check(inds, w, logits, bias, k)
 
 
+def test_router_nan_keys_are_never_picked():
+    """A NaN selection key (here through a NaN bias) is out of play: the picks are the top-k
+    of the other keys, and past the last of those the picks are -1 with weight 0."""
+    from lagunalab_b200 import ops
+    T, H = 24, 128
+    g = gen(13)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    for E, k, nan_experts in ((32, 8, [1, 6, 17, 30]), (40, 6, list(range(4, 40)))):
+        W = normal((E, H), 0.05, g)
+        bias = normal((E,), 0.01, g)
+        bias[nan_experts] = float("nan")
+        inds, w, logits = ops.router_topk(x.cuda(), W.cuda(), bias.cuda(), k)
+        sel = torch.sigmoid(logits.cpu()) + bias
+        live = [e for e in range(E) if e not in nan_experts]
+        ref = moe_ref.topk_indices(sel[:, live], min(k, len(live)))
+        ref = torch.tensor(live)[ref]
+        got = inds.cpu().long()
+        n = ref.shape[1]
+        # sets, off rows whose n-th and (n+1)-th live keys are within last-ulp rounding
+        tie = moe_ref.tie_rows(sel[:, live], n) if n < len(live) else torch.zeros(T, dtype=bool)
+        assert torch.equal(got[~tie, :n].sort(-1).values, ref[~tie].sort(-1).values)
+        assert (got[:, n:] == -1).all() and (w.cpu()[:, n:].float() == 0).all()
+        assert not set(got.reshape(-1).tolist()) & set(nan_experts)
+
+
 def test_router_8bit_gate():
     from lagunalab_b200 import ops
     T, E, H, k = 40, 64, 2048, 8
