@@ -24,6 +24,7 @@ struct MoeWs {
   __nv_bfloat16* yrows;  // [P + T, H] per-pick down outputs (combine mode)
   void* tc;
   int32_t* plan;         // segmented-plan scratch (many picks)
+  float* xg;             // [T, H/64] per-token group sums of x (GEMV path)
 };
 
 static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh, MoeWs* w,
@@ -40,6 +41,7 @@ static size_t carve_moe(void* base, int T, int H, int I, int E, int k, int I_sh,
   t.yrows = c.take<__nv_bfloat16>(with_yrows ? ((size_t)P + T) * H : 0);
   t.tc = c.take<char>(tc_workspace_bytes(T, H, I, I_sh, E, k));
   t.plan = c.take<int32_t>(plan_scratch_bytes(T, k, E) / sizeof(int32_t));
+  t.xg = c.take<float>((size_t)T * (H / 64));
   if (w) *w = t;
   return align_up(c.used, 256);
 }
@@ -235,6 +237,7 @@ static int moe_run(const void* x, int T, int H, int I, int E, int k, const int32
   a.ep = {};
   if (mode == 2) a.ep = *ep;  // expert parallel: down outputs go to the source ranks
   a.err = tc_err_word(w.tc, T, H, Ie, I_sh, E, k);
+  a.xg = w.xg;
   int max_groups = (E < P ? E : P) + (with_sh ? 1 : 0);
   // Tensor-core grouped GEMM when there are enough rows per expert to fill 128-row tiles;
   // the split-K GEMV otherwise (decode), or when the shapes do not tile.

@@ -41,6 +41,7 @@ struct GemvArgs {
   __nv_bfloat16* ypick;    // [P (+ T with the shared expert), H] per-pick down outputs
   EpRet ep;                // expert-parallel return (ep.on), replacing ypick
   int* err;                // status word: a bounded wait that expired records a code here
+  float* xg;               // [T, H/64] scratch (GEMV path): each token's 64-group sums of x
 };
 
 // The status word of the tensor-core workspace (lg_moe_status reads it); the GEMV kernels

@@ -62,6 +62,37 @@ __device__ __forceinline__ bool gv_tile_wait(uint64_t* bar, int* berr, int* err)
   return ok;
 }
 
+// xg[t, g] = the 64-group sum of x row t that the gate/up kernel's fold needs, computed once
+// per forward instead of once per 16-row tile (every tile of an expert used to recompute it):
+// four lanes per (token, group), each xsum16 over its 16 values, then the same two butterfly
+// adds as the gate/up kernel's in-register form, so the sums have the same bits.
+__global__ void __launch_bounds__(256) token_group_sums_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              int T, int H,
+                                                              float* __restrict__ xg) {
+  pdl_wait();  // x comes from the previous kernel
+  pdl_trigger();
+  const int gpr = H / 64;
+  const long long pairs = (long long)T * gpr;
+  const int c4 = threadIdx.x & 3;
+  // every lane of a warp runs the same number of iterations (the shuffles need them all)
+  const long long stride = (long long)gridDim.x * (blockDim.x / 4);
+  for (long long i0 = (long long)blockIdx.x * (blockDim.x / 4); i0 < pairs; i0 += stride) {
+    const long long i = i0 + (threadIdx.x >> 2);
+    const bool ok = i < pairs;
+    uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0;
+    if (ok) {
+      const int t = (int)(i / gpr), gg = (int)(i % gpr);
+      const __nv_bfloat16* xr = x + (size_t)t * H + gg * 64 + 16 * c4;
+      xa0 = *reinterpret_cast<const uint4*>(xr);
+      xa1 = *reinterpret_cast<const uint4*>(xr + 8);
+    }
+    float xs = xsum16(xa0, xa1);
+    xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+    xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+    if (ok && c4 == 0) xg[i] = xs;
+  }
+}
+
 template <bool STAGED>
 __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs a) {
   extern __shared__ __align__(128) uint8_t gv_smem[];
@@ -112,6 +143,11 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
     const bool tval = tn < cnt;
     const int tok = tval ? row_token(a.perm[row0 + tn], a.P, a.k) : 0;
     const __nv_bfloat16* xrow = a.x + (size_t)tok * H;
+    // the group sums of the C-layout columns 2c4, 2c4 + 1 (rows 2c4, 2c4 + 1 of this tile)
+    const int tc0 = __shfl_sync(0xffffffffu, tval ? tok : -1, (2 * c4) * 4);
+    const int tc1 = __shfl_sync(0xffffffffu, tval ? tok : -1, (2 * c4 + 1) * 4);
+    const float* xg0 = tc0 >= 0 ? a.xg + (size_t)tc0 * gpr : nullptr;
+    const float* xg1 = tc1 >= 0 ? a.xg + (size_t)tc1 * gpr : nullptr;
     float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll(STAGED ? 1 : 2)
     for (int gg = warp; gg < gpr; gg += GV_WARPS) {
@@ -134,12 +170,9 @@ __global__ void __launch_bounds__(GV_WARPS * 32) moe_gemv_gateup_kernel(GemvArgs
         xa0 = *reinterpret_cast<const uint4*>(xrow + gg * 64 + 16 * c4);
         xa1 = *reinterpret_cast<const uint4*>(xrow + gg * 64 + 16 * c4 + 8);
       }
-      // per-token group sum, moved from token-major (lane/4) to the C layout (cols 2c4, 2c4+1)
-      float xs = xsum16(xa0, xa1);
-      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
-      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
-      const float xs0 = __shfl_sync(0xffffffffu, xs, (2 * c4) * 4);
-      const float xs1 = __shfl_sync(0xffffffffu, xs, (2 * c4 + 1) * 4);
+      // the columns' group sums (token_group_sums_kernel; 0 past the group's rows)
+      const float xs0 = xg0 ? xg0[gg] : 0.f;
+      const float xs1 = xg1 ? xg1[gg] : 0.f;
       float sg0, sg8, bg0, bg8, su0, su8, bu0, bu8;
       if constexpr (STAGED) {  // the tile's scales [16][gpr], then its biases [16][gpr]
         const int i0 = r * gpr + gg, i8 = i0 + 8 * gpr, nb = 16 * gpr;
@@ -330,6 +363,14 @@ int launch_gemv(const GemvArgs& a, int max_groups, cudaStream_t s) {
   const bool staged = gv_stageable(a);
   const int Imax = a.I > a.I_sh ? a.I : a.I_sh;
   dim3 g1((Imax + 15) / 16, max_groups);
+  if (a.T > 0) {
+    const long long pairs = (long long)a.T * (a.H / 64);
+    long long blocks = (pairs + 63) / 64;  // 64 (token, group) pairs per 256-thread block
+    if (blocks > 8LL * device_sm_count()) blocks = 8LL * device_sm_count();
+    LG_CUDA_TRY(launch_k(token_group_sums_kernel, dim3((unsigned)blocks), dim3(256), 0, s, a.x,
+                         a.T, a.H, a.xg));
+    LG_LAUNCH_CHECK("token_group_sums");
+  }
   prof_begin("experts_gateup", s);
   LG_CUDA_TRY(staged ? gv_launch(moe_gemv_gateup_kernel<true>, g1, gv_smem_gu(a.H, true), s, a)
                      : gv_launch(moe_gemv_gateup_kernel<false>, g1, gv_smem_gu(a.H, false), s, a));
