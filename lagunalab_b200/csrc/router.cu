@@ -116,6 +116,11 @@ constexpr int RX_XB = RX_TT * RX_XLD * 2;          // 9,216 B
 constexpr int RX_STAGE = RX_XB + RX_EB * RX_WLD * 4;  // 27,648 B
 constexpr int RX_SMEM = RX_STAGES * RX_STAGE;      // 110,592 B
 
+// Unchecked 16-byte copy (zero fill when !ok, reading nothing). Its callers stay in bounds by
+// construction: shared offsets are stage * RX_STAGE + row * pitch + chunk * 16 with row < 64
+// and chunk < 8 (x) or 16 (W), at most RX_SMEM; global rows are guarded by T and E, columns
+// h0 + chunk * 8 (or 4) + 16 bytes <= H since H % 64 == 0 and h0 <= H - 64; row pitches are
+// multiples of 128 bytes and the host checks 16-byte bases.
 __device__ __forceinline__ void cp16_zfill(uint32_t dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
                "r"(ok ? 16 : 0)
